@@ -1,0 +1,473 @@
+"""Benchmark of the HiF4 W4A4 Linear hot path on B200.
+
+A step is one pass of the Qwen3-8B-shaped W4A4 linear set at T = 8192 prefill
+tokens: for each of q/k/v/o/gate/up/down, K1 (HiSQ1024 rotation + three-level
+HiF4 activation quantization) then K3 (tcgen05 GEMM against HiF4 weights).
+``value`` is whole-job TFLOPS (2*T*N*K summed over the projections and ranks)
+with inputs resident in HBM; ``e2e`` is the same metric through the public
+module API (``FakeQuantLinear``) with pinned host inputs copied in and outputs
+copied out every step. The attention hot path (causal GQA
+32/8 heads, S = 32768) is measured in the same run and reported under
+``attention``.
+
+``--impl reference`` times the reference algorithm on the host CPU instead: the
+numpy restatement in ``oracle/`` (the reference is PyTorch code that cannot be
+shipped to the GPU box), on a bounded sample of the same workload.
+
+Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
+``torch.distributed.run`` (one process per GPU, replicas: the linear set does not
+shard, so every rank runs its own copy and no collective is on the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT / "faquant-public_b200"), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "W4A4 GEMM & HiF4 QK/PV attn TFLOPS (% of B200 peak); prefill tokens/s"
+T_TOKENS = 8192
+PROJECTIONS = [  # (reference module path, in_features, out_features) -- Qwen3-8B
+    ("self_attn.q_proj", 4096, 4096),
+    ("self_attn.k_proj", 4096, 1024),
+    ("self_attn.v_proj", 4096, 1024),
+    ("self_attn.o_proj", 4096, 4096),
+    ("mlp.gate_proj", 4096, 12288),
+    ("mlp.up_proj", 4096, 12288),
+    ("mlp.down_proj", 12288, 4096),
+]
+ATT = dict(batch=1, hq=32, hkv=8, seq=32768, d=128)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def linear_flops(tokens: int = T_TOKENS, out_frac: float = 1.0) -> float:
+    return sum(2.0 * tokens * k * int(n * out_frac) for _, k, n in PROJECTIONS)
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------ distributed
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def init_dist(world: int, backend: str):
+    import datetime
+
+    import torch.distributed as dist
+
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return dist if world > 1 else None
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ GPU workload
+def build_linear_set(device, seed: int = 0):
+    import torch
+
+    from faquant_b200 import ops
+    from faquant_b200.hisq_rotation import derive_hisq_rotation
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for path, k, n in PROJECTIONS:
+        x = torch.randn(T_TOKENS, k, device=device, generator=g)
+        outliers = torch.randperm(k, device=device, generator=g)[: max(1, round(0.005 * k))]
+        x[:, outliers] *= 20.0
+        x = x.to(torch.bfloat16)
+        w = (torch.randn(n, k, device=device, generator=g) * 0.02).to(torch.bfloat16)
+        wq, _, _ = ops.hif4_quantize(w, levels="123")  # RTN onto the HiF4 grid
+        rot = derive_hisq_rotation(f"model.layers.0.{path}", k, seed=17, block_size=1024)
+        layers.append(dict(path=path, k=k, n=n, x=x, w=wq, signs=rot.signs.to(device),
+                           perm=rot.permutation.to(device), y=torch.empty(T_TOKENS, n, device=device,
+                                                                           dtype=torch.bfloat16)))
+        del w
+    return layers
+
+
+def run_linear_step(layers, timers=None):
+    from faquant_b200 import ops
+
+    launches = 0
+    for L in layers:
+        if timers is not None:
+            timers["q0"].append(timers["ev"]())
+        xq, _, _ = ops.hif4_quantize(L["x"], levels="123", signs=L["signs"], permutation=L["perm"], rot_block=1024)
+        if timers is not None:
+            timers["g0"].append(timers["ev"]())
+        ops.gemm_bf16(xq, L["w"], out=L["y"])
+        if timers is not None:
+            timers["g1"].append(timers["ev"]())
+        launches += 2
+    return launches
+
+
+def build_attention(device, seed: int = 1):
+    import torch
+
+    b, hq, hkv, s, d = ATT["batch"], ATT["hq"], ATT["hkv"], ATT["seq"], ATT["d"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(b, hq, s, d, device=device, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, hkv, s, d, device=device, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, hkv, s, d, device=device, generator=g).to(torch.bfloat16)
+    lo, hi = math.log(0.5), math.log(2.0)
+    smooth = torch.exp(torch.rand(d, device=device, generator=g) * (hi - lo) + lo)
+    return dict(q=q, k=k, v=v, smooth=smooth, out=torch.empty(b, s, hq, d, device=device, dtype=torch.bfloat16))
+
+
+def run_attention_step(A, timers=None):
+    from faquant_b200 import ops
+
+    qd, _, _ = ops.qk_prep(A["q"], levels="123", rotate=True, smooth_scale=A["smooth"], smooth_mode="mul")
+    kd, _, _ = ops.qk_prep(A["k"], levels="123", rotate=True, smooth_scale=A["smooth"], smooth_mode="div")
+    vd, _, _ = ops.qk_prep(A["v"], levels="123", rotate=False)
+    if timers is not None:
+        timers["a0"].append(timers["ev"]())
+    ops.hif4_attention(qd, kd, vd, causal=True, p_levels="123", quantized_normalizer=True, out=A["out"])
+    if timers is not None:
+        timers["a1"].append(timers["ev"]())
+    return 4
+
+
+def attention_flops() -> float:
+    s = ATT["seq"]
+    return 4.0 * ATT["d"] * ATT["hq"] * ATT["batch"] * s * (s + 1) / 2.0
+
+
+def flush_l2(buf):
+    buf.add_(1.0)
+
+
+# ------------------------------------------------------------------ CPU legs (oracle)
+def cpu_linear_sample(tokens: int, out_frac: float, seed: int = 0):
+    """Inputs of the bounded CPU sample: `tokens` rows and a fraction of the output
+    channels of every projection; weights quantized by the oracle (setup)."""
+    import numpy as np
+
+    from faquant_b200.hisq_rotation import derive_hisq_rotation
+    from oracle import hif4 as oh
+
+    rng = np.random.default_rng(seed)
+    sample = []
+    for path, k, n in PROJECTIONS:
+        x = rng.standard_normal((tokens, k), dtype=np.float32)
+        x[:, rng.choice(k, max(1, round(0.005 * k)), replace=False)] *= 20.0
+        x = oh.bf16_round(x)
+        ns = int(n * out_frac)
+        w = oh.bf16_round(rng.standard_normal((ns, k), dtype=np.float32) * np.float32(0.02))
+        wq = oh.fake_quantize(w, "123")
+        rot = derive_hisq_rotation(f"model.layers.0.{path}", k, seed=17, block_size=1024)
+        sample.append((x, wq, rot.signs.numpy(), rot.permutation.numpy()))
+    return sample
+
+
+def cpu_linear_step(sample):
+    from oracle import linear as olin
+
+    for x, wq, signs, perm in sample:
+        olin.fake_quant_linear(x, wq, None, levels="123", signs=signs, permutation=perm, block=1024)
+
+
+def cpu_baseline(tokens: int = 1024, out_frac: float = 0.25, steps: int = 2) -> dict:
+    sample = cpu_linear_sample(tokens, out_frac)
+    cpu_linear_step(sample)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_linear_step(sample)
+    dt = (time.perf_counter() - t0) / steps
+    flops = linear_flops(tokens, out_frac)
+    return {
+        "value": flops / dt / 1e12, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
+        "sample": f"{tokens} tokens x {int(out_frac * 100)}% of the output channels of each of the 7 projections "
+                  f"(full K), HiSQ1024 rotation + three-level HiF4 + fp32 GEMM in numpy (BLAS on all cores, "
+                  f"elementwise single-threaded), {steps} steps after 1 warm-up",
+        "seconds_per_step": dt,
+    }
+
+
+def reference_arm(args) -> None:
+    rank, world, _ = dist_env()
+    if world > 1 and rank != 0:
+        return
+    import numpy as np  # noqa: F401
+
+    tokens, frac = 1024, 0.25
+    sample = cpu_linear_sample(tokens, frac)
+    for _ in range(args.warmup):
+        cpu_linear_step(sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_linear_step(sample)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = linear_flops(tokens, frac) / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "qwen3-8b linear set (BASELINE config 2), bounded CPU sample",
+                   "tokens": tokens, "out_channel_fraction": frac, "rotation": "hisq1024", "levels": "123"},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{tokens} tokens x {int(frac * 100)}% of each projection's output channels"},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ main arm
+def main_arm(args) -> None:
+    import torch
+
+    from faquant_b200 import _lib
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = init_dist(world, "nccl")
+    _lib.load()
+    pk, pk_kind = peaks()
+
+    layers = build_linear_set(device, seed=rank)
+    A = build_attention(device, seed=1000 + rank) if not args.no_attention else None
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    ev = lambda: (lambda e: (e.record(), e)[1])(torch.cuda.Event(enable_timing=True))  # noqa: E731
+    # ---------------- device-resident timing of the linear set
+    for _ in range(args.warmup):
+        run_linear_step(layers)
+    timers = {"q0": [], "g0": [], "g1": [], "ev": ev}
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        launches = 0
+        for _ in range(args.steps):
+            launches += run_linear_step(layers, timers)
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    gemm_ms = sum(a.elapsed_time(b) for a, b in zip(timers["g0"], timers["g1"]))
+    quant_ms = sum(a.elapsed_time(b) for a, b in zip(timers["q0"], timers["g0"]))
+    n_gemm = len(timers["g0"])
+    ms_t = torch.tensor([ms], device=device)
+    if dist is not None:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = linear_flops() * world / (ms_max * 1e-3) / 1e12
+    gemm_tflops = linear_flops() * args.steps / (gemm_ms * 1e-3) / 1e12
+    quant_bytes = sum(T_TOKENS * k * (2 + 2) for _, k, _ in PROJECTIONS)  # bf16 read + bf16 QDQ write
+    quant_gbs = quant_bytes * args.steps / (quant_ms * 1e-3) / 1e9
+
+    # ---------------- attention (config 3), device-resident
+    att = None
+    if A is not None:
+        for _ in range(max(1, args.warmup // 3)):
+            run_attention_step(A)
+        atimers = {"a0": [], "a1": [], "ev": ev}
+        a_steps = max(1, args.att_steps)
+        barrier()
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(a_steps):
+            launches_att = run_attention_step(A, atimers)
+        s1.record()
+        torch.cuda.synchronize()
+        barrier()
+        a_ms = s0.elapsed_time(s1) / a_steps
+        k_ms = sum(a.elapsed_time(b) for a, b in zip(atimers["a0"], atimers["a1"])) / a_steps
+        att = {
+            "workload": "qwen3-8b causal GQA attention prefill (BASELINE config 3)", **ATT,
+            "ms_per_step": a_ms, "kernel_ms": k_ms,
+            "tflops": attention_flops() / (a_ms * 1e-3) / 1e12,
+            "kernel_tflops": attention_flops() / (k_ms * 1e-3) / 1e12,
+            "frac_of_bf16_peak": attention_flops() / (k_ms * 1e-3) / 1e12 / pk["bf16_tflops"],
+            "tokens_per_s": ATT["seq"] * ATT["batch"] / (a_ms * 1e-3),
+            "gpu_launches_per_step": launches_att,
+        }
+
+    # ---------------- e2e through FakeQuantLinear with host buffers
+    e2e = None
+    if not args.no_e2e:
+        from faquant_b200.quantization import FakeQuantLinear
+
+        mods, host_x, host_y = [], [], []
+        for L in layers:
+            lin = torch.nn.Linear(L["k"], L["n"], bias=False, device="meta")
+            lin.weight = torch.nn.Parameter(L["w"], requires_grad=False)
+            m = FakeQuantLinear(lin, quant_format="hif4", bits=4, weight_group_size=64, activation_group_size=64,
+                                symmetric=True, clip_ratio=1.0, quantize_weight=False,
+                                input_rotation_signs=L["signs"], input_rotation_permutation=L["perm"],
+                                input_rotation_block_size=1024)
+            mods.append(m)
+            host_x.append(L["x"].cpu().pin_memory())
+            host_y.append(torch.empty(T_TOKENS, L["n"], dtype=torch.bfloat16).pin_memory())
+
+        def e2e_step():
+            for m, hx, hy in zip(mods, host_x, host_y):
+                y = m(hx.to(device, non_blocking=True))
+                hy.copy_(y, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        e_steps = max(3, args.steps // 10)
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = torch.tensor([e0.elapsed_time(e1) / e_steps], device=device)
+        if dist is not None:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e2e = {"value": linear_flops() * world / (float(e_ms.item()) * 1e-3) / 1e12, "unit": "TFLOPS",
+               "ms_per_step": float(e_ms.item()),
+               "h2d_bytes_per_step": sum(h.numel() * 2 for h in host_x),
+               "d2h_bytes_per_step": sum(h.numel() * 2 for h in host_y)}
+
+    if rank == 0:
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic.json"
+        if tfile.exists():
+            traffic = json.loads(tfile.read_text()).get("gemm_bf16_tn_kernel_bytes_per_launch")
+        avg_gemm_ms = gemm_ms / n_gemm
+        gemm_flops_per_launch = linear_flops() / len(PROJECTIONS)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-8b W4A4 linear set, T=8192 (BASELINE config 2)", "tokens": T_TOKENS,
+                       "projections": [p for p, _, _ in PROJECTIONS], "rotation": "hisq1024 (seed 17)",
+                       "levels": "123", "weights": "RTN HiF4 of N(0,0.02)", "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (512 MB activations + 436 MB weights per step)"},
+            "tokens_per_s": T_TOKENS * world / (ms_max * 1e-3),
+            "roofline": {
+                "kernel": "gemm_bf16_tn_kernel", "bound": "tensor", "achieved": gemm_tflops,
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": gemm_tflops / pk["bf16_tflops"],
+                "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic,
+                "avg_launch_ms": avg_gemm_ms, "algorithmic_flops_per_launch_avg": gemm_flops_per_launch,
+                "frac_of_sustained_peak": gemm_tflops / pk.get("bf16_tflops_sustained", pk["bf16_tflops"]),
+                "frac_of_fp8_dense_nominal": gemm_tflops / 4500.0,
+                "frac_of_fp4_dense_nominal": gemm_tflops / 9000.0,
+            },
+            "quantize_kernel": {"kernel": "hif4_quantize_rotate_kernel", "bound": "hbm", "achieved": quant_gbs,
+                                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": quant_gbs / pk["hbm_gbs"],
+                                "ms_per_step": quant_ms / args.steps},
+            "clocks": clocks.summary(),
+            "gpu_launches": launches,
+            "attention": att,
+            "e2e": e2e,
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--att-steps", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-attention", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        main_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,243 @@
+// K3 -- bf16 GEMM y = a . b^T (+ bias) on the 5th-generation tensor cores.
+//
+// The W4A4 Linear runs its GEMM on the exactly-dequantized HiF4 operands in bf16:
+// every HiF4 value has at most 6 significant bits, so bf16 holds it exactly,
+// products are exact and the fp32 accumulation is the reference's fake-quant
+// semantics (F.linear on the QDQ tensors, quantization.py:277). No block-scaled
+// FP4/FP8 MMA represents HiF4 exactly: E2M1 lacks the 1.25/1.75 element steps
+// and the E6M2 scale mantissa cannot be a UE8M0 block scale.
+//
+// Structure (one CTA per SM, persistent over 128x256 output tiles):
+//   warp 0      TMA producer: A [128 x 64] and B [256 x 64] bf16 tiles, 128-byte
+//               swizzle, into a 4-stage shared-memory ring (48 KB per stage);
+//   warp 1      allocates 512 TMEM columns; one lane issues tcgen05.mma
+//               (M=128, N=256, K=16, kind::f16) and tcgen05.commit;
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator (one row per
+//               thread), bias, bf16 rounding, 16-byte stores.
+// The two accumulators (2 x 256 columns) let the epilogue of tile i overlap the
+// main loop of tile i+1. Every wait is bounded (common.cuh, mbar_wait).
+#include <algorithm>
+
+#include "common.cuh"
+#include "tma.h"
+
+namespace faq {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = 512;
+constexpr int THREADS = 192;
+constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false, false);
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+
+struct Params {
+  int m, n, k;
+  int tiles_m, tiles_n, kblocks;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* y;
+  int64_t ldy;
+  bool y_vec;
+};
+
+__device__ __forceinline__ void store_row32(const Params& p, int row, int col, const float (&v)[32]) {
+  if (row >= p.m || col >= p.n) return;
+  float r[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float b = 0.0f;
+    if (p.bias != nullptr && col + i < p.n) b = __bfloat162float(p.bias[col + i]);
+    r[i] = v[i] + b;
+  }
+  __nv_bfloat16* dst = p.y + static_cast<int64_t>(row) * p.ldy + col;
+  if (p.y_vec && col + 32 <= p.n) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const __nv_bfloat162 pair = __floats2bfloat162_rn(r[8 * j + 2 * h], r[8 * j + 2 * h + 1]);
+        w[h] = *reinterpret_cast<const uint32_t*>(&pair);
+      }
+      d4[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    for (int i = 0; i < 32 && col + i < p.n; ++i) dst[i] = __float2bfloat16_rn(r[i]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NUM_ACC);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 4);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(smem_addr(&full[stage]), STAGE_BYTES);
+          tma_load_2d(smem_addr(sA + stage * A_BYTES), &tmap_a, smem_addr(&full[stage]), kb * BK, tm * BM);
+          tma_load_2d(smem_addr(sB + stage * B_BYTES), &tmap_b, smem_addr(&full[stage]), kb * BK, tn * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: wait (bounded) until the tensor cores released every loaded stage
+      for (int s = 0; s < STAGES && ok; ++s) {
+        if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(smem_addr(&tempty[acc]), acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(smem_addr(&full[stage]), phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sA + stage * A_BYTES), b0 = smem_addr(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_f16(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), IDESC,
+                       (kb | kk) != 0);
+          tc_commit(smem_addr(&empty[stage]));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc_commit(smem_addr(&tfull[acc]));
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+      tc_fence_after();
+      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+      const int row = tm * BM + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tc_wait_ld();
+        reg_fence32(r);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        store_row32(p, row, tn * BN + c, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+}  // namespace faq
+
+using namespace faq;
+
+extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                                int64_t k, const void* bias, void* y, int64_t ldy, void* stream) {
+  FAQ_CHECK_ARG(a && b && y, "null pointer");
+  FAQ_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "bad shape");
+  FAQ_CHECK_ARG(m < (int64_t(1) << 31) && n < (int64_t(1) << 31) && k < (int64_t(1) << 31), "shape too large");
+  FAQ_CHECK_ARG(lda >= k && ldb >= k && ldy >= n, "leading dimension too small");
+  FAQ_CHECK_ARG(lda % 8 == 0 && ldb % 8 == 0 && k % 8 == 0, "TMA needs lda, ldb and k multiples of 8");
+  FAQ_CHECK_ARG(aligned16(a) && aligned16(b), "a and b must be 16-byte aligned");
+  if (m == 0 || n == 0) return FAQ_OK;
+  using namespace faq::gemm;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {BK, BM};
+    int rc = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != FAQ_OK) return rc;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {BK, BN};
+    int rc = make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, dims, strides, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != FAQ_OK) return rc;
+  }
+  Params p;
+  p.m = static_cast<int>(m);
+  p.n = static_cast<int>(n);
+  p.k = static_cast<int>(k);
+  p.tiles_m = static_cast<int>((m + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((n + BN - 1) / BN);
+  p.kblocks = static_cast<int>((k + BK - 1) / BK);
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.y_vec = aligned16(y) && ldy % 8 == 0;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(tiles, num_sms());
+  FAQ_CUDA(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(SMEM_BYTES)));
+  gemm_bf16_tn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  return launch_status("gemm_bf16_tn_kernel");
+}

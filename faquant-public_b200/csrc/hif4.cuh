@@ -1,0 +1,117 @@
+// HiF4 S1P2 quantization on the device, bit-exact with src/faquant/hif4.py.
+//
+// Arithmetic of the reference, step by step (each step is one IEEE fp32 op with
+// round-to-nearest-even, so every intermediate matches the CPU reference):
+//   s   = bf16(max64 * bf16(1/d))  d = 7 (levels 123) or 3.5 (12, 13)   hif4.py:102-103
+//   s   = clamp(s, 2^-48, 49152)                                          hif4.py:104
+//   s   = rint(s * 2^(2-e)) * 2^(e-2), e = floor(log2 s)  (E6M2 grid)     hif4.py:108-113
+//   rec = bf16(1 / s)   (correctly rounded fp32 divide, then bf16)        hif4.py:114
+//   lv2 = [max8 * rec >= 4]          (123)  | [max8 * rec >= 2] (12)      hif4.py:200-209
+//   lv3 = [max4 * rec / 2^lv2 >= 2]  (123)  | [max4 * rec >= 2] (13)      hif4.py:205-213
+//   qm  = rec / 2^lv2 / 2^lv3,  ds = s * 2^lv2 * 2^lv3   (exact)          hif4.py:236-239
+//   m   = min(floor(|x| * qm * 4 + 0.5), 7)                               hif4.py:268-269
+//   y   = sign(x) * m/4 * ds  (exact; sign(-0.0) = +0)                    hif4.py:270
+// The multiplies and adds use __fmul_rn/__fadd_rn so the compiler never fuses
+// them into an FMA, which would skip an intermediate rounding.
+#pragma once
+
+#include "common.cuh"
+
+namespace faq {
+
+__device__ __forceinline__ float divisor_reciprocal(int levels) {
+  // bf16(fp32(1/7)) = 0x3E12 = 0.142578125, bf16(fp32(1/3.5)) = 0x3E92 = 0.28515625
+  return levels == 123 ? 0.142578125f : 0.28515625f;
+}
+
+struct Hif4Scale {
+  float s;    // E6M2 scale
+  float rec;  // bf16 reciprocal
+  uint32_t code;  // (e + 48) << 2 | t
+};
+
+__device__ __forceinline__ Hif4Scale hif4_scale(float max64, int levels) {
+  float s = bf16_round(__fmul_rn(max64, divisor_reciprocal(levels)));
+  s = fminf(fmaxf(s, 3.552713678800501e-15f), 49152.0f);  // [2^-48, 49152]
+  int e = exponent_of(s);
+  const float q = rintf(__fmul_rn(s, pow2f(2 - e)));  // exact scaling, rint half-to-even
+  s = __fmul_rn(q, pow2f(e - 2));
+  e = exponent_of(s);  // q == 8 moves to the next octave
+  const uint32_t t = static_cast<uint32_t>(__fmul_rn(s, pow2f(2 - e))) - 4u;
+  Hif4Scale r;
+  r.s = s;
+  r.rec = bf16_round(__fdiv_rn(1.0f, s));
+  r.code = (static_cast<uint32_t>(e + 48) << 2) | t;
+  return r;
+}
+
+__device__ __forceinline__ float hif4_code(float a, float qm) {
+  // floor(fl(fl(|x| * qm) * 4) + 0.5) clamped to 7; the *4 is exact.
+  const float y = __fmul_rn(__fmul_rn(a, qm), 4.0f);
+  return fminf(floorf(__fadd_rn(y, 0.5f)), 7.0f);
+}
+
+// Quantize the 8 consecutive values v[0..7] of one lv2 sub-block. The 8 lanes of
+// an aligned lane group (lanes 8g .. 8g+7) together hold one 64-value block in
+// order. Writes the dequantized values to out[], returns this thread's 8 packed
+// nibbles (value i at bits 4i..4i+3) and, in lane 8g, the block's meta word.
+// All 32 lanes of the warp must call it (shuffles use the full mask).
+__device__ __forceinline__ uint32_t hif4_quant8(const float (&v)[8], int levels, float (&out)[8],
+                                               uint32_t& meta_word) {
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = fabsf(v[i]);
+  const float m3_0 = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+  const float m3_1 = fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7]));
+  const float m2 = fmaxf(m3_0, m3_1);
+  float m1 = m2;
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 4));
+  const Hif4Scale sc = hif4_scale(m1, levels);
+  uint32_t lv2 = 0, lv3_0 = 0, lv3_1 = 0;
+  if (levels == 123) {
+    lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;
+    const float thr = lv2 ? 4.0f : 2.0f;  // max4*rec/2^lv2 >= 2, the division being exact
+    lv3_0 = __fmul_rn(m3_0, sc.rec) >= thr;
+    lv3_1 = __fmul_rn(m3_1, sc.rec) >= thr;
+  } else if (levels == 12) {
+    lv2 = __fmul_rn(m2, sc.rec) >= 2.0f;
+  } else {
+    lv3_0 = __fmul_rn(m3_0, sc.rec) >= 2.0f;
+    lv3_1 = __fmul_rn(m3_1, sc.rec) >= 2.0f;
+  }
+  const float qm0 = __fmul_rn(sc.rec, pow2f(-static_cast<int>(lv2 + lv3_0)));
+  const float qm1 = __fmul_rn(sc.rec, pow2f(-static_cast<int>(lv2 + lv3_1)));
+  const float ds0 = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lv3_0)));
+  const float ds1 = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lv3_1)));
+  uint32_t nibbles = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float m = hif4_code(a[i], i < 4 ? qm0 : qm1);
+    const float mag = __fmul_rn(__fmul_rn(m, 0.25f), i < 4 ? ds0 : ds1);
+    const bool neg = v[i] < 0.0f;
+    out[i] = neg ? -mag : mag;
+    nibbles |= ((static_cast<uint32_t>(m) | (static_cast<uint32_t>(neg) << 3)) << (4 * i));
+  }
+  const int pos = threadIdx.x & 7;
+  uint32_t bits = (lv2 << (8 + pos)) | (lv3_0 << (16 + 2 * pos)) | (lv3_1 << (17 + 2 * pos));
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 4);
+  meta_word = bits | sc.code;
+  return nibbles;
+}
+
+// Decode one packed nibble with its block's meta word (inverse of the packing).
+__device__ __forceinline__ float hif4_decode(uint32_t nibble, uint32_t meta, int index_in_block) {
+  const uint32_t code = meta & 0xFFu;
+  const int e = static_cast<int>(code >> 2) - 48;
+  const float s = __fmul_rn(1.0f + 0.25f * static_cast<float>(code & 3u), pow2f(e));
+  const int sub8 = index_in_block >> 3, sub4 = index_in_block >> 2;
+  const int shift = static_cast<int>((meta >> (8 + sub8)) & 1u) + static_cast<int>((meta >> (16 + sub4)) & 1u);
+  const float mag = __fmul_rn(__fmul_rn(static_cast<float>(nibble & 7u), 0.25f), __fmul_rn(s, pow2f(shift)));
+  return (nibble & 8u) ? -mag : mag;
+}
+
+}  // namespace faq

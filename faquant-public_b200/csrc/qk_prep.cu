@@ -1,0 +1,204 @@
+// K4 -- attention operand preparation: (offset) -> Smooth-QK -> Hadamard over
+// head_dim -> one bf16 rounding -> HiF4 along head_dim, for Q, K or V.
+//
+// Reference: qwen3._attention_forward (src/faquant/qwen3.py:101-130) computes, in one
+// fp32 excursion, k - offset, q * s, k / s (true division), hadamard_transform over
+// head_dim (rotation.py:14-29, whose final `/ sqrt(128)` is a correctly rounded fp32
+// divide), and a single cast to bf16; the simulator then fake-quantizes Q/K/V along
+// head_dim (simulated_flash_attention.py:588-619). Wan does the same
+// (wan22_attention.py:186-192, 221, 257-259).
+//
+// Mapping: d/8 lanes per (b, h, s) row, 8 consecutive channels per lane, so the
+// Hadamard strides 1, 2, 4 are inside a lane and 8 .. d/2 are lane shuffles, and
+// the HiF4 64-blocks are 8 aligned lanes (hif4_quant8). HBM-bound: one read and
+// one write of the operand.
+#include "common.cuh"
+#include "hif4.cuh"
+
+namespace faq {
+
+struct QkPrepParams {
+  const void* x;
+  int64_t batch, heads, seq;
+  int64_t sb, sh, ss;
+  const float* offset;  // [heads, d] or null
+  const float* smooth;  // [d] or [heads, d] or null
+  int64_t smooth_head_stride;
+  int smooth_mode;  // 0 none, 1 multiply, 2 divide
+  int rotate;
+  int levels;  // 0 = no quantization
+  __nv_bfloat16* out;
+  int64_t ob, oh, os;
+  uint8_t* codes;
+  uint32_t* meta;
+  bool x_vec, out_vec;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256) qk_prep_kernel(QkPrepParams p) {
+  constexpr int LANES = D / 8;           // lanes per row
+  constexpr int ROWS_PER_WARP = 32 / LANES;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LANES;          // position of the lane inside its row
+  const int64_t rows = p.batch * p.heads * p.seq;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t base = warp_id * ROWS_PER_WARP; base < rows; base += warps_total * ROWS_PER_WARP) {
+    const int64_t r = base + lane / LANES;
+    const bool live = r < rows;
+    const int64_t rr = live ? r : 0;
+    const int64_t s = rr % p.seq, h = (rr / p.seq) % p.heads, b = rr / (p.seq * p.heads);
+    const T* src = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + s * p.ss + sub * 8;
+    float v[8];
+    if (p.x_vec) {
+      if constexpr (sizeof(T) == 2) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = __uint_as_float(w[i] << 16);
+          v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+      } else {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        const float4 c = reinterpret_cast<const float4*>(src)[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if constexpr (sizeof(T) == 2)
+          v[i] = __bfloat162float(src[i]);
+        else
+          v[i] = src[i];
+      }
+    }
+    if (p.offset != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fsub_rn(v[i], p.offset[h * D + sub * 8 + i]);
+    }
+    if (p.smooth_mode != 0) {
+      const float* sm = p.smooth + h * p.smooth_head_stride + sub * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = p.smooth_mode == 1 ? __fmul_rn(v[i], sm[i]) : __fdiv_rn(v[i], sm[i]);
+    }
+    if (p.rotate) {
+      // strides 1, 2, 4 inside the lane
+#pragma unroll
+      for (int st = 1; st < 8; st <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if ((i & st) == 0) {
+            const float l = v[i], rgt = v[i + st];
+            v[i] = __fadd_rn(l, rgt);
+            v[i + st] = __fsub_rn(l, rgt);
+          }
+        }
+      }
+      // strides 8 .. D/2 across the lanes of the row
+#pragma unroll
+      for (int ls = 1; ls < LANES; ls <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float other = __shfl_xor_sync(0xffffffffu, v[i], ls);
+          v[i] = (sub & ls) ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if constexpr (D == 128)
+          v[i] = __fdiv_rn(v[i], 11.313708498984761f);  // fp32(sqrt(128)), correctly rounded divide
+        else
+          v[i] = __fmul_rn(v[i], 0.125f);  // 1/sqrt(64), exact
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = bf16_round(v[i]);
+    float q[8];
+    uint32_t nib = 0, meta_word = 0;
+    if (p.levels != 0) {
+      nib = hif4_quant8(v, p.levels, q, meta_word);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[i] = v[i];
+    }
+    if (!live) continue;
+    __nv_bfloat16* dst = p.out + b * p.ob + h * p.oh + s * p.os + sub * 8;
+    if (p.out_vec) {
+      uint4 u;
+      u.x = exact_bf16_bits(q[0]) | (exact_bf16_bits(q[1]) << 16);
+      u.y = exact_bf16_bits(q[2]) | (exact_bf16_bits(q[3]) << 16);
+      u.z = exact_bf16_bits(q[4]) | (exact_bf16_bits(q[5]) << 16);
+      u.w = exact_bf16_bits(q[6]) | (exact_bf16_bits(q[7]) << 16);
+      *reinterpret_cast<uint4*>(dst) = u;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[i] = __ushort_as_bfloat16(static_cast<unsigned short>(exact_bf16_bits(q[i])));
+    }
+    if (p.levels != 0) {
+      if (p.codes) reinterpret_cast<uint32_t*>(p.codes + r * (D / 2))[sub] = nib;
+      if (p.meta && (lane & 7) == 0) p.meta[r * (D / 64) + sub / 8] = meta_word;
+    }
+  }
+}
+
+}  // namespace faq
+
+extern "C" int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb,
+                           int64_t sh, int64_t ss, const float* offset, const float* smooth, int64_t smooth_head_stride,
+                           int smooth_mode, int rotate, int levels, void* out, int64_t ob, int64_t oh, int64_t os,
+                           uint8_t* codes, uint32_t* meta, void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(x && out, "null pointer");
+  FAQ_CHECK_ARG(x_dtype == FAQ_BF16 || x_dtype == FAQ_F32, "x_dtype must be FAQ_BF16 or FAQ_F32");
+  FAQ_CHECK_ARG(batch >= 0 && heads > 0 && seq >= 0, "bad shape");
+  if (d != 64 && d != 128) return fail(FAQ_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  FAQ_CHECK_ARG(smooth_mode >= 0 && smooth_mode <= 2, "smooth_mode must be 0, 1 or 2");
+  FAQ_CHECK_ARG(smooth_mode == 0 || smooth != nullptr, "smooth_mode needs smooth");
+  FAQ_CHECK_ARG(levels == 0 || levels == 123 || levels == 12 || levels == 13, "levels must be 0, 123, 12 or 13");
+  FAQ_CHECK_ARG(levels != 0 || (codes == nullptr && meta == nullptr), "codes/meta need levels");
+  FAQ_CHECK_ARG(!codes || (reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
+  if (batch == 0 || seq == 0) return FAQ_OK;
+  QkPrepParams p;
+  p.x = x;
+  p.batch = batch;
+  p.heads = heads;
+  p.seq = seq;
+  p.sb = sb;
+  p.sh = sh;
+  p.ss = ss;
+  p.offset = offset;
+  p.smooth = smooth;
+  p.smooth_head_stride = smooth_head_stride;
+  p.smooth_mode = smooth_mode;
+  p.rotate = rotate;
+  p.levels = levels;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ob = ob;
+  p.oh = oh;
+  p.os = os;
+  p.codes = codes;
+  p.meta = meta;
+  const int64_t vec_elems = x_dtype == FAQ_BF16 ? 8 : 4;
+  p.x_vec = aligned16(x) && sb % vec_elems == 0 && sh % vec_elems == 0 && ss % vec_elems == 0;
+  p.out_vec = aligned16(out) && ob % 8 == 0 && oh % 8 == 0 && os % 8 == 0;
+  const int64_t rows = batch * heads * seq;
+  const int rows_per_block = 8 * (32 / (d / 8));
+  const int64_t blocks = std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
+                                           static_cast<int64_t>(num_sms()) * 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+  if (x_dtype == FAQ_BF16) {
+    if (d == 128)
+      qk_prep_kernel<__nv_bfloat16, 128><<<g, 256, 0, st>>>(p);
+    else
+      qk_prep_kernel<__nv_bfloat16, 64><<<g, 256, 0, st>>>(p);
+  } else {
+    if (d == 128)
+      qk_prep_kernel<float, 128><<<g, 256, 0, st>>>(p);
+    else
+      qk_prep_kernel<float, 64><<<g, 256, 0, st>>>(p);
+  }
+  return launch_status("qk_prep_kernel");
+}

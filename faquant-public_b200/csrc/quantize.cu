@@ -1,0 +1,491 @@
+// K1 (activation rotation + HiF4 quantization), HiF4 dequantization and K2 (weight
+// packing). All three are HBM-bound streaming kernels: one pass over the input,
+// 16-byte vector accesses, outputs written once.
+//
+// K1 with a rotation works on whole rows staged in shared memory, because the
+// HiSQ permutation gathers from anywhere in the row (hisq_rotation.py:50-71):
+//   1. the row is loaded into shared memory (x dtype; input_scale applied);
+//   2. each warp takes segments of 32*E consecutive output channels (E = max(1,
+//      block/32)); lane l holds channels seg + 32 i + l, i < E, gathered through
+//      the permutation with the sign applied in fp32 (quantization.py:212-213);
+//      the Walsh-Hadamard butterflies run in the reference's stage order (stride
+//      1, 2, ..., block/2, each (l + r, l - r), rotation.py:22-28): strides < 32
+//      across lanes with shuffles, larger strides inside a lane;
+//   3. normalization by 1/sqrt(block): an exact power-of-two multiply when
+//      log2(block) is even, else a correctly rounded divide by fp32(sqrt(block))
+//      (torch's CPU `x / math.sqrt(n)`), then one rounding to x's dtype;
+//   4. HiF4 quantization: 8 values per thread, 8 lanes per 64-block (hif4.cuh).
+#include <cmath>
+
+#include "common.cuh"
+#include "hif4.cuh"
+
+namespace faq {
+
+// number of valid values (0..8) in an 8-value chunk with `left` values left in the row
+__device__ __forceinline__ int valid8(int64_t left) { return left <= 0 ? 0 : (left >= 8 ? 8 : static_cast<int>(left)); }
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ float round_to(float v);
+template <>
+__device__ __forceinline__ float round_to<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float round_to<__nv_bfloat16>(float v) { return bf16_round(v); }
+
+// Load 8 consecutive elements of type T starting at p (16-byte vectors when `vec`).
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8], bool vec, int valid) {
+  if (vec && valid >= 8) {
+    if constexpr (sizeof(T) == 2) {
+      const uint4 u = *reinterpret_cast<const uint4*>(p);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else {
+      const float4 a = reinterpret_cast<const float4*>(p)[0];
+      const float4 b = reinterpret_cast<const float4*>(p)[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < valid ? to_f32<T>(p[i]) : 0.0f;
+  }
+}
+
+// Store 8 values (exactly representable in T) at p.
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&v)[8], bool vec, int valid) {
+  if (vec && valid >= 8) {
+    if constexpr (sizeof(T) == 2) {
+      uint4 u;
+      u.x = exact_bf16_bits(v[0]) | (exact_bf16_bits(v[1]) << 16);
+      u.y = exact_bf16_bits(v[2]) | (exact_bf16_bits(v[3]) << 16);
+      u.z = exact_bf16_bits(v[4]) | (exact_bf16_bits(v[5]) << 16);
+      u.w = exact_bf16_bits(v[6]) | (exact_bf16_bits(v[7]) << 16);
+      *reinterpret_cast<uint4*>(p) = u;
+    } else {
+      reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  } else {
+    for (int i = 0; i < 8 && i < valid; ++i) {
+      if constexpr (sizeof(T) == 2)
+        p[i] = __ushort_as_bfloat16(static_cast<unsigned short>(exact_bf16_bits(v[i])));
+      else
+        p[i] = v[i];
+    }
+  }
+}
+
+struct QuantOut {
+  uint8_t* codes;   // [rows, k64/2] or null
+  uint32_t* meta;   // [rows, k64/64] or null
+  void* qdq;        // [rows, ldq] or null
+  int64_t ldq;
+  bool qdq_vec;
+};
+
+// Quantize the 8 values of chunk `c` (columns 8c..8c+7) of row `row` and write outputs.
+template <typename T>
+__device__ __forceinline__ void quantize_and_store(const float (&v)[8], int64_t row, int64_t c, int64_t k,
+                                                   int64_t k64, int levels, const QuantOut& o) {
+  float q[8];
+  uint32_t meta_word;
+  const uint32_t nib = hif4_quant8(v, levels, q, meta_word);
+  if (o.codes) reinterpret_cast<uint32_t*>(o.codes + row * (k64 / 2))[c] = nib;
+  if (o.meta && (threadIdx.x & 7) == 0) o.meta[row * (k64 / 64) + c / 8] = meta_word;
+  if (o.qdq) {
+    const int64_t col = c * 8;
+    const int valid = valid8(k - col);
+    if (valid > 0) store8<T>(static_cast<T*>(o.qdq) + row * o.ldq + col, q, o.qdq_vec, valid);
+  }
+}
+
+// ---------------------------------------------------------------- K1, no rotation
+// One thread per 8 values; threads of a row are consecutive so that each 64-block
+// is held by 8 aligned lanes. Rows are padded to k64 with zeros.
+template <typename T>
+__global__ void __launch_bounds__(256) hif4_quantize_direct_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
+                                                                   int64_t ldx, const T* __restrict__ input_scale,
+                                                                   bool x_vec, int levels, QuantOut o) {
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const int64_t chunks_per_row = k64 / 8;
+  const int64_t total = rows * chunks_per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // every lane of a warp runs the same number of iterations (the shuffles need
+  // all 32): the loop bound is rounded up to a whole warp.
+  const int64_t total_warps = (total + 31) / 32 * 32;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx - threadIdx.x % 32 < total_warps;
+       idx += stride) {
+    const bool live = idx < total;
+    const int64_t row = live ? idx / chunks_per_row : 0;
+    const int64_t c = live ? idx % chunks_per_row : 0;
+    const int64_t col = c * 8;
+    const int valid = live ? valid8(k - col) : 0;
+    float v[8];
+    load8<T>(x + row * ldx + col, v, x_vec, valid);
+    if (input_scale != nullptr) {
+      float s[8];
+      load8<T>(input_scale + col, s, x_vec, valid);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = round_to<T>(__fmul_rn(v[i], s[i]));
+    }
+    float q[8];
+    uint32_t meta_word;
+    const uint32_t nib = hif4_quant8(v, levels, q, meta_word);
+    if (!live) continue;
+    if (o.codes) reinterpret_cast<uint32_t*>(o.codes + row * (k64 / 2))[c] = nib;
+    if (o.meta && (threadIdx.x & 7) == 0) o.meta[row * (k64 / 64) + c / 8] = meta_word;
+    if (o.qdq && valid > 0) store8<T>(static_cast<T*>(o.qdq) + row * o.ldq + col, q, o.qdq_vec, valid);
+  }
+}
+
+// ---------------------------------------------------------------- K1, rotation
+template <typename T, int LOG2B>
+__global__ void __launch_bounds__(256) hif4_quantize_rotate_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
+                                                                   int64_t ldx, const T* __restrict__ input_scale,
+                                                                   const int8_t* __restrict__ signs,
+                                                                   const int64_t* __restrict__ perm, bool x_vec,
+                                                                   int levels, QuantOut o) {
+  constexpr int B = 1 << LOG2B;
+  constexpr int E = B >= 32 ? B / 32 : 1;  // elements per lane in a segment
+  constexpr int SEG = 32 * E;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int64_t k64 = (k + 63) / 64 * 64;
+  // layout: src index | sign bit (int32 [k]) ; row in x dtype [k64] ; rotated row [k64]
+  int32_t* s_map = reinterpret_cast<int32_t*>(smem_raw);
+  T* s_in = reinterpret_cast<T*>(smem_raw + ((k * 4 + 15) / 16) * 16);
+  T* s_rot = s_in + k64;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+
+  for (int64_t j = tid; j < k; j += blockDim.x) {
+    const int64_t src = perm ? perm[j] : j;
+    s_map[j] = static_cast<int32_t>(src << 1) | (signs[src] < 0 ? 1 : 0);
+  }
+  __syncthreads();
+
+  const int64_t nseg = (k + SEG - 1) / SEG;
+  const int64_t chunks = k64 / 8;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    // 1. stage the row (input_scale applied in x's dtype)
+    for (int64_t c = tid; c < chunks; c += blockDim.x) {
+      const int64_t col = c * 8;
+      const int valid = valid8(k - col);
+      float v[8];
+      load8<T>(x + row * ldx + col, v, x_vec, valid);
+      if (input_scale != nullptr) {
+        float s[8];
+        load8<T>(input_scale + col, s, x_vec, valid);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = round_to<T>(__fmul_rn(v[i], s[i]));
+      }
+      store8<T>(s_in + col, v, true, 8);
+    }
+    __syncthreads();
+    // 2-3. gather, butterflies, normalization, rounding
+    for (int64_t seg = warp; seg < nseg; seg += nwarps) {
+      float v[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int64_t j = seg * SEG + i * 32 + lane;
+        float val = 0.0f;
+        if (j < k) {
+          const int32_t m = s_map[j];
+          val = to_f32<T>(s_in[m >> 1]);
+          if (m & 1) val = -val;  // x * (-1) in fp32 is exact
+        }
+        v[i] = val;
+      }
+#pragma unroll
+      for (int st = 1; st < B; st <<= 1) {
+        if (st < 32) {
+#pragma unroll
+          for (int i = 0; i < E; ++i) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[i], st);
+            v[i] = (lane & st) ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+          }
+        } else {
+          const int d = st >> 5;
+#pragma unroll
+          for (int i = 0; i < E; ++i) {
+            if ((i & d) == 0) {
+              const float l = v[i], r = v[i + d];
+              v[i] = __fadd_rn(l, r);
+              v[i + d] = __fsub_rn(l, r);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        float r;
+        if constexpr ((LOG2B & 1) == 0) {
+          r = __fmul_rn(v[i], pow2f(-(LOG2B / 2)));
+        } else {
+          r = __fdiv_rn(v[i], static_cast<float>(LOG2B == 1 ? 1.4142135623730951 : LOG2B == 3 ? 2.8284271247461903
+                                                : LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
+                                                : 22.627416997969522));
+        }
+        const int64_t j = seg * SEG + i * 32 + lane;
+        if (j < k64) {
+          if constexpr (sizeof(T) == 2)
+            s_rot[j] = __float2bfloat16_rn(r);
+          else
+            s_rot[j] = r;
+        }
+      }
+    }
+    __syncthreads();
+    // 4. quantize the rotated row
+    for (int64_t c0 = 0; c0 < chunks; c0 += blockDim.x) {
+      const int64_t c = c0 + tid;
+      float v[8];
+      const int64_t col = c * 8;
+      const int valid = c < chunks ? valid8(k - col) : 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = i < valid ? to_f32<T>(s_rot[col + i]) : 0.0f;
+      float q[8];
+      uint32_t meta_word;
+      const uint32_t nib = hif4_quant8(v, levels, q, meta_word);
+      if (c < chunks) {
+        if (o.codes) reinterpret_cast<uint32_t*>(o.codes + row * (k64 / 2))[c] = nib;
+        if (o.meta && (tid & 7) == 0) o.meta[row * (k64 / 64) + c / 8] = meta_word;
+        if (o.qdq && valid > 0) store8<T>(static_cast<T*>(o.qdq) + row * o.ldq + col, q, o.qdq_vec, valid);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- dequantize
+template <typename T>
+__global__ void __launch_bounds__(256) hif4_dequantize_kernel(const uint8_t* __restrict__ codes,
+                                                              const uint32_t* __restrict__ meta, int64_t rows,
+                                                              int64_t k, T* __restrict__ out, int64_t ldo, bool vec) {
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const int64_t chunks_per_row = k64 / 8;
+  const int64_t total = rows * chunks_per_row;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = idx / chunks_per_row, c = idx % chunks_per_row;
+    const int64_t col = c * 8;
+    const int valid = valid8(k - col);
+    if (valid == 0) continue;
+    const uint32_t nib = reinterpret_cast<const uint32_t*>(codes + row * (k64 / 2))[c];
+    const uint32_t m = meta[row * (k64 / 64) + c / 8];
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = hif4_decode((nib >> (4 * i)) & 0xFu, m, static_cast<int>((col & 63) + i));
+    store8<T>(out + row * ldo + col, v, vec, valid);
+  }
+}
+
+// ---------------------------------------------------------------- K2: pack weights
+// With GPTQ metadata: code = clamp(round(|w| / ds * 4), 0, 7) (hif4.py:311, torch.round
+// is half-to-even = rintf); without it, the RTN fit of the quantizer. Values the
+// packed form does not reproduce exactly are counted in *mismatches.
+template <typename T>
+__global__ void __launch_bounds__(256) hif4_pack_kernel(const T* __restrict__ w, int64_t n, int64_t k, int64_t ldw,
+                                                        const float* __restrict__ scale, const int8_t* __restrict__ lv2,
+                                                        const int8_t* __restrict__ lv3, bool w_vec, int levels,
+                                                        uint8_t* __restrict__ codes, uint32_t* __restrict__ meta,
+                                                        unsigned long long* mismatches) {
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const int64_t chunks_per_row = k64 / 8;
+  const int64_t total = n * chunks_per_row;
+  const int64_t total_warps = (total + 31) / 32 * 32;
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx - threadIdx.x % 32 < total_warps;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const bool live = idx < total;
+    const int64_t row = live ? idx / chunks_per_row : 0, c = live ? idx % chunks_per_row : 0;
+    const int64_t col = c * 8;
+    const int valid = live ? valid8(k - col) : 0;
+    float v[8];
+    load8<T>(w + row * ldw + col, v, w_vec, valid);
+    uint32_t nib = 0, meta_word = 0;
+    float q[8];
+    if (scale == nullptr) {
+      nib = hif4_quant8(v, levels, q, meta_word);
+    } else if (live) {
+      const int64_t blk = row * (k64 / 64) + c / 8;
+      const int pos = static_cast<int>(c & 7);
+      const float s = scale[blk];
+      const int e2 = lv2[blk * 8 + pos];
+      const int e3a = lv3[blk * 16 + 2 * pos], e3b = lv3[blk * 16 + 2 * pos + 1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float ds = __fmul_rn(s, pow2f(e2 + (i < 4 ? e3a : e3b)));
+        const float m = fminf(fmaxf(rintf(__fmul_rn(__fdiv_rn(fabsf(v[i]), ds), 4.0f)), 0.0f), 7.0f);
+        const bool neg = v[i] < 0.0f;
+        const float mag = __fmul_rn(__fmul_rn(m, 0.25f), ds);
+        q[i] = neg ? -mag : mag;
+        nib |= (static_cast<uint32_t>(m) | (static_cast<uint32_t>(neg) << 3)) << (4 * i);
+      }
+      const int e = exponent_of(s);
+      meta_word = (static_cast<uint32_t>(e + 48) << 2) | (static_cast<uint32_t>(__fmul_rn(s, pow2f(2 - e))) - 4u);
+      uint32_t bits = (static_cast<uint32_t>(e2) << (8 + pos)) | (static_cast<uint32_t>(e3a) << (16 + 2 * pos)) |
+                      (static_cast<uint32_t>(e3b) << (17 + 2 * pos));
+      meta_word |= bits;
+    }
+    if (scale != nullptr) {
+      // gather the lv bits of the 8 lanes of the block
+      uint32_t bits = meta_word & 0xFFFFFF00u;
+      bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+      bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+      bits |= __shfl_xor_sync(0xffffffffu, bits, 4);
+      meta_word = (meta_word & 0xFFu) | bits;
+    }
+    if (!live) continue;
+    int bad = 0;
+    for (int i = 0; i < valid; ++i) bad += (__float_as_uint(q[i]) != __float_as_uint(v[i])) && !(q[i] == 0.0f && v[i] == 0.0f);
+    if (bad && mismatches) atomicAdd(mismatches, static_cast<unsigned long long>(bad));
+    reinterpret_cast<uint32_t*>(codes + row * (k64 / 2))[c] = nib;
+    if ((threadIdx.x & 7) == 0) meta[row * (k64 / 64) + c / 8] = meta_word;
+  }
+}
+
+// ---------------------------------------------------------------- host launchers
+static bool valid_levels(int levels) { return levels == 123 || levels == 12 || levels == 13; }
+
+template <typename T>
+static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* input_scale,
+                           const int8_t* signs, const int64_t* perm, int rot_block, int levels, const QuantOut& o,
+                           cudaStream_t stream) {
+  const bool x_vec = aligned16(x) && (ldx * static_cast<int64_t>(sizeof(T))) % 16 == 0 &&
+                     (input_scale == nullptr || aligned16(input_scale));
+  const int sms = num_sms();
+  if (signs == nullptr) {
+    const int64_t k64 = (k + 63) / 64 * 64;
+    const int64_t threads = rows * (k64 / 8);
+    const int64_t blocks = std::min<int64_t>((threads + 255) / 256, static_cast<int64_t>(sms) * 16);
+    hif4_quantize_direct_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const T*>(x), rows, k, ldx, static_cast<const T*>(input_scale), x_vec, levels, o);
+    return launch_status("hif4_quantize_direct_kernel");
+  }
+  int block = rot_block == 0 ? 1 : rot_block;
+  int log2b = 0;
+  while ((1 << log2b) < block) ++log2b;
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const size_t smem = static_cast<size_t>((k * 4 + 15) / 16 * 16) + 2 * static_cast<size_t>(k64) * sizeof(T);
+  if (smem > 220 * 1024)
+    return fail(FAQ_ERR_UNSUPPORTED, "rotated row of k=" + std::to_string(k) + " does not fit in shared memory");
+  const int per_sm = std::max(1, static_cast<int>((228 * 1024) / (smem + 1024)));
+  const int64_t blocks = std::min<int64_t>(rows, static_cast<int64_t>(sms) * std::min(per_sm, 8));
+  if (blocks == 0) return FAQ_OK;
+#define FAQ_ROT_CASE(L)                                                                                         \
+  case L: {                                                                                                     \
+    auto kern = hif4_quantize_rotate_kernel<T, L>;                                                              \
+    FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))); \
+    kern<<<static_cast<unsigned>(blocks), 256, smem, stream>>>(static_cast<const T*>(x), rows, k, ldx,           \
+                                                               static_cast<const T*>(input_scale), signs, perm, \
+                                                               x_vec, levels, o);                               \
+    return launch_status("hif4_quantize_rotate_kernel");                                                       \
+  }
+  switch (log2b) {
+    FAQ_ROT_CASE(0)
+    FAQ_ROT_CASE(1)
+    FAQ_ROT_CASE(2)
+    FAQ_ROT_CASE(3)
+    FAQ_ROT_CASE(4)
+    FAQ_ROT_CASE(5)
+    FAQ_ROT_CASE(6)
+    FAQ_ROT_CASE(7)
+    FAQ_ROT_CASE(8)
+    FAQ_ROT_CASE(9)
+    FAQ_ROT_CASE(10)
+    default:
+      return fail(FAQ_ERR_UNSUPPORTED, "rotation block " + std::to_string(rot_block) + " > 1024");
+  }
+#undef FAQ_ROT_CASE
+}
+
+}  // namespace faq
+
+using namespace faq;
+
+extern "C" int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
+                                 const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block,
+                                 int levels, uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
+  FAQ_CHECK_ARG(x != nullptr, "x is null");
+  FAQ_CHECK_ARG(x_dtype == FAQ_BF16 || x_dtype == FAQ_F32, "x_dtype must be FAQ_BF16 or FAQ_F32");
+  FAQ_CHECK_ARG(rows >= 0 && k > 0, "need rows >= 0 and k > 0 (HiF4 does not support an empty axis)");
+  FAQ_CHECK_ARG(ldx >= k, "ldx < k");
+  FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
+  FAQ_CHECK_ARG(codes || meta || qdq, "all outputs are null");
+  FAQ_CHECK_ARG(qdq == nullptr || ldq >= k, "ldq < k");
+  FAQ_CHECK_ARG(!codes || (reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
+  FAQ_CHECK_ARG(!meta || (reinterpret_cast<uintptr_t>(meta) & 3) == 0, "meta must be 4-byte aligned");
+  FAQ_CHECK_ARG(perm == nullptr || signs != nullptr, "a permutation needs signs (pass all-ones signs)");
+  if (signs != nullptr) {
+    FAQ_CHECK_ARG(rot_block >= 0 && (rot_block & (rot_block - 1)) == 0, "rot_block must be 0 or a power of two");
+    FAQ_CHECK_ARG(rot_block == 0 || k % rot_block == 0, "k must be divisible by rot_block");
+    FAQ_CHECK_ARG(k < (int64_t(1) << 30), "k too large");
+  }
+  if (rows == 0) return FAQ_OK;
+  QuantOut o{codes, meta, qdq, ldq, false};
+  const size_t es = x_dtype == FAQ_BF16 ? 2 : 4;
+  o.qdq_vec = qdq && aligned16(qdq) && (ldq * static_cast<int64_t>(es)) % 16 == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (x_dtype == FAQ_BF16)
+    return launch_quantize<__nv_bfloat16>(x, rows, k, ldx, input_scale, signs, perm, rot_block, levels, o, s);
+  return launch_quantize<float>(x, rows, k, ldx, input_scale, signs, perm, rot_block, levels, o, s);
+}
+
+extern "C" int faq_hif4_dequantize(const uint8_t* codes, const uint32_t* meta, int64_t rows, int64_t k, void* out,
+                                   int out_dtype, int64_t ldo, void* stream) {
+  FAQ_CHECK_ARG(codes && meta && out, "null pointer");
+  FAQ_CHECK_ARG(out_dtype == FAQ_BF16 || out_dtype == FAQ_F32, "out_dtype must be FAQ_BF16 or FAQ_F32");
+  FAQ_CHECK_ARG(rows >= 0 && k > 0 && ldo >= k, "bad shape");
+  FAQ_CHECK_ARG((reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
+  if (rows == 0) return FAQ_OK;
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const int64_t blocks = std::min<int64_t>((rows * (k64 / 8) + 255) / 256, static_cast<int64_t>(num_sms()) * 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t es = out_dtype == FAQ_BF16 ? 2 : 4;
+  const bool vec = aligned16(out) && (ldo * static_cast<int64_t>(es)) % 16 == 0;
+  if (out_dtype == FAQ_BF16)
+    hif4_dequantize_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        codes, meta, rows, k, static_cast<__nv_bfloat16*>(out), ldo, vec);
+  else
+    hif4_dequantize_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, s>>>(codes, meta, rows, k,
+                                                                                static_cast<float*>(out), ldo, vec);
+  return launch_status("hif4_dequantize_kernel");
+}
+
+extern "C" int faq_hif4_pack_weight(const void* w, int w_dtype, int64_t n, int64_t k, int64_t ldw,
+                                    const float* scale, const int8_t* lv2, const int8_t* lv3, int levels,
+                                    uint8_t* codes, uint32_t* meta, unsigned long long* mismatches, void* stream) {
+  FAQ_CHECK_ARG(w && codes && meta, "null pointer");
+  FAQ_CHECK_ARG(w_dtype == FAQ_BF16 || w_dtype == FAQ_F32, "w_dtype must be FAQ_BF16 or FAQ_F32");
+  FAQ_CHECK_ARG(n >= 0 && k > 0 && ldw >= k, "bad shape");
+  FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
+  FAQ_CHECK_ARG((scale == nullptr) == (lv2 == nullptr) && (scale == nullptr) == (lv3 == nullptr),
+                "scale, lv2 and lv3 come together");
+  FAQ_CHECK_ARG(scale == nullptr || k % 64 == 0, "GPTQ metadata needs k % 64 == 0");
+  FAQ_CHECK_ARG((reinterpret_cast<uintptr_t>(codes) & 3) == 0 && (reinterpret_cast<uintptr_t>(meta) & 3) == 0,
+                "codes/meta must be 4-byte aligned");
+  if (n == 0) return FAQ_OK;
+  const int64_t k64 = (k + 63) / 64 * 64;
+  const int64_t blocks = std::min<int64_t>((n * (k64 / 8) + 255) / 256, static_cast<int64_t>(num_sms()) * 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t es = w_dtype == FAQ_BF16 ? 2 : 4;
+  const bool vec = aligned16(w) && (ldw * static_cast<int64_t>(es)) % 16 == 0;
+  if (w_dtype == FAQ_BF16)
+    hif4_pack_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(w), n, k, ldw, scale, lv2, lv3, vec, levels, codes, meta, mismatches);
+  else
+    hif4_pack_kernel<float><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const float*>(w), n, k, ldw, scale, lv2, lv3, vec, levels, codes, meta, mismatches);
+  return launch_status("hif4_pack_kernel");
+}

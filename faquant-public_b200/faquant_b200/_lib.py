@@ -1,0 +1,94 @@
+"""ctypes binding of ``libfaquant_b200.so`` (the C ABI of ``include/faquant_b200.h``).
+
+The library sits next to this file (built in-tree by ``build.py``). Loading it
+is the only way these operators run: a missing library or a missing CUDA device
+raises, there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libfaquant_b200.so")
+
+FAQ_OK = 0
+FAQ_BF16 = 0
+FAQ_F32 = 1
+FAQ_STATUS_TIMEOUT = 1
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+
+# name -> argument types (all return int status)
+SIGNATURES: dict[str, list] = {
+    "faq_version": [],
+    "faq_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "faq_device_status": [ctypes.POINTER(ctypes.c_uint), _int],
+    "faq_hif4_quantize": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int, _int,
+                          _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
+    "faq_hif4_dequantize": [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _int, _i64, _c_void_p],
+    "faq_hif4_pack_weight": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
+                             _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+    "faq_gemm_bf16_tn": [_c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64,
+                         _c_void_p],
+    "faq_qk_prep": [_c_void_p, _int, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _int,
+                    _int, _int, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
+    "faq_hif4_attention": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
+                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _int,
+                           _int, _c_void_p, _i64, _i64, _i64, _c_void_p],
+    "faq_selftest_wait_timeout": [_i64, _c_void_p],
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class FaqError(RuntimeError):
+    """A C-ABI call returned an error status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once) and declare every exported signature."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise FaqError(
+                    f"{LIB_PATH} is missing; build it with `python faquant-public_b200/build.py` "
+                    "(the HiF4 operators have no CPU fallback)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, argtypes in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = ctypes.c_int
+            _lib = lib
+        return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    load().faq_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+_CODE_NAMES = {1: "FAQ_ERR_ARG", 2: "FAQ_ERR_CUDA", 3: "FAQ_ERR_UNSUPPORTED", 4: "FAQ_ERR_TIMEOUT"}
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FAQ_OK:
+        exc = ValueError if rc == 1 else NotImplementedError if rc == 3 else FaqError
+        raise exc(f"{what}: {_CODE_NAMES.get(rc, rc)}: {last_error()}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)
+
+
+def device_status(reset: bool = False) -> int:
+    status = ctypes.c_uint(0)
+    check(load().faq_device_status(ctypes.byref(status), int(reset)), "faq_device_status")
+    return status.value

@@ -1,0 +1,285 @@
+"""Tensor-level entry points over the C ABI (device tensors in, device tensors out).
+
+Each function validates its torch arguments, allocates the outputs with torch
+(the library itself never allocates) and launches on the current CUDA stream.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+
+LEVELS = {"123": 123, "12": 12, "13": 13}
+
+
+def levels_code(levels: str | int) -> int:
+    key = str(levels)
+    if key not in LEVELS:
+        raise ValueError(f"HiF4 levels must be one of {tuple(LEVELS)}, got {levels!r}")
+    return LEVELS[key]
+
+
+def default_levels(kind: str) -> str:
+    """The reference's process-wide level variants (``src/faquant/hif4.py:13-43``).
+
+    ``kind`` is ``weight``, ``act`` or one of the attention operands ``q``, ``k``,
+    ``p``, ``v``. Read from the same environment variables, at call time.
+    """
+    weight = os.environ.get("FAQUANT_HIF4_SCALE_LEVELS", "123")
+    act = os.environ.get("FAQUANT_HIF4_ACT_SCALE_LEVELS", weight)
+    attn = os.environ.get("FAQUANT_HIF4_ATTN_SCALE_LEVELS", act)
+    if kind == "weight":
+        value = weight
+    elif kind == "act":
+        value = act
+    elif kind in ("q", "k", "p", "v"):
+        value = attn
+        for entry in filter(None, os.environ.get("FAQUANT_HIF4_ATTN_OPERAND_LEVELS", "").split(",")):
+            operand, _, val = entry.partition("=")
+            if operand == kind:
+                value = val
+    else:
+        raise ValueError(f"unknown HiF4 operand kind {kind!r}")
+    levels_code(value)
+    return value
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.FAQ_BF16
+    if t.dtype == torch.float32:
+        return _lib.FAQ_F32
+    raise TypeError(f"unsupported dtype {t.dtype}; the HiF4 kernels take bfloat16 or float32")
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("faquant_b200 operators run on CUDA tensors only (no CPU fallback)")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    if device is None:
+        raise RuntimeError("no CUDA tensor given")
+    return device
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _rows_view(x: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """``x [..., k]`` as a 2-D row view and its row stride (copies only when needed)."""
+    k = x.shape[-1]
+    if x.dim() == 2 and x.stride(1) == 1 and x.stride(0) >= k:
+        return x, x.stride(0)
+    return x.contiguous().reshape(-1, k), k
+
+
+def hif4_quantize(
+    x: torch.Tensor,
+    *,
+    levels: str | int = "123",
+    input_scale: torch.Tensor | None = None,
+    signs: torch.Tensor | None = None,
+    permutation: torch.Tensor | None = None,
+    rot_block: int | None = None,
+    want_qdq: bool = True,
+    want_codes: bool = False,
+) -> tuple[torch.Tensor | None, torch.Tensor | None, torch.Tensor | None]:
+    """Rotation (optional) + HiF4 quantization of ``x [..., k]`` along the last axis.
+
+    Returns ``(qdq, codes, meta)``: the dequantized values in ``x.dtype`` (shape of
+    ``x``) and the packed codes ``uint8 [rows, k64/2]`` / meta ``int32 [rows, k64/64]``.
+    """
+    device = _require_cuda(x, input_scale, signs, permutation)
+    if x.shape[-1] == 0:
+        raise ValueError("HiF4 does not support an empty axis")
+    k = x.shape[-1]
+    rows, ldx = _rows_view(x)
+    n = rows.shape[0]
+    k64 = (k + 63) // 64 * 64
+    qdq = torch.empty((n, k), dtype=x.dtype, device=device) if want_qdq else None
+    codes = torch.empty((n, k64 // 2), dtype=torch.uint8, device=device) if want_codes else None
+    meta = torch.empty((n, k64 // 64), dtype=torch.int32, device=device) if want_codes else None
+    if input_scale is not None:
+        input_scale = input_scale.to(device=device, dtype=x.dtype).contiguous()
+        if input_scale.numel() != k:
+            raise ValueError("input_scale must have one entry per input channel")
+    if signs is not None:
+        signs = signs.to(device=device, dtype=torch.int8).contiguous()
+        if permutation is not None:
+            permutation = permutation.to(device=device, dtype=torch.int64).contiguous()
+    block = 0 if rot_block is None else int(rot_block)
+    _lib.call(
+        "faq_hif4_quantize", rows.data_ptr(), _dtype_code(x), n, k, ldx, _ptr(input_scale), _ptr(signs),
+        _ptr(permutation), block, levels_code(levels), _ptr(codes), _ptr(meta), _ptr(qdq), k, _stream(device),
+    )
+    if qdq is not None:
+        qdq = qdq.reshape(x.shape)
+    return qdq, codes, meta
+
+
+def hif4_dequantize(codes: torch.Tensor, meta: torch.Tensor, k: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    device = _require_cuda(codes, meta)
+    rows = codes.shape[0]
+    out = torch.empty((rows, k), dtype=dtype, device=device)
+    _lib.call("faq_hif4_dequantize", codes.contiguous().data_ptr(), meta.contiguous().data_ptr(), rows, k,
+              out.data_ptr(), _dtype_code(out), k, _stream(device))
+    return out
+
+
+def hif4_pack_weight(
+    weight: torch.Tensor,
+    *,
+    levels: str | int = "123",
+    scale: torch.Tensor | None = None,
+    lv2: torch.Tensor | None = None,
+    lv3: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """Pack an ``[n, k]`` HiF4-grid weight; returns ``(codes, meta, mismatches)``."""
+    device = _require_cuda(weight)
+    n, k = weight.shape
+    k64 = (k + 63) // 64 * 64
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    codes = torch.empty((n, k64 // 2), dtype=torch.uint8, device=device)
+    meta = torch.empty((n, k64 // 64), dtype=torch.int32, device=device)
+    counter = torch.zeros(1, dtype=torch.int64, device=device)
+    if scale is not None:
+        scale = scale.to(device=device, dtype=torch.float32).reshape(n, k // 64).contiguous()
+        lv2 = lv2.to(device=device, dtype=torch.int8).reshape(n, k // 64, 8).contiguous()
+        lv3 = lv3.to(device=device, dtype=torch.int8).reshape(n, k // 64, 16).contiguous()
+    _lib.call("faq_hif4_pack_weight", w.data_ptr(), _dtype_code(w), n, k, w.stride(0), _ptr(scale), _ptr(lv2),
+              _ptr(lv3), levels_code(levels), codes.data_ptr(), meta.data_ptr(), counter.data_ptr(), _stream(device))
+    return codes, meta, int(counter.item())
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``a [m, k] @ b [n, k]^T (+ bias)`` in bf16 with fp32 accumulation (tcgen05)."""
+    device = _require_cuda(a, b, bias)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("gemm_bf16 takes bfloat16 operands")
+    if a.stride(-1) != 1:
+        a = a.contiguous()
+    if b.stride(-1) != 1:
+        b = b.contiguous()
+    m, k = a.shape
+    n = b.shape[0]
+    if b.shape[1] != k:
+        raise ValueError("inner dimensions differ")
+    lda = a.stride(0) if m > 1 else k
+    ldb = b.stride(0) if n > 1 else k
+    if k % 8 or lda % 8 or ldb % 8 or a.data_ptr() % 16 or b.data_ptr() % 16:
+        # TMA wants 16-byte aligned rows: pad k with zeros, which adds nothing to the sums
+        k8 = (k + 7) // 8 * 8
+        a = torch.nn.functional.pad(a, (0, k8 - k))
+        b = torch.nn.functional.pad(b, (0, k8 - k))
+        k, lda, ldb = k8, k8, k8
+    if bias is not None:
+        bias = bias.to(device=device, dtype=torch.bfloat16).contiguous()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+    _lib.call("faq_gemm_bf16_tn", a.data_ptr(), lda, b.data_ptr(), ldb, m, n, k, _ptr(bias), out.data_ptr(),
+              out.stride(0) if m > 1 else n, _stream(device))
+    return out
+
+
+def selftest_wait_timeout(limit_ns: int) -> None:
+    device = torch.device("cuda", torch.cuda.current_device())
+    _lib.call("faq_selftest_wait_timeout", int(limit_ns), _stream(device))
+
+
+def qk_prep(
+    x: torch.Tensor,
+    *,
+    levels: str | int | None = "123",
+    rotate: bool = True,
+    smooth_scale: torch.Tensor | None = None,
+    smooth_mode: str | None = None,
+    key_offset: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    want_codes: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
+    """Attention operand preparation of ``x [B, H, S, D]`` (any strides, D contiguous).
+
+    ``smooth_mode`` is ``"mul"`` (Q), ``"div"`` (K) or None; ``smooth_scale`` is
+    ``[D]`` or ``[H, D]``; ``key_offset`` is ``[H, D]`` (K only). Returns the bf16
+    operand ``[B, H, S, D]`` (``out`` if given) and optional packed codes/meta.
+    """
+    device = _require_cuda(x, smooth_scale, key_offset)
+    if x.dim() != 4:
+        raise ValueError("qk_prep expects [batch, heads, seq, head_dim]")
+    b, h, s, d = x.shape
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=device)
+    mode = {None: 0, "mul": 1, "div": 2}[smooth_mode]
+    head_stride = 0
+    if smooth_scale is not None:
+        smooth_scale = smooth_scale.to(device=device, dtype=torch.float32).contiguous()
+        head_stride = d if smooth_scale.dim() == 2 else 0
+    if key_offset is not None:
+        key_offset = key_offset.to(device=device, dtype=torch.float32).reshape(h, d).contiguous()
+    lv = 0 if levels is None else levels_code(levels)
+    codes = meta = None
+    if want_codes and lv:
+        codes = torch.empty((b * h * s, d // 2), dtype=torch.uint8, device=device)
+        meta = torch.empty((b * h * s, d // 64), dtype=torch.int32, device=device)
+    _lib.call("faq_qk_prep", x.data_ptr(), _dtype_code(x), b, h, s, d, x.stride(0), x.stride(1), x.stride(2),
+              _ptr(key_offset), _ptr(smooth_scale), head_stride, mode, int(rotate), lv, out.data_ptr(),
+              out.stride(0), out.stride(1), out.stride(2), _ptr(codes), _ptr(meta), _stream(device))
+    return out, codes, meta
+
+
+def hif4_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    scale: float | None = None,
+    causal: bool = True,
+    p_levels: str | int | None = "123",
+    quantized_normalizer: bool = True,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """HiF4 QK/PV attention of pre-quantized bf16 operands.
+
+    ``q [B, Hq, Sq, 128]``, ``k/v [B, Hkv, Sk, 128]`` (any strides with the head dim
+    contiguous); returns ``[B, Sq, Hq, 128]`` bf16 (``out`` if given).
+    """
+    device = _require_cuda(q, k, v)
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.dim() != 4:
+            raise TypeError("hif4_attention takes rank-4 bfloat16 Q/K/V")
+    b, hq, sq, d = q.shape
+    _, hkv, sk, _ = k.shape
+    if v.shape != k.shape:
+        raise ValueError("K and V shapes differ")
+
+    def fix(t: torch.Tensor) -> torch.Tensor:
+        ok = t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+        return t if ok else t.contiguous()
+
+    q, k, v = fix(q), fix(k), fix(v)
+    if out is None:
+        out = torch.empty((b, sq, hq, d), dtype=torch.bfloat16, device=device)
+    scale = float(scale if scale is not None else d**-0.5)
+    lv = 0 if p_levels is None else levels_code(p_levels)
+    _lib.call("faq_hif4_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), b, hq, hkv, sq, sk, d,
+              q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+              v.stride(0), v.stride(1), v.stride(2), scale, int(causal), lv, int(quantized_normalizer),
+              out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), _stream(device))
+    return out

@@ -1,0 +1,240 @@
+"""HiF4 W4A4 Linear: the drop-in for ``faquant.quantization`` on B200.
+
+Mirrors ``src/faquant/quantization.py``: ``fake_quantize`` (:30-94),
+``FakeQuantLinear`` (:97-277) with the same constructor arguments, buffers and
+``state_dict`` keys, ``replace_linear_with_fake_quant`` (:300-375) and
+``quantize_qwen3_linears`` (:378-408). The forward pass is two launches of the
+C-ABI library: K1 (input scale, HiSQ signs/permutation/block Hadamard, HiF4
+quantization, bit-exact with the reference) and K3 (tcgen05 GEMM on the
+exactly-dequantized bf16 operands). Only ``quant_format="hif4"`` is implemented;
+every other format, and the QAD-only clamp/companding knobs, raise
+``NotImplementedError`` -- there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import ops
+
+HIF4_BLOCK_SIZE = 64
+
+
+def _is_pow2(n: int) -> bool:
+    return n > 0 and n & (n - 1) == 0
+
+
+def fake_quantize(
+    x: torch.Tensor,
+    *,
+    quant_format: str = "int",
+    bits: int = 4,
+    group_size: int = -1,
+    symmetric: bool = True,
+    clip_ratio: float = 1.0,
+    hif4_levels: str | None = None,
+) -> torch.Tensor:
+    """HiF4 quantize-dequantize on the device (``quantization.py:30-57`` argument rules)."""
+    if quant_format != "hif4":
+        raise NotImplementedError(f"faquant_b200 implements quant_format='hif4' only, got {quant_format!r}")
+    if bits != 4:
+        raise ValueError("HiF4 requires bits=4")
+    if group_size not in (-1, HIF4_BLOCK_SIZE):
+        raise ValueError("HiF4 requires group_size=64 (or -1 for direct use)")
+    if not symmetric:
+        raise ValueError("HiF4 does not support asymmetric quantization")
+    if clip_ratio != 1.0:
+        raise ValueError("HiF4 direct-cast does not support clipping")
+    qdq, _, _ = ops.hif4_quantize(x, levels=hif4_levels or ops.default_levels("act"))
+    return qdq
+
+
+def _quantize_weight_on_device(weight: torch.Tensor, levels: str) -> torch.Tensor:
+    """RTN HiF4 of a weight (``quantization.py:174-184``), computed on a CUDA device."""
+    source = weight.detach()
+    device = source.device if source.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    qdq, _, _ = ops.hif4_quantize(source.to(device), levels=levels)
+    return qdq.to(device=weight.device, dtype=weight.dtype)
+
+
+class FakeQuantLinear(nn.Module):
+    """Linear layer with dynamic HiF4 input and HiF4-grid weights, on tcgen05."""
+
+    faquant_quantizes_input = True
+
+    def __init__(
+        self,
+        linear: nn.Linear,
+        *,
+        quant_format: str = "int",
+        bits: int,
+        weight_group_size: int,
+        activation_group_size: int,
+        symmetric: bool,
+        clip_ratio: float,
+        quantize_weight: bool = True,
+        online_hadamard: bool = False,
+        online_hadamard_block_size: int | None = None,
+        input_scale: torch.Tensor | None = None,
+        input_rotation_signs: torch.Tensor | None = None,
+        input_rotation_permutation: torch.Tensor | None = None,
+        input_rotation_block_size: int | None = None,
+        weight_override: torch.Tensor | None = None,
+        activation_min: float | None = None,
+        activation_max: float | None = None,
+        activation_compand_log_scale: torch.Tensor | None = None,
+    ) -> None:
+        super().__init__()
+        if quant_format != "hif4":
+            raise NotImplementedError(f"faquant_b200 implements quant_format='hif4' only, got {quant_format!r}")
+        if bits != 4 or weight_group_size not in (-1, 64) or activation_group_size not in (-1, 64):
+            raise ValueError("HiF4 requires bits=4 and group_size=64")
+        if not symmetric or clip_ratio != 1.0:
+            raise ValueError("HiF4 is symmetric and does not support clipping")
+        self.in_features = linear.in_features
+        self.out_features = linear.out_features
+        self.quant_format = quant_format
+        self.bits = bits
+        self.activation_group_size = activation_group_size
+        self.symmetric = symmetric
+        self.clip_ratio = clip_ratio
+        self.online_hadamard = online_hadamard
+        self.online_hadamard_block_size = online_hadamard_block_size
+        self.register_buffer("input_scale", None if input_scale is None else input_scale.detach().float().clone())
+        self.register_buffer(
+            "input_rotation_signs",
+            None if input_rotation_signs is None else input_rotation_signs.detach().to(torch.int8).clone(),
+        )
+        self.register_buffer(
+            "input_rotation_permutation",
+            None if input_rotation_permutation is None else input_rotation_permutation.detach().long().clone(),
+        )
+        self.input_rotation_block_size = input_rotation_block_size
+        self.register_buffer(
+            "activation_min", None if activation_min is None else torch.as_tensor(activation_min).detach().float().clone()
+        )
+        self.register_buffer(
+            "activation_max", None if activation_max is None else torch.as_tensor(activation_max).detach().float().clone()
+        )
+        self.register_buffer(
+            "activation_compand_log_scale",
+            None if activation_compand_log_scale is None else activation_compand_log_scale.detach().float().clone(),
+        )
+        weight = linear.weight.detach() if weight_override is None else weight_override.detach()
+        if quantize_weight:
+            weight = _quantize_weight_on_device(weight, ops.default_levels("weight"))
+        weight = weight.to(dtype=linear.weight.dtype)
+        with torch.inference_mode(False):
+            weight = weight.detach().clone()
+        self.weight = nn.Parameter(weight, requires_grad=False)
+        if linear.bias is None:
+            self.register_parameter("bias", None)
+        else:
+            with torch.inference_mode(False):
+                self.bias = nn.Parameter(linear.bias.detach().clone(), requires_grad=False)
+        self._gemm_weight: torch.Tensor | None = None
+
+    def _rotation(self) -> tuple[torch.Tensor | None, torch.Tensor | None, int]:
+        if self.activation_min is not None or self.activation_max is not None:
+            raise NotImplementedError("activation clamping (QAD) is not implemented by faquant_b200")
+        if self.activation_compand_log_scale is not None:
+            raise NotImplementedError("activation companding (QAD) is not implemented by faquant_b200")
+        if self.input_rotation_signs is not None:
+            if self.online_hadamard:
+                raise NotImplementedError("an input rotation followed by an online Hadamard is not implemented")
+            block = self.input_rotation_block_size
+            return self.input_rotation_signs, self.input_rotation_permutation, 0 if block is None else int(block)
+        if self.online_hadamard:
+            block = self.online_hadamard_block_size or self.in_features
+            if not _is_pow2(block):
+                raise NotImplementedError("the 12*2^n generalized Hadamard is not implemented; use a power of two")
+            ones = torch.ones(self.in_features, dtype=torch.int8, device=self.weight.device)
+            return ones, None, int(block)
+        return None, None, 0
+
+    def _operand_weight(self) -> torch.Tensor:
+        w = self.weight
+        if w.dtype == torch.bfloat16:
+            return w
+        cached = self._gemm_weight
+        if cached is None or cached.device != w.device or cached.shape != w.shape:
+            # HiF4 values are exact in bf16 (<= 6 significant bits)
+            cached = w.detach().to(torch.bfloat16)
+            self._gemm_weight = cached
+        return cached
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError("faquant_b200.FakeQuantLinear runs on CUDA tensors only")
+        signs, perm, block = self._rotation()
+        shape = x.shape
+        qdq, _, _ = ops.hif4_quantize(
+            x.reshape(-1, shape[-1]),
+            levels=ops.default_levels("act"),
+            input_scale=self.input_scale,
+            signs=signs,
+            permutation=perm,
+            rot_block=block,
+        )
+        a = qdq if qdq.dtype == torch.bfloat16 else qdq.to(torch.bfloat16)  # exact
+        y = ops.gemm_bf16(a, self._operand_weight(), self.bias)
+        y = y.reshape(*shape[:-1], self.out_features)
+        return y if y.dtype == x.dtype else y.to(x.dtype)
+
+
+def replace_linear_with_fake_quant(parent: nn.Module, name: str, config: object, *, weights_prequantized: bool) -> None:
+    """Swap ``parent.<name>`` for a ``FakeQuantLinear`` reading its ``faquant_*`` attributes."""
+    linear = getattr(parent, name)
+    if isinstance(linear, FakeQuantLinear):
+        return
+    online_hadamard = bool(getattr(linear, "faquant_online_hadamard", False))
+    online_hadamard_block_size = getattr(linear, "faquant_online_hadamard_block_size", None)
+    if online_hadamard:
+        linear = linear.module
+    if not isinstance(linear, nn.Linear):
+        raise TypeError(f"{parent.__class__.__name__}.{name} is not nn.Linear")
+    weight_override = getattr(linear, "faquant_weight_override", None)
+    replacement = FakeQuantLinear(
+        linear,
+        quant_format=config.quant_format,
+        bits=config.bits,
+        weight_group_size=config.weight_group_size,
+        activation_group_size=config.activation_group_size,
+        symmetric=config.symmetric,
+        clip_ratio=config.clip_ratio,
+        quantize_weight=not weights_prequantized,
+        online_hadamard=online_hadamard,
+        online_hadamard_block_size=online_hadamard_block_size,
+        input_scale=getattr(linear, "faquant_input_scale", None),
+        input_rotation_signs=getattr(linear, "faquant_input_rotation_signs", None),
+        input_rotation_permutation=getattr(linear, "faquant_input_rotation_permutation", None),
+        input_rotation_block_size=getattr(linear, "faquant_input_rotation_block_size", None),
+        weight_override=None if weights_prequantized else weight_override,
+        activation_min=getattr(linear, "faquant_activation_min", None),
+        activation_max=getattr(linear, "faquant_activation_max", None),
+        activation_compand_log_scale=getattr(linear, "faquant_activation_compand_log_scale", None),
+    )
+    for attr in ("faquant_hif4_qat_parameters", "faquant_hif4_qat_master"):
+        value = getattr(linear, attr, None)
+        if value is not None:
+            setattr(replacement, attr, value)
+    setattr(parent, name, replacement)
+
+
+@torch.inference_mode()
+def quantize_qwen3_linears(model: nn.Module, config: object, *, weights_prequantized: bool = False,
+                           exempt: frozenset[tuple[int, str]] = frozenset()) -> None:
+    """Install HiF4 W4A4 on the Qwen3 projections (``quantization.py:378-408``)."""
+    target = config.quant_target
+    if target == "none":
+        return
+    for index, layer in enumerate(model.model.layers):
+        if target in ("attention", "all"):
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                if (index, name) not in exempt:
+                    replace_linear_with_fake_quant(layer.self_attn, name, config, weights_prequantized=weights_prequantized)
+        if target in ("ffn", "all"):
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                if (index, name) not in exempt:
+                    replace_linear_with_fake_quant(layer.mlp, name, config, weights_prequantized=weights_prequantized)

@@ -1,0 +1,166 @@
+/*
+ * faquant_b200.h -- C ABI of libfaquant_b200.so, the B200 (sm_100a) kernels behind
+ * FAQUANT's two HiF4 hot paths: the W4A4 quantized Linear and the HiF4 QK/PV
+ * flash attention.
+ *
+ * Conventions (every entry point):
+ *  - returns FAQ_OK (0) or a FAQ_ERR_* code; faq_last_error() gives the message
+ *    of the calling thread's last failure;
+ *  - all pointers are device pointers unless stated, sizes and strides are in
+ *    ELEMENTS, the innermost dimension is contiguous;
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream); work is
+ *    stream-ordered, the calls are thread-safe across streams and never
+ *    synchronize the device;
+ *  - the library allocates no device memory: every output is caller-owned;
+ *  - arguments are validated on the host; a device-side wait that exceeds its
+ *    time limit records FAQ_STATUS_TIMEOUT in a status word read by
+ *    faq_device_status() (kernels never trap).
+ *
+ * Packed HiF4 storage format (this project's own; the reference stores only
+ * bf16 dequantized values plus fp32/int8 metadata, qad_checkpoint.py:43-48):
+ *  - codes: uint8 [rows, K64/2], K64 = K rounded up to 64. Value 2i is the low
+ *    nibble and value 2i+1 the high nibble of byte i; nibble = sign<<3 | m with
+ *    sign = (x < 0) and m in 0..7 the element magnitude in quarters;
+ *  - meta:  uint32 [rows, K64/64], one word per 64-value block:
+ *      bits  0-7 : E6M2 scale code, (e + 48) << 2 | t, scale = (1 + t/4) * 2^e;
+ *      bits  8-15: lv2 exponent bit of each 8-value sub-block;
+ *      bits 16-31: lv3 exponent bit of each 4-value sub-block;
+ *  - value = (-1)^sign * (m / 4) * scale * 2^(lv2 + lv3).
+ */
+#ifndef FAQUANT_B200_H_
+#define FAQUANT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FAQ_OK 0
+#define FAQ_ERR_ARG 1         /* invalid argument (shape, stride, alignment, null) */
+#define FAQ_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define FAQ_ERR_UNSUPPORTED 3 /* valid for the reference, not supported by these kernels */
+#define FAQ_ERR_TIMEOUT 4     /* a device-side wait ran out (see faq_device_status) */
+
+/* device status word bits */
+#define FAQ_STATUS_TIMEOUT 1u
+
+/* element types */
+#define FAQ_BF16 0
+#define FAQ_F32 1
+
+/* HiF4 scale-level variants (src/faquant/hif4.py:13-43) */
+#define FAQ_LEVELS_123 123
+#define FAQ_LEVELS_12 12
+#define FAQ_LEVELS_13 13
+
+/* Version of the library as major*10000 + minor*100 + patch. */
+int faq_version(void);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated). */
+int faq_last_error(char* buf, size_t len);
+
+/* Read the device status word of the current device into *status; clear it
+ * when `reset` is non-zero. Synchronizes with the legacy default stream. */
+int faq_device_status(unsigned int* status, int reset);
+
+/*
+ * K1 -- activation rotation + HiF4 quantization, rows of x [rows, k] (row stride ldx).
+ *
+ * Replaces the input path of FakeQuantLinear.forward (src/faquant/quantization.py:200-221
+ * and :267-274): optional per-channel input_scale multiplied in x's dtype
+ * (:200-201); when `signs` is given, x*signs in fp32 (int8 [k]), a gather by
+ * `perm` (int64 [k], NULL = identity), an fp32 Walsh-Hadamard over consecutive
+ * blocks of `rot_block` (a power of two 1..1024 dividing k; 0 = no Hadamard)
+ * normalized by 1/sqrt(rot_block) (rotation.py:14-29, 117-135) and one rounding
+ * to x's dtype; then HiF4 quantization along k in blocks of 64 with a
+ * zero-padded tail (hif4.py:376-390), `levels` in {123, 12, 13}.
+ * Outputs (any may be NULL, not all): packed `codes`/`meta` (format above) and
+ * the dequantized values `qdq` [rows, ldq] in x's dtype (bit-exact with the
+ * reference's fake_quantize output).
+ */
+int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
+                      const void* input_scale, const int8_t* signs, const int64_t* perm,
+                      int rot_block, int levels, uint8_t* codes, uint32_t* meta, void* qdq,
+                      int64_t ldq, void* stream);
+
+/* Dequantize packed HiF4 rows back to out [rows, ldo] (bf16 or fp32).
+ * The inverse of the packing above; replaces expand_hif4_parameters +
+ * quantize_hif4_with_parameters (hif4.py:222-271) for stored codes. */
+int faq_hif4_dequantize(const uint8_t* codes, const uint32_t* meta, int64_t rows, int64_t k,
+                        void* out, int out_dtype, int64_t ldo, void* stream);
+
+/*
+ * K2 -- pack HiF4-grid weights w [n, k] (bf16 or fp32, row stride ldw) into codes/meta.
+ * With `scale` (fp32 [n, k/64]), `lv2` (int8 [n, k/64, 8]) and `lv3` (int8 [n, k/64, 16])
+ * -- the compact metadata GPTQ records (gptq.py:411-423, 562-570) -- codes are
+ * round(|w| / dequant_scale * 4) clamped to 0..7 (hif4.py:311). Without them the
+ * metadata is fitted from w as the RTN quantizer does (FakeQuantLinear.__init__,
+ * quantization.py:169-184). Every value that the packed form does not reproduce
+ * exactly increments *mismatches (device int64, caller-zeroed; may be NULL).
+ */
+int faq_hif4_pack_weight(const void* w, int w_dtype, int64_t n, int64_t k, int64_t ldw,
+                         const float* scale, const int8_t* lv2, const int8_t* lv3, int levels,
+                         uint8_t* codes, uint32_t* meta, unsigned long long* mismatches,
+                         void* stream);
+
+/*
+ * K3 -- y [m, n] = a [m, k] . b [n, k]^T (+ bias [n]); bf16 operands and output,
+ * fp32 accumulation on tcgen05 tensor cores (TMEM accumulators, TMA loads).
+ * Replaces F.linear(x_qdq, weight, bias) (quantization.py:277, wan22_hif4.py:88)
+ * on exactly-dequantized HiF4 operands. Needs lda, ldb multiples of 8, 16-byte
+ * aligned a/b and k a multiple of 8.
+ */
+int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
+                     int64_t n, int64_t k, const void* bias, void* y, int64_t ldy, void* stream);
+
+/*
+ * K4 -- attention operand preparation for one of Q, K or V.
+ * x is [batch, heads, seq, d] with element strides (sb, sh, ss) and d contiguous,
+ * bf16 or fp32. Replaces the post-RoPE block of qwen3._attention_forward
+ * (src/faquant/qwen3.py:101-130), Wan's self_forward/rotate_heads
+ * (wan22_attention.py:186-192, 257-259) and the operand QDQ of the simulator
+ * (simulated_flash_attention.py:588-619): in fp32, x - offset (fp32 [heads, d],
+ * K only), then x * smooth (smooth_mode 1, Q) or x / smooth (smooth_mode 2, K)
+ * with smooth fp32 [d] (smooth_head_stride 0) or [heads, d]; a normalized
+ * Hadamard over d when `rotate` (d a power of two <= 128); one rounding to bf16;
+ * then, when `levels` != 0, HiF4 quantization along d. Output bf16 with strides
+ * (ob, oh, os); optional packed codes/meta for the rows in (b, h, s) order.
+ */
+int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d,
+                int64_t sb, int64_t sh, int64_t ss, const float* offset, const float* smooth,
+                int64_t smooth_head_stride, int smooth_mode, int rotate, int levels, void* out,
+                int64_t ob, int64_t oh, int64_t os, uint8_t* codes, uint32_t* meta, void* stream);
+
+/*
+ * K5 -- HiF4 QK/PV flash attention on pre-quantized bf16 operands (output of K4).
+ * q [batch, hq, sq, 128], k/v [batch, hkv, sk, 128] with element strides, d contiguous;
+ * out [batch, sq, hq, 128] bf16 with element strides (ob, os, oh).
+ * Replaces simulated_flash_attention_forward (simulated_flash_attention.py:457-909,
+ * no mask) and Wan's hif4_attention (wan22_attention.py:165-183): scores
+ * q.k^T * scale in fp32, bottom-right causal mask when `causal`, online softmax
+ * over key tiles of 128 against the running max, HiF4 quantization of
+ * P = exp(s - max) along each tile's keys in groups of 64 (`p_levels`, 0 = no P
+ * quantization), the denominator from the quantized P when
+ * `normalizer_quantized` (P-Reordering) else from the unquantized P, fp32 PV
+ * accumulation, out = acc / denominator. GQA maps q head h to kv head
+ * h / (hq / hkv) (simulated_flash_attention.py:231-240).
+ */
+int faq_hif4_attention(const void* q, const void* k, const void* v, int64_t batch, int64_t hq,
+                       int64_t hkv, int64_t sq, int64_t sk, int d, int64_t qb, int64_t qh,
+                       int64_t qs, int64_t kb, int64_t kh, int64_t ks, int64_t vb, int64_t vh,
+                       int64_t vs, float scale, int causal, int p_levels, int normalizer_quantized,
+                       void* out, int64_t ob, int64_t os, int64_t oh, void* stream);
+
+/* Diagnostics: launch one CTA that waits on an mbarrier nothing arrives at, for
+ * at most `limit_ns` nanoseconds, then records FAQ_STATUS_TIMEOUT and returns.
+ * Exercises the bounded-wait path of the kernels without faulting the GPU. */
+int faq_selftest_wait_timeout(int64_t limit_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAQUANT_B200_H_ */

@@ -1,0 +1,163 @@
+"""GPU parity of K3 (tcgen05 GEMM), K4 (Q/K/V preparation) and K5 (HiF4 attention).
+
+Tolerances:
+- GEMM: the kernel rounds an fp32 accumulation to bf16, so against the exact
+  (fp64) product of the HiF4 operands each element is within half a bf16 ulp plus
+  fp32 accumulation-order error: |y - ref| <= 2^-8 |ref| + 1e-4 * max|ref|.
+- Attention: P = exp(s - max) uses the hardware ex2 where the reference uses CPU
+  exp, so P differs by ulps and a P value can cross a HiF4 rounding boundary;
+  outputs must agree within ATT_REL_FRO (relative Frobenius) and ATT_MAX_ABS.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from inputs import ATTENTION_CASES, attention_inputs, sha
+from oracle import attention as oatt
+from oracle import hif4 as oh
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ATT_REL_FRO = 5e-3
+ATT_MAX_ABS = 6e-2
+
+
+def _ops():
+    from faquant_b200 import ops
+
+    return ops
+
+
+def _hif4_operand(rows: int, cols: int, seed: int, scale: float = 1.0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, cols, generator=g) * scale
+    return torch.from_numpy(oh.fake_quantize(x.numpy())).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,n,k,bias", [(128, 256, 64, False), (300, 520, 200, True), (1000, 1000, 1024, True),
+                                        (2048, 4096, 4096, False), (64, 48, 256, True), (1, 8, 64, False)])
+def test_gemm_matches_fp64(m: int, n: int, k: int, bias: bool) -> None:
+    ops = _ops()
+    a = _hif4_operand(m, k, 1).to(DEV)
+    b = _hif4_operand(n, k, 2, 0.02).to(DEV)
+    bvec = (torch.randn(n, generator=torch.Generator().manual_seed(3)) * 0.1).to(torch.bfloat16).to(DEV) if bias else None
+    y = ops.gemm_bf16(a, b, bvec)
+    ref = a.double() @ b.double().T
+    if bvec is not None:
+        ref = ref + bvec.double()
+    err = (y.double() - ref).abs()
+    bound = 2.0**-8 * ref.abs() + 1e-4 * ref.abs().max()
+    assert bool((err <= bound).all()), float((err - bound).max())
+
+
+def test_gemm_strided_and_tail_k() -> None:
+    ops = _ops()
+    a_full = _hif4_operand(200, 136, 4).to(DEV)
+    a = a_full[:, :128]  # lda 136
+    b = _hif4_operand(72, 128, 5).to(DEV)
+    y = ops.gemm_bf16(a, b)
+    ref = a.double() @ b.double().T
+    assert torch.allclose(y.double(), ref, rtol=2**-8, atol=1e-3)
+    a2 = _hif4_operand(33, 100, 6).to(DEV)  # k % 8 != 0 -> zero padded
+    b2 = _hif4_operand(40, 100, 7).to(DEV)
+    y2 = ops.gemm_bf16(a2, b2)
+    assert torch.allclose(y2.double(), a2.double() @ b2.double().T, rtol=2**-8, atol=1e-3)
+
+
+def test_qk_prep_matches_reference_fixture() -> None:
+    ops = _ops()
+    g = load_golden("qk_prep")
+    q = torch.from_numpy(g["q"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    k = torch.from_numpy(g["k"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    scale = torch.from_numpy(g["scale"]).to(DEV)
+    offset = torch.from_numpy(g["offset"]).to(DEV)
+    qo, _, _ = ops.qk_prep(q, levels=None, rotate=True, smooth_scale=scale, smooth_mode="mul")
+    ko, _, _ = ops.qk_prep(k, levels=None, rotate=True, smooth_scale=scale, smooth_mode="div", key_offset=offset)
+    assert np.array_equal(qo.cpu().view(torch.int16).numpy().view(np.uint16), g["q_out"])
+    assert np.array_equal(ko.cpu().view(torch.int16).numpy().view(np.uint16), g["k_out"])
+    # with HiF4 along head_dim: equals the oracle's QDQ of the transformed operand, codes too
+    qq, codes, meta = ops.qk_prep(q, levels="123", rotate=True, smooth_scale=scale, smooth_mode="mul",
+                                  want_codes=True)
+    expect = oh.fake_quantize(oh.bf16_to_f32(g["q_out"]), "123")
+    assert np.array_equal(qq.cpu().view(torch.int16).numpy().view(np.uint16), oh.f32_to_bf16_bits(expect))
+    oc, om = oh.hif4_encode(oh.bf16_to_f32(g["q_out"]).reshape(-1, 128), "123")
+    assert np.array_equal(codes.cpu().numpy(), oc)
+    assert np.array_equal(meta.cpu().numpy().view(np.uint32), om)
+
+
+def test_qk_prep_strided_fp32_input_and_per_head_scale() -> None:
+    ops = _ops()
+    rng = np.random.default_rng(9)
+    x = torch.from_numpy(rng.standard_normal((2, 50, 3, 128)).astype(np.float32)).to(DEV).transpose(1, 2)  # [B,H,S,D]
+    s = torch.from_numpy(rng.uniform(0.5, 2, (3, 128)).astype(np.float32)).to(DEV)
+    out, _, _ = ops.qk_prep(x, levels="13", rotate=True, smooth_scale=s, smooth_mode="div")
+    xt = x.cpu().numpy()
+    qf = (xt / s.cpu().numpy()[None, :, None, :]).astype(np.float32)
+    from oracle.rotation import hadamard
+
+    expect = oh.fake_quantize(oh.bf16_round(hadamard(qf)), "13")
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), oh.f32_to_bf16_bits(expect))
+
+
+def _attention_gpu(q, k, v, *, causal, normalizer, qk_quant, pv_quant, levels="123"):
+    ops = _ops()
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    if qk_quant:
+        qd, _, _ = ops.qk_prep(qd, levels=levels, rotate=False)
+        kd, _, _ = ops.qk_prep(kd, levels=levels, rotate=False)
+    if pv_quant:
+        vd, _, _ = ops.qk_prep(vd, levels=levels, rotate=False)
+    return ops.hif4_attention(qd, kd, vd, causal=causal, p_levels=levels if pv_quant else None,
+                              quantized_normalizer=normalizer == "quantized_same")
+
+
+def _check_close(out: torch.Tensor, ref: np.ndarray) -> tuple[float, float]:
+    o = out.float().cpu().numpy()
+    err = o - ref
+    rel = float(np.linalg.norm(err) / max(np.linalg.norm(ref), 1e-30))
+    mx = float(np.abs(err).max())
+    assert rel <= ATT_REL_FRO and mx <= ATT_MAX_ABS, (rel, mx)
+    return rel, mx
+
+
+@pytest.mark.parametrize("case", ATTENTION_CASES, ids=[c[0] for c in ATTENTION_CASES])
+def test_attention_matches_reference_fixture(case) -> None:
+    g = load_golden("attention")
+    tag, b, h, kv, sq, sk, causal, normalizer, qk, pv, seed = case
+    q, k, v = attention_inputs(b, h, kv, sq, sk, seed)
+    assert str(g[f"{tag}_in_sha"]) == sha(q) + sha(k) + sha(v)
+    out = _attention_gpu(q, k, v, causal=causal, normalizer=normalizer, qk_quant=qk, pv_quant=pv)
+    _check_close(out, oh.bf16_to_f32(g[f"{tag}_out"]))
+
+
+@pytest.mark.parametrize("causal,normalizer,levels", [(True, "quantized_same", "123"), (False, "unquantized", "123"),
+                                                      (True, "unquantized", "12")])
+def test_attention_matches_oracle_mid_size(causal: bool, normalizer: str, levels: str) -> None:
+    q, k, v = attention_inputs(1, 8, 2, 1000, 1000, 77)
+    out = _attention_gpu(q, k, v, causal=causal, normalizer=normalizer, qk_quant=True, pv_quant=True, levels=levels)
+    ref = oatt.attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), causal=causal,
+                         normalizer=normalizer, levels={"q": levels, "k": levels, "p": levels, "v": levels})
+    _check_close(out, ref)
+
+
+def test_attention_unit_values_are_exactly_one_under_p_reordering() -> None:
+    # simulated_flash_attention tests :653-688: V = 1 and P-Reordering give exactly 1
+    q, k, _ = attention_inputs(1, 4, 2, 300, 300, 88)
+    v = torch.ones(1, 2, 300, 128, dtype=torch.bfloat16)
+    out = _attention_gpu(q, k, v, causal=True, normalizer="quantized_same", qk_quant=True, pv_quant=True)
+    assert torch.equal(out.float().cpu(), torch.ones(1, 300, 4, 128))
+
+
+def test_bounded_wait_reports_timeout_status() -> None:
+    from faquant_b200 import _lib
+
+    ops = _ops()
+    _lib.device_status(reset=True)
+    ops.selftest_wait_timeout(50_000_000)  # 50 ms on an mbarrier nothing arrives at
+    torch.cuda.synchronize()
+    assert _lib.device_status(reset=True) & _lib.FAQ_STATUS_TIMEOUT
+    assert _lib.device_status() == 0
