@@ -175,12 +175,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait(smem_addr(&k_empty[st]), ph)) { ok = false; break; }
+        if (!mbar_wait_site(smem_addr(&k_empty[st]), ph, 1, j)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_addr(&k_full[st]), TILE_BYTES);
         for (int c = 0; c < 2; ++c)
           tma_load_4d(smem_addr(base + OFF_K + st * TILE_BYTES + c * CHUNK_BYTES), &tmap_k, smem_addr(&k_full[st]),
                       c * 64, j * BN, hk, b);
-        if (!mbar_wait(smem_addr(&v_empty[st]), ph)) { ok = false; break; }
+        if (!mbar_wait_site(smem_addr(&v_empty[st]), ph, 2, j)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_addr(&v_full[st]), TILE_BYTES);
         for (int c = 0; c < 2; ++c)
           tma_load_4d(smem_addr(base + OFF_V + st * TILE_BYTES + c * CHUNK_BYTES), &tmap_v, smem_addr(&v_full[st]),
@@ -191,8 +191,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = std::max(0, n_tiles - 2); j < n_tiles; ++j) {
           const int st = j & 1;
           const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait(smem_addr(&k_empty[st]), ph)) break;
-          if (!mbar_wait(smem_addr(&v_empty[st]), ph)) break;
+          if (!mbar_wait_site(smem_addr(&k_empty[st]), ph, 3, j)) break;
+          if (!mbar_wait_site(smem_addr(&v_empty[st]), ph, 3, j)) break;
         }
       }
     }
@@ -200,13 +200,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
-      bool ok = mbar_wait(smem_addr(q_full), 0);
+      bool ok = mbar_wait_site(smem_addr(q_full), 0, 4, 0);
       const uint32_t q_base = smem_addr(base + OFF_Q);
       auto issue_qk = [&](int j) -> bool {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(smem_addr(&k_full[st]), ph)) return false;
-        if (!mbar_wait(smem_addr(&s_empty[st]), ph ^ 1)) return false;
+        if (!mbar_wait_site(smem_addr(&k_full[st]), ph, 5, j)) return false;
+        if (!mbar_wait_site(smem_addr(&s_empty[st]), ph ^ 1, 6, j)) return false;
         tc_fence_after();
         const uint32_t k_base = smem_addr(base + OFF_K + st * TILE_BYTES);
         const uint32_t d_tmem = tmem + S_COL0 + st * BN;
@@ -223,8 +223,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = 0; j < n_tiles && ok; ++j) {
         if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
         const int st = j & 1;
-        if (!mbar_wait(smem_addr(p_full), j & 1)) break;
-        if (!mbar_wait(smem_addr(&v_full[st]), (j >> 1) & 1)) break;
+        if (!mbar_wait_site(smem_addr(p_full), j & 1, 7, j)) break;
+        if (!mbar_wait_site(smem_addr(&v_full[st]), (j >> 1) & 1, 8, j)) break;
         tc_fence_after();
         const uint32_t p_base = smem_addr(base + OFF_P);
         const uint32_t v_base = smem_addr(base + OFF_V + st * TILE_BYTES);
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      if (!mbar_wait(smem_addr(&s_full[st]), (j >> 1) & 1)) { ok = false; break; }
+      if (!mbar_wait_warp(smem_addr(&s_full[st]), (j >> 1) & 1, 9, j)) { ok = false; break; }
       tc_fence_after();
       float s[BN];
       {
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       m_run = m_new;
       // P and O may be touched only after PV of the previous tile finished
       if (j > 0) {
-        if (!mbar_wait(smem_addr(o_done), (j - 1) & 1)) { ok = false; break; }
+        if (!mbar_wait_warp(smem_addr(o_done), (j - 1) & 1, 10, j)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
@@ -346,28 +346,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(p_full));
     }
-    if (ok && n_tiles > 0 && mbar_wait(smem_addr(o_done), (n_tiles - 1) & 1)) {
+    if (ok && n_tiles > 0 && mbar_wait_warp(smem_addr(o_done), (n_tiles - 1) & 1, 11, n_tiles)) {
       tc_fence_after();
-      if (qpos < p.sq) {
-        __nv_bfloat16* dst = p.out + b * p.ob + qpos * p.os + static_cast<int64_t>(h) * p.oh;
-        const float inv_ok = l_run > 0.0f ? 1.0f : 0.0f;
+      // tcgen05.ld is .sync.aligned: every lane of the warp loads, even the lanes of
+      // query rows past the end (a tile can end mid-warp); only the stores are predicated.
+      const bool store = qpos < p.sq;
+      __nv_bfloat16* dst = p.out + b * p.ob + (store ? qpos : 0) * p.os + static_cast<int64_t>(h) * p.oh;
+      const bool has_mass = l_run > 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_addr + O_COL + c * 32, r);
-          tc_wait_ld();
-          reg_fence32(r);
-          float o[32];
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_addr + O_COL + c * 32, r);
+        tc_wait_ld();
+        reg_fence32(r);
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(r[i]);
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float a0 = inv_ok != 0.0f ? __fdiv_rn(o[2 * i], l_run) : 0.0f;
-            const float a1 = inv_ok != 0.0f ? __fdiv_rn(o[2 * i + 1], l_run) : 0.0f;
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
-            w[i] = *reinterpret_cast<const uint32_t*>(&pr);
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float a0 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i]), l_run) : 0.0f;
+          const float a1 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i + 1]), l_run) : 0.0f;
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+          w[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        if (store) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);

@@ -46,7 +46,22 @@ int num_sms();
 // defines it exactly once.
 __device__ unsigned int g_status = 0;
 
+// Where waits gave up: up to kTraceSlots records of (site | tile << 8, block x | block y << 16, block z),
+// read by faq_device_trace(). Written only on a timeout.
+constexpr int kTraceSlots = 32;
+__device__ unsigned int g_trace_count = 0;
+__device__ unsigned int g_trace[kTraceSlots * 3];
+
 __device__ __forceinline__ void report_timeout() { atomicOr(&g_status, FAQ_STATUS_TIMEOUT); }
+
+__device__ __forceinline__ void trace_timeout(int site, int tile) {
+  const unsigned int slot = atomicAdd(&g_trace_count, 1u);
+  if (slot < kTraceSlots) {
+    g_trace[slot * 3 + 0] = static_cast<unsigned int>(site) | (static_cast<unsigned int>(tile) << 8);
+    g_trace[slot * 3 + 1] = blockIdx.x | (blockIdx.y << 16);
+    g_trace[slot * 3 + 2] = blockIdx.z;
+  }
+}
 
 // Default wait limit of the kernels' spin loops: 2 s of %globaltimer.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
@@ -114,6 +129,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
       return false;
     }
   }
+}
+
+// Bounded wait for a barrier that a whole warp waits on together. Every lane polls
+// (bounded), then the lanes agree: the result is warp-uniform, so a timeout can
+// never leave part of the warp inside a loop of .sync.aligned instructions.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int site = 0, int tile = 0,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, parity, limit_ns));
+  if (!ok && (threadIdx.x & 31) == 0) trace_timeout(site, tile);
+  return ok;
+}
+// Single-lane variant that records the site on a timeout.
+__device__ __forceinline__ bool mbar_wait_site(uint32_t bar, uint32_t parity, int site, int tile) {
+  const bool ok = mbar_wait(bar, parity);
+  if (!ok) trace_timeout(site, tile);
+  return ok;
 }
 
 // ---------------------------------------------------------------- TMA

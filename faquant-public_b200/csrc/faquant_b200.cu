@@ -119,6 +119,19 @@ extern "C" int faq_device_status(unsigned int* status, int reset) {
   return FAQ_OK;
 }
 
+extern "C" int faq_device_trace(unsigned int* records, int max_records, int reset) {
+  FAQ_CHECK_ARG(records != nullptr && max_records >= 0, "bad arguments");
+  unsigned int count = 0;
+  FAQ_CUDA(cudaMemcpyFromSymbol(&count, faq::g_trace_count, sizeof(count)));
+  const int n = static_cast<int>(std::min<unsigned int>(count, std::min<unsigned int>(max_records, faq::kTraceSlots)));
+  if (n > 0) FAQ_CUDA(cudaMemcpyFromSymbol(records, faq::g_trace, sizeof(unsigned int) * 3 * n));
+  if (reset) {
+    const unsigned int zero = 0;
+    FAQ_CUDA(cudaMemcpyToSymbol(faq::g_trace_count, &zero, sizeof(zero)));
+  }
+  return static_cast<int>(count);
+}
+
 extern "C" int faq_selftest_wait_timeout(int64_t limit_ns, void* stream) {
   FAQ_CHECK_ARG(limit_ns > 0 && limit_ns <= 5000000000ll, "limit_ns must be in (0, 5 s]");
   faq::selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(limit_ns));

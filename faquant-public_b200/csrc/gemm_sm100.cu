@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) { ok = false; break; }
+          if (!mbar_wait_site(smem_addr(&empty[stage]), phase ^ 1, 21, kb)) { ok = false; break; }
           mbar_arrive_expect_tx(smem_addr(&full[stage]), STAGE_BYTES);
           tma_load_2d(smem_addr(sA + stage * A_BYTES), &tmap_a, smem_addr(&full[stage]), kb * BK, tm * BM);
           tma_load_2d(smem_addr(sB + stage * B_BYTES), &tmap_b, smem_addr(&full[stage]), kb * BK, tn * BN);
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // drain: wait (bounded) until the tensor cores released every loaded stage
       for (int s = 0; s < STAGES && ok; ++s) {
-        if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) break;
+        if (!mbar_wait_site(smem_addr(&empty[stage]), phase ^ 1, 22, s)) break;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
@@ -139,11 +139,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
-        if (!mbar_wait(smem_addr(&tempty[acc]), acc_phase ^ 1)) break;
+        if (!mbar_wait_site(smem_addr(&tempty[acc]), acc_phase ^ 1, 23, it)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!mbar_wait(smem_addr(&full[stage]), phase)) { ok = false; break; }
+          if (!mbar_wait_site(smem_addr(&full[stage]), phase, 24, kb)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_addr(sA + stage * A_BYTES), b0 = smem_addr(sB + stage * B_BYTES);
 #pragma unroll
@@ -163,7 +163,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+      if (!mbar_wait_warp(smem_addr(&tfull[acc]), acc_phase, 25, it)) break;
       tc_fence_after();
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
       const int row = tm * BM + quarter * 32 + lane;

@@ -293,8 +293,11 @@ __global__ void __launch_bounds__(256) hif4_dequantize_kernel(const uint8_t* __r
 
 // ---------------------------------------------------------------- K2: pack weights
 // With GPTQ metadata: code = clamp(round(|w| / ds * 4), 0, 7) (hif4.py:311, torch.round
-// is half-to-even = rintf); without it, the RTN fit of the quantizer. Values the
-// packed form does not reproduce exactly are counted in *mismatches.
+// is half-to-even = rintf); without it, the RTN fit of the quantizer applied to w,
+// which must then be the SOURCE weight: RTN is not idempotent (a quantized block
+// has a smaller maximum and can fit another E6M2 scale), which is why the reference
+// fits weight metadata from the source (quantization.py:329-345). Values the packed
+// form does not reproduce exactly are counted in *mismatches.
 template <typename T>
 __global__ void __launch_bounds__(256) hif4_pack_kernel(const T* __restrict__ w, int64_t n, int64_t k, int64_t ldw,
                                                         const float* __restrict__ scale, const int8_t* __restrict__ lv2,
@@ -417,12 +420,12 @@ using namespace faq;
 extern "C" int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64_t ldx,
                                  const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block,
                                  int levels, uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
-  FAQ_CHECK_ARG(x != nullptr, "x is null");
   FAQ_CHECK_ARG(x_dtype == FAQ_BF16 || x_dtype == FAQ_F32, "x_dtype must be FAQ_BF16 or FAQ_F32");
   FAQ_CHECK_ARG(rows >= 0 && k > 0, "need rows >= 0 and k > 0 (HiF4 does not support an empty axis)");
+  FAQ_CHECK_ARG(x != nullptr || rows == 0, "x is null");
   FAQ_CHECK_ARG(ldx >= k, "ldx < k");
   FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
-  FAQ_CHECK_ARG(codes || meta || qdq, "all outputs are null");
+  FAQ_CHECK_ARG(codes || meta || qdq || rows == 0, "all outputs are null");
   FAQ_CHECK_ARG(qdq == nullptr || ldq >= k, "ldq < k");
   FAQ_CHECK_ARG(!codes || (reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
   FAQ_CHECK_ARG(!meta || (reinterpret_cast<uintptr_t>(meta) & 3) == 0, "meta must be 4-byte aligned");

@@ -40,6 +40,7 @@ SIGNATURES: dict[str, list] = {
                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _int,
                            _int, _c_void_p, _i64, _i64, _i64, _c_void_p],
     "faq_selftest_wait_timeout": [_i64, _c_void_p],
+    "faq_device_trace": [ctypes.POINTER(ctypes.c_uint), _int, _int],
 }
 
 _lock = threading.Lock()
@@ -86,6 +87,19 @@ def check(rc: int, what: str) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
+
+
+def device_trace(reset: bool = False) -> list[tuple[int, int, int, int, int]]:
+    """Records of the device waits that gave up: (site, tile, block x, block y, block z)."""
+    buf = (ctypes.c_uint * 96)()
+    n = load().faq_device_trace(buf, 32, int(reset))
+    if n < 0:
+        raise FaqError(f"faq_device_trace failed: {last_error()}")
+    out = []
+    for i in range(min(n, 32)):
+        w0, w1, w2 = buf[3 * i], buf[3 * i + 1], buf[3 * i + 2]
+        out.append((w0 & 0xFF, w0 >> 8, w1 & 0xFFFF, w1 >> 16, w2))
+    return out
 
 
 def device_status(reset: bool = False) -> int:

@@ -98,8 +98,11 @@ int faq_hif4_dequantize(const uint8_t* codes, const uint32_t* meta, int64_t rows
  * -- the compact metadata GPTQ records (gptq.py:411-423, 562-570) -- codes are
  * round(|w| / dequant_scale * 4) clamped to 0..7 (hif4.py:311). Without them the
  * metadata is fitted from w as the RTN quantizer does (FakeQuantLinear.__init__,
- * quantization.py:169-184). Every value that the packed form does not reproduce
- * exactly increments *mismatches (device int64, caller-zeroed; may be NULL).
+ * quantization.py:169-184), so w must be the source (unquantized) weight: RTN is
+ * not idempotent, re-fitting an already quantized block can pick another scale.
+ * Every value that the packed form does not reproduce exactly increments
+ * *mismatches (device int64, caller-zeroed; may be NULL): zero for an on-grid
+ * weight with its metadata, the number of changed values for an RTN source.
  */
 int faq_hif4_pack_weight(const void* w, int w_dtype, int64_t n, int64_t k, int64_t ldw,
                          const float* scale, const int8_t* lv2, const int8_t* lv3, int levels,
@@ -153,6 +156,12 @@ int faq_hif4_attention(const void* q, const void* k, const void* v, int64_t batc
                        int64_t qs, int64_t kb, int64_t kh, int64_t ks, int64_t vb, int64_t vh,
                        int64_t vs, float scale, int causal, int p_levels, int normalizer_quantized,
                        void* out, int64_t ob, int64_t os, int64_t oh, void* stream);
+
+/* Diagnostics: copy up to max_records records of the waits that gave up (3 words
+ * each: site | tile << 8, blockIdx.x | blockIdx.y << 16, blockIdx.z) into `records`
+ * (host memory); returns the number of timeouts recorded (>= 0) or -FAQ_ERR_*.
+ * Clears the record count when `reset` is non-zero. */
+int faq_device_trace(unsigned int* records, int max_records, int reset);
 
 /* Diagnostics: launch one CTA that waits on an mbarrier nothing arrives at, for
  * at most `limit_ns` nanoseconds, then records FAQ_STATUS_TIMEOUT and returns.

@@ -146,19 +146,22 @@ def test_input_scale_strided_rows_and_empty() -> None:
 def test_pack_rtn_and_gptq_weights() -> None:
     ops = _ops()
     g = load_golden("linear_123")
-    wq = torch.from_numpy(g["r64_wq"].view(np.int16)).view(torch.bfloat16).to(DEV)
-    codes, meta, bad = ops.hif4_pack_weight(wq, levels="123")
-    assert bad == 0
-    assert torch.equal(ops.hif4_dequantize(codes, meta, wq.shape[1]), wq)
-    # GPTQ weight with its recorded metadata (gptq.py:562-570)
+    tag, rows, fin, fout, block, seed, rname, rseed = LINEAR_CASES[0]
+    _, w_src, _ = linear_inputs(rows, fin, fout, seed)
+    wq = torch.from_numpy(g[f"{tag}_wq"].view(np.int16)).view(torch.bfloat16).to(DEV)
+    # RTN: pack from the source weight; the packed form decodes to the reference's RTN weight
+    codes, meta, changed = ops.hif4_pack_weight(w_src.to(DEV), levels="123")
+    assert torch.equal(ops.hif4_dequantize(codes, meta, fin), wq)
+    assert changed == int((w_src.to(DEV) != wq).sum())
+    # GPTQ weight with its recorded metadata (gptq.py:562-570): exact, nothing changed
     gp = load_golden("gptq")
     w = torch.from_numpy(gp["w"].view(np.int16)).view(torch.bfloat16).to(DEV)
-    codes, meta, bad = ops.hif4_pack_weight(w, scale=torch.from_numpy(gp["scale"]), lv2=torch.from_numpy(gp["lv2"]),
-                                            lv3=torch.from_numpy(gp["lv3"]))
+    scale, lv2, lv3 = (torch.from_numpy(gp[n]) for n in ("scale", "lv2", "lv3"))
+    codes, meta, bad = ops.hif4_pack_weight(w, scale=scale, lv2=lv2, lv3=lv3)
     assert bad == 0
     assert torch.equal(ops.hif4_dequantize(codes, meta, w.shape[1]), w)
-    # a weight off the grid is reported
-    off = wq.clone()
+    # a weight off its recorded grid is reported
+    off = w.clone()
     off[0, 0] = off[0, 0] * 1.01 + 1e-3
-    _, _, bad = ops.hif4_pack_weight(off, levels="123")
+    _, _, bad = ops.hif4_pack_weight(off, scale=scale, lv2=lv2, lv3=lv3)
     assert bad >= 1
