@@ -144,12 +144,23 @@ def test_attention_matches_oracle_mid_size(causal: bool, normalizer: str, levels
     _check_close(out, ref)
 
 
-def test_attention_unit_values_are_exactly_one_under_p_reordering() -> None:
-    # simulated_flash_attention tests :653-688: V = 1 and P-Reordering give exactly 1
+def test_attention_unit_values_are_exact_under_p_reordering() -> None:
+    # simulated_flash_attention tests :653-688: with P-Reordering the numerator and the
+    # denominator are sums of the same quantized P, so V = c gives exactly c. HiF4 itself
+    # maps 1.0 to 0.9375 (scale 0.15625, code 6 with both micro-exponents), so the
+    # QDQ'd V = 1 gives exactly 0.9375 and an unquantized V = 1 gives exactly 1.
+    ops = _ops()
     q, k, _ = attention_inputs(1, 4, 2, 300, 300, 88)
-    v = torch.ones(1, 2, 300, 128, dtype=torch.bfloat16)
-    out = _attention_gpu(q, k, v, causal=True, normalizer="quantized_same", qk_quant=True, pv_quant=True)
+    ones = torch.ones(1, 2, 300, 128, dtype=torch.bfloat16, device=DEV)
+    qd, _, _ = ops.qk_prep(q.to(DEV), levels="123", rotate=True)
+    kd, _, _ = ops.qk_prep(k.to(DEV), levels="123", rotate=True)
+    out = ops.hif4_attention(qd, kd, ones, causal=True, p_levels="123", quantized_normalizer=True)
     assert torch.equal(out.float().cpu(), torch.ones(1, 300, 4, 128))
+    vq, _, _ = ops.qk_prep(ones, levels="123", rotate=False)
+    c = float(oh.fake_quantize(np.ones((1, 64), np.float32))[0, 0])
+    assert c == 0.9375 and float(vq[0, 0, 0, 0]) == c
+    out = ops.hif4_attention(qd, kd, vq, causal=True, p_levels="123", quantized_normalizer=True)
+    assert torch.equal(out.float().cpu(), torch.full((1, 300, 4, 128), c))
 
 
 def test_bounded_wait_reports_timeout_status() -> None:
