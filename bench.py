@@ -450,6 +450,42 @@ def main_arm(args) -> None:
         dist.destroy_process_group()
 
 
+def kernel_case(name: str, reps: int) -> None:
+    """One kernel on a profiling-sized case (inputs > L2, a few GB at most), for ncu."""
+    import torch
+
+    from faquant_b200 import ops
+    from faquant_b200.hisq_rotation import derive_hisq_rotation
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if name == "gemm":  # q_proj-shaped: 8192 x 4096 x 4096 (A 64 MB + B 32 MB + Y 64 MB)
+        a, _, _ = ops.hif4_quantize(torch.randn(8192, 4096, device=dev, generator=g).to(torch.bfloat16))
+        b, _, _ = ops.hif4_quantize((torch.randn(4096, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+        y = torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16)
+        for _ in range(reps):
+            ops.gemm_bf16(a, b, out=y)
+    elif name == "quantize":  # gate_proj input: 8192 x 4096 bf16, HiSQ1024
+        x = torch.randn(8192, 4096, device=dev, generator=g).to(torch.bfloat16)
+        rot = derive_hisq_rotation("model.layers.0.mlp.gate_proj", 4096, seed=17, block_size=1024)
+        s, p = rot.signs.to(dev), rot.permutation.to(dev)
+        for _ in range(reps):
+            ops.hif4_quantize(x, levels="123", signs=s, permutation=p, rot_block=1024)
+    elif name == "attention":  # 8 q heads / 2 kv heads, S = 8192, causal
+        q = torch.randn(1, 8, 8192, 128, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, 2, 8192, 128, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(1, 2, 8192, 128, device=dev, generator=g).to(torch.bfloat16)
+        qd, _, _ = ops.qk_prep(q, levels="123", rotate=True)
+        kd, _, _ = ops.qk_prep(k, levels="123", rotate=True)
+        vd, _, _ = ops.qk_prep(v, levels="123", rotate=False)
+        for _ in range(reps):
+            ops.hif4_attention(qd, kd, vd, causal=True, p_levels="123", quantized_normalizer=True)
+    else:
+        raise SystemExit(f"unknown kernel case {name!r}")
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": name, "reps": reps, "ok": True}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -460,7 +496,13 @@ def main() -> None:
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention"],
+                    help="run one kernel on a profiling-sized case (for ncu) and exit")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args.kernel_case, args.reps)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -97,12 +97,12 @@ __device__ __forceinline__ float quantize_p64(float* p, int levels) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int sh = lv2 + (h ? lv3b : lv3a);
-      const float qm = __fmul_rn(sc.rec, pow2f(-sh));
+      const float qm4 = __fmul_rn(sc.rec, pow2f(2 - sh));  // 4 * qm, exact
       const float ds4 = __fmul_rn(sc.s, pow2f(sh - 2));
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         float& v = p[8 * i + 4 * h + t];
-        v = __fmul_rn(hif4_code(v, qm), ds4);
+        v = __fmul_rn(hif4_code4(v, qm4), ds4);
         sum = __fadd_rn(sum, v);
       }
     }

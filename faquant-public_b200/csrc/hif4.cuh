@@ -45,11 +45,16 @@ __device__ __forceinline__ Hif4Scale hif4_scale(float max64, int levels) {
   return r;
 }
 
-__device__ __forceinline__ float hif4_code(float a, float qm) {
-  // floor(fl(fl(|x| * qm) * 4) + 0.5) clamped to 7; the *4 is exact.
-  const float y = __fmul_rn(__fmul_rn(a, qm), 4.0f);
-  return fminf(floorf(__fadd_rn(y, 0.5f)), 7.0f);
+// Element code from |x| and qm4 = 4 * qm (exact): min(floor(fl(fl(|x| * qm4) + 0.5)), 7).
+// fl(|x| * qm) * 4 == fl(|x| * 4qm) because scaling by 4 is exact, so one multiply
+// reproduces the reference's two. floor(t) of 0 <= t < 2^23 is taken on the FP32
+// adder: t + 2^23 rounded toward zero is exactly 2^23 + floor(t).
+__device__ __forceinline__ float hif4_code4(float a, float qm4) {
+  const float t = __fadd_rn(__fmul_rn(a, qm4), 0.5f);
+  const float f = __fsub_rn(__fadd_rz(t, 8388608.0f), 8388608.0f);
+  return fminf(f, 7.0f);
 }
+__device__ __forceinline__ float hif4_code(float a, float qm) { return hif4_code4(a, __fmul_rn(qm, 4.0f)); }
 
 // Quantize the 8 consecutive values v[0..7] of one lv2 sub-block. The 8 lanes of
 // an aligned lane group (lanes 8g .. 8g+7) together hold one 64-value block in
@@ -81,14 +86,14 @@ __device__ __forceinline__ uint32_t hif4_quant8(const float (&v)[8], int levels,
     lv3_0 = __fmul_rn(m3_0, sc.rec) >= 2.0f;
     lv3_1 = __fmul_rn(m3_1, sc.rec) >= 2.0f;
   }
-  const float qm0 = __fmul_rn(sc.rec, pow2f(-static_cast<int>(lv2 + lv3_0)));
-  const float qm1 = __fmul_rn(sc.rec, pow2f(-static_cast<int>(lv2 + lv3_1)));
+  const float qm0 = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lv3_0)));  // 4 * qm
+  const float qm1 = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lv3_1)));
   const float ds0 = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lv3_0)));
   const float ds1 = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lv3_1)));
   uint32_t nibbles = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float m = hif4_code(a[i], i < 4 ? qm0 : qm1);
+    const float m = hif4_code4(a[i], i < 4 ? qm0 : qm1);
     const float mag = __fmul_rn(__fmul_rn(m, 0.25f), i < 4 ? ds0 : ds1);
     const bool neg = v[i] < 0.0f;
     out[i] = neg ? -mag : mag;

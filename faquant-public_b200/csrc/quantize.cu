@@ -268,6 +268,177 @@ __global__ void __launch_bounds__(256) hif4_quantize_rotate_kernel(const T* __re
   }
 }
 
+// ---------------------------------------------------------------- K1 v2, rotation, bf16 rows
+// The fast path for bf16 rows with k % 64 == 0, k <= 32768 and 16-byte aligned rows:
+//   - persistent CTAs; each row arrives by a TMA bulk copy (cp.async.bulk) into one
+//     of two shared-memory buffers, issued one row ahead, so the load of row r+1
+//     overlaps the arithmetic of row r;
+//   - the permutation and the sign share one 16-bit word per channel (index | sign << 15);
+//   - butterflies of stride < min(block, 512) run in registers, one warp per
+//     segment of min(block, 512) channels (16 values per lane at most), and write
+//     fp32 to shared memory; for block 1024 the last butterfly (stride 512) runs in
+//     the quantization pass, which reads both halves -- the stages keep the
+//     reference's order (rotation.py:22-28);
+//   - the quantization pass normalizes, rounds to bf16 and quantizes 8 values per
+//     thread (hif4_quant8).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+template <int LOG2B>
+__global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                               int k, int64_t ldx,
+                                                               const __nv_bfloat16* __restrict__ input_scale,
+                                                               const int8_t* __restrict__ signs,
+                                                               const int64_t* __restrict__ perm, int levels,
+                                                               QuantOut o) {
+  constexpr int B = 1 << LOG2B;
+  constexpr int HALF = B > 512 ? 512 : B;           // butterflies done in registers
+  constexpr int E = HALF >= 32 ? HALF / 32 : 1;     // values per lane
+  constexpr int SEG = 32 * E;
+  constexpr bool SPLIT = B > 512;                   // last stage in the quantization pass
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);                 // 2 barriers
+  uint16_t* s_map = reinterpret_cast<uint16_t*>(smem_raw + 64);           // [k]
+  const size_t map_bytes = (static_cast<size_t>(k) * 2 + 127) / 128 * 128;
+  __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_raw + 64 + map_bytes);  // [2][k]
+  float* s_mid = reinterpret_cast<float*>(smem_raw + 64 + map_bytes + static_cast<size_t>(k) * 4);  // [k]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
+
+  if (tid == 0) {
+    mbar_init(smem_addr(&bars[0]), 1);
+    mbar_init(smem_addr(&bars[1]), 1);
+    fence_barrier_init();
+  }
+  for (int j = tid; j < k; j += blockDim.x) {
+    const int src = perm ? static_cast<int>(perm[j]) : j;
+    s_map[j] = static_cast<uint16_t>(src | ((signs[src] < 0) ? 0x8000 : 0));
+  }
+  __syncthreads();
+  const int64_t first = blockIdx.x;
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      const int64_t r = first + static_cast<int64_t>(b) * gridDim.x;
+      if (r < rows) {
+        mbar_arrive_expect_tx(smem_addr(&bars[b]), row_bytes);
+        bulk_load(smem_addr(s_in + b * k), x + r * ldx, row_bytes, smem_addr(&bars[b]));
+      }
+    }
+  }
+  const int nseg = k / SEG;
+  const int chunks = k / 8;
+  int it = 0;
+  for (int64_t row = first; row < rows; row += gridDim.x, ++it) {
+    const int buf = it & 1;
+    const __nv_bfloat16* in = s_in + buf * k;
+    // CTA-uniform decision: a barrier follows, so no warp may leave the loop alone
+    if (!__syncthreads_and(mbar_wait(smem_addr(&bars[buf]), (it >> 1) & 1))) {
+      if (tid == 0) {
+        trace_timeout(30, it);
+        // bounded drain of the copies still in flight into either buffer
+        for (int b = 0; b < 2; ++b) {
+          const int64_t r = row + static_cast<int64_t>(b) * gridDim.x;
+          if (r < rows) mbar_wait(smem_addr(&bars[(it + b) & 1]), ((it + b) >> 1) & 1);
+        }
+      }
+      break;
+    }
+    // gather + butterflies in registers
+    for (int seg = warp; seg < nseg; seg += nwarps) {
+      float v[E];
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int j = seg * SEG + i * 32 + lane;
+        const uint32_t m = s_map[j];
+        const int src = static_cast<int>(m & 0x7FFFu);
+        float val = __bfloat162float(in[src]);
+        if (input_scale != nullptr) val = bf16_round(__fmul_rn(val, __bfloat162float(input_scale[src])));
+        v[i] = (m & 0x8000u) ? -val : val;
+      }
+#pragma unroll
+      for (int st = 1; st < HALF; st <<= 1) {
+        if (st < 32) {
+#pragma unroll
+          for (int i = 0; i < E; ++i) {
+            const float other = __shfl_xor_sync(0xffffffffu, v[i], st);
+            v[i] = (lane & st) ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+          }
+        } else {
+          const int d = st >> 5;
+#pragma unroll
+          for (int i = 0; i < E; ++i) {
+            if ((i & d) == 0) {
+              const float l = v[i], r = v[i + d];
+              v[i] = __fadd_rn(l, r);
+              v[i + d] = __fsub_rn(l, r);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        float r = v[i];
+        if constexpr (!SPLIT) {
+          if constexpr ((LOG2B & 1) == 0)
+            r = __fmul_rn(r, pow2f(-(LOG2B / 2)));
+          else
+            r = __fdiv_rn(r, static_cast<float>(LOG2B == 1 ? 1.4142135623730951 : LOG2B == 3 ? 2.8284271247461903
+                                                : LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
+                                                : 22.627416997969522));
+          r = bf16_round(r);
+        }
+        s_mid[seg * SEG + i * 32 + lane] = r;
+      }
+    }
+    __syncthreads();
+    // the input buffer is free again: prefetch the row after next into it
+    if (tid == 0) {
+      const int64_t r2 = row + 2 * static_cast<int64_t>(gridDim.x);
+      if (r2 < rows) {
+        mbar_arrive_expect_tx(smem_addr(&bars[buf]), row_bytes);
+        bulk_load(smem_addr(s_in + buf * k), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
+      }
+    }
+    // quantization pass (with the last butterfly for block 1024)
+    for (int c0 = 0; c0 < chunks; c0 += blockDim.x) {
+      const int c = c0 + tid;
+      const bool live = c < chunks;
+      const int col = live ? c * 8 : 0;
+      float v[8];
+      {
+        const float4 a0 = *reinterpret_cast<const float4*>(s_mid + col);
+        const float4 a1 = *reinterpret_cast<const float4*>(s_mid + col + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+      }
+      if constexpr (SPLIT) {
+        const int partner = col ^ 512;
+        const float4 b0 = *reinterpret_cast<const float4*>(s_mid + partner);
+        const float4 b1 = *reinterpret_cast<const float4*>(s_mid + partner + 4);
+        const float w[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const bool lower = (col & 512) == 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float r = lower ? __fadd_rn(v[i], w[i]) : __fsub_rn(w[i], v[i]);
+          v[i] = bf16_round(__fmul_rn(r, 0.03125f));  // 1/sqrt(1024), exact
+        }
+      }
+      float q[8];
+      uint32_t meta_word;
+      const uint32_t nib = hif4_quant8(v, levels, q, meta_word);
+      if (live) {
+        if (o.codes) reinterpret_cast<uint32_t*>(o.codes + row * (k / 2))[c] = nib;
+        if (o.meta && (tid & 7) == 0) o.meta[row * (k / 64) + c / 8] = meta_word;
+        if (o.qdq) store8<__nv_bfloat16>(static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col, q, o.qdq_vec, 8);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------- dequantize
 template <typename T>
 __global__ void __launch_bounds__(256) hif4_dequantize_kernel(const uint8_t* __restrict__ codes,
@@ -379,6 +550,43 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
   int block = rot_block == 0 ? 1 : rot_block;
   int log2b = 0;
   while ((1 << log2b) < block) ++log2b;
+  if constexpr (sizeof(T) == 2) {
+    const bool v2 = k % 64 == 0 && k <= 32768 && x_vec && (block >= 32 || k % 32 == 0) && block <= 1024;
+    if (v2) {
+      const size_t smem2 = 64 + (static_cast<size_t>(k) * 2 + 127) / 128 * 128 + static_cast<size_t>(k) * 4 +
+                           static_cast<size_t>(k) * 4;
+      if (smem2 <= 200 * 1024) {
+        const int threads = k >= 8192 ? 512 : 256;
+        const int per_sm = std::max(1, std::min(4, static_cast<int>((220 * 1024) / (smem2 + 1024))));
+        const int64_t blocks2 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
+#define FAQ_ROT2_CASE(L)                                                                                          \
+  case L: {                                                                                                       \
+    auto kern = hif4_rotate_bf16_kernel<L>;                                                                       \
+    FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem2)));  \
+    kern<<<static_cast<unsigned>(blocks2), threads, smem2, stream>>>(                                             \
+        static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                      \
+        static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o);                                   \
+    return launch_status("hif4_rotate_bf16_kernel");                                                             \
+  }
+        switch (log2b) {
+          FAQ_ROT2_CASE(0)
+          FAQ_ROT2_CASE(1)
+          FAQ_ROT2_CASE(2)
+          FAQ_ROT2_CASE(3)
+          FAQ_ROT2_CASE(4)
+          FAQ_ROT2_CASE(5)
+          FAQ_ROT2_CASE(6)
+          FAQ_ROT2_CASE(7)
+          FAQ_ROT2_CASE(8)
+          FAQ_ROT2_CASE(9)
+          FAQ_ROT2_CASE(10)
+          default:
+            break;
+        }
+#undef FAQ_ROT2_CASE
+      }
+    }
+  }
   const int64_t k64 = (k + 63) / 64 * 64;
   const size_t smem = static_cast<size_t>((k * 4 + 15) / 16 * 16) + 2 * static_cast<size_t>(k64) * sizeof(T);
   if (smem > 220 * 1024)

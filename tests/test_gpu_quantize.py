@@ -70,9 +70,15 @@ BLOCKS = [1, 2, 4, 8, 16, 32, 64, 128, 256, 512, 1024]
 
 @pytest.mark.parametrize("block", BLOCKS)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_rotation_blocks_bit_exact(block: int, dtype: torch.dtype) -> None:
+@pytest.mark.parametrize("kind", ["ragged", "aligned"])
+def test_rotation_blocks_bit_exact(block: int, dtype: torch.dtype, kind: str) -> None:
+    """Every block size through both kernels: rows with a ragged 64-tail (staged path)
+    and rows of whole 64-blocks (the double-buffered bf16 path)."""
     ops = _ops()
-    k = block * max(1, 2048 // block) if block >= 64 else 64 * 5 + (block if block < 64 else 0)
+    if kind == "aligned":
+        k = 3072 if block <= 1024 and 3072 % block == 0 else 2048
+    else:
+        k = 2048 if block >= 64 else 64 * 5 + block
     k = k - k % block
     rng = np.random.default_rng(block)
     x = torch.from_numpy(rng.standard_normal((37, k)).astype(np.float32) * 3).to(dtype)
