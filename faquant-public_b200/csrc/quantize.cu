@@ -439,6 +439,239 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
   }
 }
 
+// ---------------------------------------------------------------- K1 v3, rotation, bf16 rows
+// Throughput path for bf16 rows with k % 1024 == 0 and 32 <= block <= 1024 (all HiSQ and
+// r64 shapes of the BASELINE configurations). Work is counted in instructions per element
+// because the v2 form of this kernel was issue-bound, not memory-bound:
+//   - 4 warps; warp w owns 1024-channel chunks w, w+4, ...; lane l gathers the 32
+//     consecutive output channels 32l .. 32l+31 of its chunk through the permutation
+//     (the 16-bit map is stored lane-transposed, two entries per word, so map loads are
+//     conflict-free) and applies the sign with one XOR of the sign bit;
+//   - butterflies of stride 1..16 run inside the lane, a padded 32x33 shared-memory
+//     transpose gives lane c the channels c, c+32, c+64, ..., and strides 32..block/2
+//     run inside the lane again -- the stages in the reference's order;
+//   - normalization, one bf16 rounding, natural-order store;
+//   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
+//     block maximum, per-4/per-8 maxima in registers, nibbles only when codes are asked.
+template <int LOG2B, bool CODES>
+__global__ void __launch_bounds__(128) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
+                                                             int64_t ldx, const __nv_bfloat16* __restrict__ input_scale,
+                                                             const int8_t* __restrict__ signs,
+                                                             const int64_t* __restrict__ perm, int levels, QuantOut o) {
+  constexpr int B = 1 << LOG2B;
+  static_assert(B >= 32 && B <= 1024, "v3 handles blocks 32..1024");
+  constexpr int NW = 4;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                       // [k/2]
+  __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_raw + 16 + static_cast<size_t>(k) * 2);  // [2][k]
+  uint16_t* s_out = reinterpret_cast<uint16_t*>(smem_raw + 16 + static_cast<size_t>(k) * 6);          // [k]
+  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);                 // [NW][32*33]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
+  const int nchunks = k >> 10;
+
+  if (tid == 0) {
+    mbar_init(smem_addr(&bars[0]), 1);
+    mbar_init(smem_addr(&bars[1]), 1);
+    fence_barrier_init();
+  }
+  // map word (chunk, t2, lane) = entries for channels chunk*1024 + 32 lane + 2 t2 (+1)
+  for (int w = tid; w < k / 2; w += blockDim.x) {
+    const int l = w & 31, t2 = (w >> 5) & 15, ch = w >> 9;
+    const int j0 = (ch << 10) + 32 * l + 2 * t2;
+    uint32_t word = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = j0 + h;
+      const int src = perm ? static_cast<int>(perm[j]) : j;
+      word |= static_cast<uint32_t>(src | ((signs[src] < 0) ? 0x8000 : 0)) << (16 * h);
+    }
+    s_map[w] = word;
+  }
+  __syncthreads();
+  const int64_t first = blockIdx.x;
+  if (tid == 0) {
+    for (int b = 0; b < 2; ++b) {
+      const int64_t r = first + static_cast<int64_t>(b) * gridDim.x;
+      if (r < rows) {
+        mbar_arrive_expect_tx(smem_addr(&bars[b]), row_bytes);
+        bulk_load(smem_addr(s_in + b * k), x + r * ldx, row_bytes, smem_addr(&bars[b]));
+      }
+    }
+  }
+  const uint16_t* in_base = reinterpret_cast<const uint16_t*>(s_in);
+  float* tr = s_tr + warp * (32 * 33);
+  const int tasks = k >> 5;  // 32-value halves of 64-blocks
+  int it = 0;
+  for (int64_t row = first; row < rows; row += gridDim.x, ++it) {
+    const int buf = it & 1;
+    if (!__syncthreads_and(mbar_wait(smem_addr(&bars[buf]), (it >> 1) & 1))) {
+      if (tid == 0) {
+        trace_timeout(31, it);
+        for (int b = 0; b < 2; ++b) {
+          const int64_t r = row + static_cast<int64_t>(b) * gridDim.x;
+          if (r < rows) mbar_wait(smem_addr(&bars[(it + b) & 1]), ((it + b) >> 1) & 1);
+        }
+      }
+      break;
+    }
+    const uint16_t* in = in_base + buf * k;
+    for (int ch = warp; ch < nchunks; ch += NW) {
+      float v[32];
+      const uint32_t* mrow = s_map + (ch << 9) + lane;
+#pragma unroll
+      for (int t2 = 0; t2 < 16; ++t2) {
+        const uint32_t word = mrow[t2 * 32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t m = (word >> (16 * h)) & 0xFFFFu;
+          const uint32_t src = m & 0x7FFFu;
+          uint32_t bits = static_cast<uint32_t>(in[src]) << 16;
+          if (input_scale != nullptr)
+            bits = __float_as_uint(bf16_round(__fmul_rn(__uint_as_float(bits), __bfloat162float(input_scale[src]))));
+          v[2 * t2 + h] = __uint_as_float(bits ^ ((m & 0x8000u) << 16));  // * (+-1), exact
+        }
+      }
+      // strides 1 .. 16 inside the lane
+#pragma unroll
+      for (int st = 1; st < 32 && st < B; st <<= 1) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          if ((t & st) == 0) {
+            const float l = v[t], r = v[t + st];
+            v[t] = __fadd_rn(l, r);
+            v[t + st] = __fsub_rn(l, r);
+          }
+        }
+      }
+      // transpose: lane c gets channels c + 32 i
+#pragma unroll
+      for (int t = 0; t < 32; ++t) tr[lane * 33 + t] = v[t];
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = tr[i * 33 + lane];
+      __syncwarp();
+      // strides 32 .. B/2 inside the lane
+#pragma unroll
+      for (int d = 1; d < B / 32; d <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if ((i & d) == 0) {
+            const float l = v[i], r = v[i + d];
+            v[i] = __fadd_rn(l, r);
+            v[i + d] = __fsub_rn(l, r);
+          }
+        }
+      }
+      uint16_t* out = s_out + (ch << 10) + lane;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float r;
+        if constexpr ((LOG2B & 1) == 0)
+          r = __fmul_rn(v[i], pow2f(-(LOG2B / 2)));
+        else
+          r = __fdiv_rn(v[i], static_cast<float>(LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
+                                                 : 22.627416997969522));
+        out[i * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(r));
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const int64_t r2 = row + 2 * static_cast<int64_t>(gridDim.x);
+      if (r2 < rows) {
+        mbar_arrive_expect_tx(smem_addr(&bars[buf]), row_bytes);
+        bulk_load(smem_addr(s_in + buf * k), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
+      }
+    }
+    // quantization: thread = 32 consecutive values; partner lane (tid ^ 1) holds the other half
+    for (int t0 = 0; t0 < tasks; t0 += blockDim.x) {
+      const int task = t0 + tid;
+      const bool live = task < tasks;
+      const int col = (live ? task : 0) * 32;
+      float a[32];
+      uint32_t sgn = 0;  // sign bits of the 32 values
+      {
+        const uint4* src = reinterpret_cast<const uint4*>(s_out + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 u = src[q];
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float lo = __uint_as_float(w4[h] << 16), hi = __uint_as_float(w4[h] & 0xFFFF0000u);
+            sgn |= static_cast<uint32_t>(lo < 0.0f) << (8 * q + 2 * h);
+            sgn |= static_cast<uint32_t>(hi < 0.0f) << (8 * q + 2 * h + 1);
+            a[8 * q + 2 * h] = fabsf(lo);
+            a[8 * q + 2 * h + 1] = fabsf(hi);
+          }
+        }
+      }
+      float m3[8], m2[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[4 * i], a[4 * i + 1]), fmaxf(a[4 * i + 2], a[4 * i + 3]));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
+      float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+      const Hif4Scale sc = hif4_scale(m1, levels);
+      uint32_t lvbits = 0;  // bit i: lv2 of sub-block i (4), bit 4+j: lv3 of quarter j (8)
+      float qm4[8], ds4[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t lv2 = 0, la = 0, lb = 0;
+        if (levels == 123) {
+          lv2 = __fmul_rn(m2[i], sc.rec) >= 4.0f;
+          const float thr = lv2 ? 4.0f : 2.0f;
+          la = __fmul_rn(m3[2 * i], sc.rec) >= thr;
+          lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= thr;
+        } else if (levels == 12) {
+          lv2 = __fmul_rn(m2[i], sc.rec) >= 2.0f;
+        } else {
+          la = __fmul_rn(m3[2 * i], sc.rec) >= 2.0f;
+          lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
+        }
+        lvbits |= (lv2 << i) | (la << (4 + 2 * i)) | (lb << (5 + 2 * i));
+        qm4[2 * i] = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + la)));
+        qm4[2 * i + 1] = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lb)));
+        ds4[2 * i] = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + la) - 2));
+        ds4[2 * i + 1] = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lb) - 2));
+      }
+      uint32_t packed[16];
+      uint32_t nib[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float m = hif4_code4(a[i], qm4[i >> 2]);
+        const uint32_t neg = (sgn >> i) & 1u;
+        const uint32_t mag_bits = __float_as_uint(__fmul_rn(m, ds4[i >> 2]));
+        const uint32_t bf = (mag_bits >> 16) | (neg << 15);
+        if (i & 1)
+          packed[i >> 1] |= bf << 16;
+        else
+          packed[i >> 1] = bf;
+        if constexpr (CODES) nib[i >> 3] |= ((static_cast<uint32_t>(m) | (neg << 3)) << (4 * (i & 7)));
+      }
+      const int half = task & 1;
+      uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
+      mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
+      if (live) {
+        if (o.qdq) {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        }
+        if constexpr (CODES) {
+          if (o.codes)
+            *reinterpret_cast<uint4*>(o.codes + row * (k / 2) + col / 2) = make_uint4(nib[0], nib[1], nib[2], nib[3]);
+        }
+        if (o.meta && half == 0) o.meta[row * (k / 64) + task / 2] = mb | sc.code;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------- dequantize
 template <typename T>
 __global__ void __launch_bounds__(256) hif4_dequantize_kernel(const uint8_t* __restrict__ codes,
@@ -551,6 +784,36 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
   int log2b = 0;
   while ((1 << log2b) < block) ++log2b;
   if constexpr (sizeof(T) == 2) {
+    const bool v3 = k % 1024 == 0 && k <= 32768 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
+                    (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
+    if (v3) {
+      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + 4 * 32 * 33 * 4;
+      if (smem3 <= 200 * 1024) {
+        const int per_sm = std::max(1, std::min(8, static_cast<int>((224 * 1024) / (smem3 + 1024))));
+        const int64_t blocks3 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
+        const bool codes = o.codes != nullptr;
+#define FAQ_ROT3_CASE(L)                                                                                          \
+  case L: {                                                                                                       \
+    auto kern = codes ? hif4_rotate_v3_kernel<L, true> : hif4_rotate_v3_kernel<L, false>;                          \
+    FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem3)));  \
+    kern<<<static_cast<unsigned>(blocks3), 128, smem3, stream>>>(                                                 \
+        static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                      \
+        static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o);                                   \
+    return launch_status("hif4_rotate_v3_kernel");                                                               \
+  }
+        switch (log2b) {
+          FAQ_ROT3_CASE(5)
+          FAQ_ROT3_CASE(6)
+          FAQ_ROT3_CASE(7)
+          FAQ_ROT3_CASE(8)
+          FAQ_ROT3_CASE(9)
+          FAQ_ROT3_CASE(10)
+          default:
+            break;
+        }
+#undef FAQ_ROT3_CASE
+      }
+    }
     const bool v2 = k % 64 == 0 && k <= 32768 && x_vec && (block >= 32 || k % 32 == 0) && block <= 1024;
     if (v2) {
       const size_t smem2 = 64 + (static_cast<size_t>(k) * 2 + 127) / 128 * 128 + static_cast<size_t>(k) * 4 +
