@@ -335,6 +335,14 @@ def main_arm(args) -> None:
     value = linear_flops() * world / (ms_max * 1e-3) / 1e12
     gemm_tflops = linear_flops() * args.steps / (gemm_ms * 1e-3) / 1e12
     quant_bytes = sum(T_TOKENS * k * (2 + 2) for _, k, _ in PROJECTIONS)  # bf16 read + bf16 QDQ write
+    nproj = len(PROJECTIONS)
+    per_proj = {
+        p: {"quantize_ms": sum(timers["q0"][i].elapsed_time(timers["g0"][i]) for i in range(j, n_gemm, nproj))
+            / args.steps,
+            "gemm_ms": sum(timers["g0"][i].elapsed_time(timers["g1"][i]) for i in range(j, n_gemm, nproj))
+            / args.steps}
+        for j, (p, _, _) in enumerate(PROJECTIONS)
+    }
     quant_gbs = quant_bytes * args.steps / (quant_ms * 1e-3) / 1e9
 
     # ---------------- attention (config 3), device-resident
@@ -437,6 +445,7 @@ def main_arm(args) -> None:
             "quantize_kernel": {"kernel": "hif4_quantize_rotate_kernel", "bound": "hbm", "achieved": quant_gbs,
                                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": quant_gbs / pk["hbm_gbs"],
                                 "ms_per_step": quant_ms / args.steps},
+            "per_projection_ms": per_proj,
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "attention": att,

@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 // Throughput path for bf16 rows with k % 1024 == 0 and 32 <= block <= 1024 (all HiSQ and
 // r64 shapes of the BASELINE configurations). Work is counted in instructions per element
 // because the v2 form of this kernel was issue-bound, not memory-bound:
-//   - 4 warps; warp w owns 1024-channel chunks w, w+4, ...; lane l gathers the 32
+//   - one warp per 1024-channel chunk (4..16 warps); warp w owns chunks w, w+W, ...; lane l gathers the 32
 //     consecutive output channels 32l .. 32l+31 of its chunk through the permutation
 //     (the 16-bit map is stored lane-transposed, two entries per word, so map loads are
 //     conflict-free) and applies the sign with one XOR of the sign bit;
@@ -454,19 +454,19 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 //   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
 //     block maximum, per-4/per-8 maxima in registers, nibbles only when codes are asked.
 template <int LOG2B, bool CODES>
-__global__ void __launch_bounds__(128) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
+__global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                              int64_t ldx, const __nv_bfloat16* __restrict__ input_scale,
                                                              const int8_t* __restrict__ signs,
                                                              const int64_t* __restrict__ perm, int levels, QuantOut o) {
   constexpr int B = 1 << LOG2B;
   static_assert(B >= 32 && B <= 1024, "v3 handles blocks 32..1024");
-  constexpr int NW = 4;
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int NW = blockDim.x >> 5;  // one warp per 1024-channel chunk, up to 16
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                       // [k/2]
   __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_raw + 16 + static_cast<size_t>(k) * 2);  // [2][k]
   uint16_t* s_out = reinterpret_cast<uint16_t*>(smem_raw + 16 + static_cast<size_t>(k) * 6);          // [k]
-  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);                 // [NW][32*33]
+  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);                 // [warps][32*33]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
   const int nchunks = k >> 10;
@@ -787,7 +787,8 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
     const bool v3 = k % 1024 == 0 && k <= 32768 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
                     (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
     if (v3) {
-      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + 4 * 32 * 33 * 4;
+      const int warps3 = std::min(16, std::max(4, static_cast<int>(k / 1024)));
+      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + static_cast<size_t>(warps3) * 32 * 33 * 4;
       if (smem3 <= 200 * 1024) {
         const int per_sm = std::max(1, std::min(8, static_cast<int>((224 * 1024) / (smem3 + 1024))));
         const int64_t blocks3 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
@@ -796,7 +797,7 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
   case L: {                                                                                                       \
     auto kern = codes ? hif4_rotate_v3_kernel<L, true> : hif4_rotate_v3_kernel<L, false>;                          \
     FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem3)));  \
-    kern<<<static_cast<unsigned>(blocks3), 128, smem3, stream>>>(                                                 \
+    kern<<<static_cast<unsigned>(blocks3), warps3 * 32, smem3, stream>>>(                                                 \
         static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                      \
         static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o);                                   \
     return launch_status("hif4_rotate_v3_kernel");                                                               \
