@@ -441,18 +441,23 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 
 // ---------------------------------------------------------------- K1 v3, rotation, bf16 rows
 // Throughput path for bf16 rows with k % 1024 == 0 and 32 <= block <= 1024 (all HiSQ and
-// r64 shapes of the BASELINE configurations). Work is counted in instructions per element
-// because the v2 form of this kernel was issue-bound, not memory-bound:
-//   - one warp per 1024-channel chunk (4..16 warps); warp w owns chunks w, w+W, ...; lane l gathers the 32
-//     consecutive output channels 32l .. 32l+31 of its chunk through the permutation
-//     (the 16-bit map is stored lane-transposed, two entries per word, so map loads are
-//     conflict-free) and applies the sign with one XOR of the sign bit;
-//   - butterflies of stride 1..16 run inside the lane, a padded 32x33 shared-memory
-//     transpose gives lane c the channels c, c+32, c+64, ..., and strides 32..block/2
-//     run inside the lane again -- the stages in the reference's order;
-//   - normalization, one bf16 rounding, natural-order store;
+// r64 shapes of the BASELINE configurations). It is issue-bound (a 1024-point Hadamard is
+// 10 adds per value before any quantization), so the work is counted per element:
+//   - one warp per 1024-channel chunk (4..16 warps); lane l gathers output channels
+//     32l .. 32l+31 of its chunk through a 32-bit map entry (byte offset | sign << 31),
+//     stored lane-transposed so that one 16-byte load brings 4 entries without bank
+//     conflicts; the sign is one XOR of the sign bit (x * -1 is exact);
+//   - butterflies (the reference's stage order, rotation.py:22-28): stride 1 inside a
+//     float2, strides 2..16 on float2 pairs (packed FP32x2 adds), a 32x34 shared-memory
+//     transpose, then strides 32..block/2 the same way;
+//   - normalization by an exact power of two as ffma2(v, 2^-k, +0), which also maps
+//     -0.0 to +0.0; that changes no output (the reference's sign(-0.0) is 0) and lets
+//     the quantization pass copy sign bits instead of comparing;
 //   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
-//     block maximum, per-4/per-8 maxima in registers, nibbles only when codes are asked.
+//     block maximum, per-4/per-8 maxima in registers, the element code on FP32x2.
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+
 template <int LOG2B, bool CODES>
 __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                              int64_t ldx, const __nv_bfloat16* __restrict__ input_scale,
@@ -460,13 +465,14 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
                                                              const int64_t* __restrict__ perm, int levels, QuantOut o) {
   constexpr int B = 1 << LOG2B;
   static_assert(B >= 32 && B <= 1024, "v3 handles blocks 32..1024");
+  constexpr int TS = 34;  // transpose row stride (floats): 64-bit stores and column loads conflict-free
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int NW = blockDim.x >> 5;  // one warp per 1024-channel chunk, up to 16
+  const int NW = blockDim.x >> 5;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
-  uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                       // [k/2]
-  __nv_bfloat16* s_in = reinterpret_cast<__nv_bfloat16*>(smem_raw + 16 + static_cast<size_t>(k) * 2);  // [2][k]
-  uint16_t* s_out = reinterpret_cast<uint16_t*>(smem_raw + 16 + static_cast<size_t>(k) * 6);          // [k]
-  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);                 // [warps][32*33]
+  uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                                   // [k]
+  unsigned char* s_in = smem_raw + 16 + static_cast<size_t>(k) * 4;                                // [2][k] bf16
+  uint16_t* s_out = reinterpret_cast<uint16_t*>(smem_raw + 16 + static_cast<size_t>(k) * 8);      // [k]
+  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 10);            // [NW][32*TS]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
   const int nchunks = k >> 10;
@@ -476,18 +482,13 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
     mbar_init(smem_addr(&bars[1]), 1);
     fence_barrier_init();
   }
-  // map word (chunk, t2, lane) = entries for channels chunk*1024 + 32 lane + 2 t2 (+1)
-  for (int w = tid; w < k / 2; w += blockDim.x) {
-    const int l = w & 31, t2 = (w >> 5) & 15, ch = w >> 9;
-    const int j0 = (ch << 10) + 32 * l + 2 * t2;
-    uint32_t word = 0;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int j = j0 + h;
-      const int src = perm ? static_cast<int>(perm[j]) : j;
-      word |= static_cast<uint32_t>(src | ((signs[src] < 0) ? 0x8000 : 0)) << (16 * h);
-    }
-    s_map[w] = word;
+  // entry (chunk, t4, lane, e) at word ((chunk*8 + t4)*32 + lane)*4 + e describes output
+  // channel chunk*1024 + 32*lane + 4*t4 + e
+  for (int w = tid; w < k; w += blockDim.x) {
+    const int e = w & 3, l = (w >> 2) & 31, t4 = (w >> 7) & 7, ch = w >> 10;
+    const int j = (ch << 10) + 32 * l + 4 * t4 + e;
+    const int src = perm ? static_cast<int>(perm[j]) : j;
+    s_map[w] = static_cast<uint32_t>(src * 2) | ((signs[src] < 0) ? 0x80000000u : 0u);
   }
   __syncthreads();
   const int64_t first = blockIdx.x;
@@ -496,12 +497,11 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       const int64_t r = first + static_cast<int64_t>(b) * gridDim.x;
       if (r < rows) {
         mbar_arrive_expect_tx(smem_addr(&bars[b]), row_bytes);
-        bulk_load(smem_addr(s_in + b * k), x + r * ldx, row_bytes, smem_addr(&bars[b]));
+        bulk_load(smem_addr(s_in + b * row_bytes), x + r * ldx, row_bytes, smem_addr(&bars[b]));
       }
     }
   }
-  const uint16_t* in_base = reinterpret_cast<const uint16_t*>(s_in);
-  float* tr = s_tr + warp * (32 * 33);
+  float* tr = s_tr + warp * (32 * TS);
   const int tasks = k >> 5;  // 32-value halves of 64-blocks
   int it = 0;
   for (int64_t row = first; row < rows; row += gridDim.x, ++it) {
@@ -516,64 +516,79 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       }
       break;
     }
-    const uint16_t* in = in_base + buf * k;
+    const unsigned char* in = s_in + buf * row_bytes;
     for (int ch = warp; ch < nchunks; ch += NW) {
-      float v[32];
-      const uint32_t* mrow = s_map + (ch << 9) + lane;
+      float2 p[16];
+      const uint4* mrow = reinterpret_cast<const uint4*>(s_map) + (ch << 8) + lane;
 #pragma unroll
-      for (int t2 = 0; t2 < 16; ++t2) {
-        const uint32_t word = mrow[t2 * 32];
+      for (int t4 = 0; t4 < 8; ++t4) {
+        const uint4 m4 = mrow[t4 * 32];
+        const uint32_t m[4] = {m4.x, m4.y, m4.z, m4.w};
+        float g[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t m = (word >> (16 * h)) & 0xFFFFu;
-          const uint32_t src = m & 0x7FFFu;
-          uint32_t bits = static_cast<uint32_t>(in[src]) << 16;
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t off = m[e] & 0x7FFFFFFFu;
+          uint32_t bits = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(in + off)) << 16;
           if (input_scale != nullptr)
-            bits = __float_as_uint(bf16_round(__fmul_rn(__uint_as_float(bits), __bfloat162float(input_scale[src]))));
-          v[2 * t2 + h] = __uint_as_float(bits ^ ((m & 0x8000u) << 16));  // * (+-1), exact
+            bits = __float_as_uint(bf16_round(__fmul_rn(__uint_as_float(bits), __bfloat162float(input_scale[off >> 1]))));
+          g[e] = __uint_as_float(bits ^ (m[e] & 0x80000000u));
         }
+        p[2 * t4] = make_float2(g[0], g[1]);
+        p[2 * t4 + 1] = make_float2(g[2], g[3]);
       }
-      // strides 1 .. 16 inside the lane
+      // stride 1: inside each float2
 #pragma unroll
-      for (int st = 1; st < 32 && st < B; st <<= 1) {
+      for (int q = 0; q < 16; ++q) p[q] = make_float2(__fadd_rn(p[q].x, p[q].y), __fsub_rn(p[q].x, p[q].y));
+      // strides 2 .. 16 (and < B): float2 index distance d = stride / 2
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          if ((t & st) == 0) {
-            const float l = v[t], r = v[t + st];
-            v[t] = __fadd_rn(l, r);
-            v[t + st] = __fsub_rn(l, r);
+      for (int d = 1; d < 16 && 2 * d < B; d <<= 1) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if ((q & d) == 0) {
+            const float2 l = p[q], r = p[q + d];
+            p[q] = f2add(l, r);
+            p[q + d] = f2sub(l, r);
           }
         }
       }
-      // transpose: lane c gets channels c + 32 i
+      // transpose through shared memory: lane c then holds channels c + 32 i
 #pragma unroll
-      for (int t = 0; t < 32; ++t) tr[lane * 33 + t] = v[t];
+      for (int q = 0; q < 16; ++q) *reinterpret_cast<float2*>(tr + lane * TS + 2 * q) = p[q];
       __syncwarp();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = tr[i * 33 + lane];
+      for (int q = 0; q < 16; ++q) p[q] = make_float2(tr[(2 * q) * TS + lane], tr[(2 * q + 1) * TS + lane]);
       __syncwarp();
-      // strides 32 .. B/2 inside the lane
+      // strides 32 .. B/2: i xor 1 inside the float2, then float2 distance d
+      if constexpr (B >= 64) {
 #pragma unroll
-      for (int d = 1; d < B / 32; d <<= 1) {
+        for (int q = 0; q < 16; ++q) p[q] = make_float2(__fadd_rn(p[q].x, p[q].y), __fsub_rn(p[q].x, p[q].y));
+      }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if ((i & d) == 0) {
-            const float l = v[i], r = v[i + d];
-            v[i] = __fadd_rn(l, r);
-            v[i + d] = __fsub_rn(l, r);
+      for (int d = 1; 64 * d < B; d <<= 1) {
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          if ((q & d) == 0) {
+            const float2 l = p[q], r = p[q + d];
+            p[q] = f2add(l, r);
+            p[q + d] = f2sub(l, r);
           }
         }
       }
       uint16_t* out = s_out + (ch << 10) + lane;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float r;
-        if constexpr ((LOG2B & 1) == 0)
-          r = __fmul_rn(v[i], pow2f(-(LOG2B / 2)));
-        else
-          r = __fdiv_rn(v[i], static_cast<float>(LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
-                                                 : 22.627416997969522));
-        out[i * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(r));
+      for (int q = 0; q < 16; ++q) {
+        float2 r;
+        if constexpr ((LOG2B & 1) == 0) {
+          const float c = pow2f(-(LOG2B / 2));
+          r = __ffma2_rn(p[q], make_float2(c, c), make_float2(0.0f, 0.0f));  // exact; -0 -> +0
+        } else {
+          const float sq = static_cast<float>(LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
+                                                : 22.627416997969522);
+          r = make_float2(__fadd_rn(__fdiv_rn(p[q].x, sq), 0.0f), __fadd_rn(__fdiv_rn(p[q].y, sq), 0.0f));
+        }
+        const __nv_bfloat162 b2 = __float22bfloat162_rn(r);
+        out[(2 * q) * 32] = __bfloat16_as_ushort(b2.x);
+        out[(2 * q + 1) * 32] = __bfloat16_as_ushort(b2.y);
       }
     }
     __syncthreads();
@@ -581,7 +596,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       const int64_t r2 = row + 2 * static_cast<int64_t>(gridDim.x);
       if (r2 < rows) {
         mbar_arrive_expect_tx(smem_addr(&bars[buf]), row_bytes);
-        bulk_load(smem_addr(s_in + buf * k), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
+        bulk_load(smem_addr(s_in + buf * row_bytes), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
       }
     }
     // quantization: thread = 32 consecutive values; partner lane (tid ^ 1) holds the other half
@@ -589,8 +604,8 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       const int task = t0 + tid;
       const bool live = task < tasks;
       const int col = (live ? task : 0) * 32;
-      float a[32];
-      uint32_t sgn = 0;  // sign bits of the 32 values
+      uint32_t sgn[16];  // sign bits of each bf16 pair (no -0.0 here)
+      float2 a[16];      // |x| pairs
       {
         const uint4* src = reinterpret_cast<const uint4*>(s_out + col);
 #pragma unroll
@@ -599,24 +614,23 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
-            const float lo = __uint_as_float(w4[h] << 16), hi = __uint_as_float(w4[h] & 0xFFFF0000u);
-            sgn |= static_cast<uint32_t>(lo < 0.0f) << (8 * q + 2 * h);
-            sgn |= static_cast<uint32_t>(hi < 0.0f) << (8 * q + 2 * h + 1);
-            a[8 * q + 2 * h] = fabsf(lo);
-            a[8 * q + 2 * h + 1] = fabsf(hi);
+            const uint32_t w = w4[h];
+            sgn[4 * q + h] = w & 0x80008000u;
+            const uint32_t m = w & 0x7FFF7FFFu;
+            a[4 * q + h] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
           }
         }
       }
       float m3[8], m2[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[4 * i], a[4 * i + 1]), fmaxf(a[4 * i + 2], a[4 * i + 3]));
+      for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[2 * i].x, a[2 * i].y), fmaxf(a[2 * i + 1].x, a[2 * i + 1].y));
 #pragma unroll
       for (int i = 0; i < 4; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
       float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
       const Hif4Scale sc = hif4_scale(m1, levels);
       uint32_t lvbits = 0;  // bit i: lv2 of sub-block i (4), bit 4+j: lv3 of quarter j (8)
-      float qm4[8], ds4[8];
+      float2 qm4[8], ds4[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         uint32_t lv2 = 0, la = 0, lb = 0;
@@ -632,24 +646,31 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
         }
         lvbits |= (lv2 << i) | (la << (4 + 2 * i)) | (lb << (5 + 2 * i));
-        qm4[2 * i] = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + la)));
-        qm4[2 * i + 1] = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lb)));
-        ds4[2 * i] = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + la) - 2));
-        ds4[2 * i + 1] = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lb) - 2));
+        const float qa = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + la)));
+        const float qb = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lb)));
+        const float da = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + la) - 2));
+        const float db = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lb) - 2));
+        qm4[2 * i] = make_float2(qa, qa);
+        qm4[2 * i + 1] = make_float2(qb, qb);
+        ds4[2 * i] = make_float2(da, da);
+        ds4[2 * i + 1] = make_float2(db, db);
       }
       uint32_t packed[16];
       uint32_t nib[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float m = hif4_code4(a[i], qm4[i >> 2]);
-        const uint32_t neg = (sgn >> i) & 1u;
-        const uint32_t mag_bits = __float_as_uint(__fmul_rn(m, ds4[i >> 2]));
-        const uint32_t bf = (mag_bits >> 16) | (neg << 15);
-        if (i & 1)
-          packed[i >> 1] |= bf << 16;
-        else
-          packed[i >> 1] = bf;
-        if constexpr (CODES) nib[i >> 3] |= ((static_cast<uint32_t>(m) | (neg << 3)) << (4 * (i & 7)));
+      for (int q = 0; q < 16; ++q) {
+        // pair q = values 2q, 2q+1 of the 32, both in quarter q / 2
+        const float2 t = __fadd2_rn(__fmul2_rn(a[q], qm4[q >> 1]), make_float2(0.5f, 0.5f));
+        const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
+        float2 f = __fadd2_rn(r, make_float2(-8388608.0f, -8388608.0f));
+        f = make_float2(fminf(f.x, 7.0f), fminf(f.y, 7.0f));
+        const float2 mag = __fmul2_rn(f, ds4[q >> 1]);
+        packed[q] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[q];
+        if constexpr (CODES) {
+          const uint32_t na = static_cast<uint32_t>(f.x) | ((sgn[q] >> 12) & 8u);
+          const uint32_t nb = static_cast<uint32_t>(f.y) | ((sgn[q] >> 28) & 8u);
+          nib[q >> 2] |= (na | (nb << 4)) << (8 * (q & 3));
+        }
       }
       const int half = task & 1;
       uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
@@ -788,7 +809,7 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
                     (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
     if (v3) {
       const int warps3 = std::min(16, std::max(4, static_cast<int>(k / 1024)));
-      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + static_cast<size_t>(warps3) * 32 * 33 * 4;
+      const size_t smem3 = 16 + static_cast<size_t>(k) * 10 + static_cast<size_t>(warps3) * 32 * 34 * 4;
       if (smem3 <= 200 * 1024) {
         const int per_sm = std::max(1, std::min(8, static_cast<int>((224 * 1024) / (smem3 + 1024))));
         const int64_t blocks3 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
