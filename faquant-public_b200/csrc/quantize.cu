@@ -574,7 +574,15 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           }
         }
       }
-      uint16_t* out = s_out + (ch << 10) + lane;
+      // s_out is stored with the 16-byte chunk index c rotated in its low 2 bits by
+      // (c >> 3): chunk c of the row lives at (c & ~3) | ((c + (c >> 3)) & 3). Lane writes
+      // stay contiguous, and the quantization pass's 16-byte reads (4 consecutive chunks
+      // per thread) spread over all banks. For element 32 i + lane of a chunk the rotated
+      // low bits are ((lane >> 3) + (i >> 1)) & 3.
+      uint16_t* out = s_out + (ch << 10) + (lane & 7);
+      int rot8[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) rot8[r] = 8 * (((lane >> 3) + r) & 3);
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         float2 r;
@@ -587,8 +595,9 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           r = make_float2(__fadd_rn(__fdiv_rn(p[q].x, sq), 0.0f), __fadd_rn(__fdiv_rn(p[q].y, sq), 0.0f));
         }
         const __nv_bfloat162 b2 = __float22bfloat162_rn(r);
-        out[(2 * q) * 32] = __bfloat16_as_ushort(b2.x);
-        out[(2 * q + 1) * 32] = __bfloat16_as_ushort(b2.y);
+        // elements i = 2q and 2q + 1: both have i >> 1 == q
+        out[(2 * q) * 32 + rot8[q & 3]] = __bfloat16_as_ushort(b2.x);
+        out[(2 * q + 1) * 32 + rot8[q & 3]] = __bfloat16_as_ushort(b2.y);
       }
     }
     __syncthreads();
@@ -599,13 +608,16 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
         bulk_load(smem_addr(s_in + buf * row_bytes), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
       }
     }
-    // quantization: thread = 32 consecutive values; partner lane (tid ^ 1) holds the other half
+    // quantization: thread = 32 consecutive values; partner lane (tid ^ 1) holds the other half.
+    // Slot s (16 bytes = one sub-block of 8 values) of the thread holds logical sub-block
+    // qs = (s - (task >> 1)) & 3 because of the rotated layout above.
     for (int t0 = 0; t0 < tasks; t0 += blockDim.x) {
       const int task = t0 + tid;
       const bool live = task < tasks;
       const int col = (live ? task : 0) * 32;
+      const int rot = (task >> 1) & 3;
       uint32_t sgn[16];  // sign bits of each bf16 pair (no -0.0 here)
-      float2 a[16];      // |x| pairs
+      float2 a[16];      // |x| pairs, slot-major
       {
         const uint4* src = reinterpret_cast<const uint4*>(s_out + col);
 #pragma unroll
@@ -629,10 +641,11 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
       const Hif4Scale sc = hif4_scale(m1, levels);
-      uint32_t lvbits = 0;  // bit i: lv2 of sub-block i (4), bit 4+j: lv3 of quarter j (8)
+      uint32_t lvbits = 0;  // bit qs: lv2 of logical sub-block qs, bit 4+j: lv3 of logical quarter j
       float2 qm4[8], ds4[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
+        const int qs = (i - rot) & 3;
         uint32_t lv2 = 0, la = 0, lb = 0;
         if (levels == 123) {
           lv2 = __fmul_rn(m2[i], sc.rec) >= 4.0f;
@@ -645,7 +658,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           la = __fmul_rn(m3[2 * i], sc.rec) >= 2.0f;
           lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
         }
-        lvbits |= (lv2 << i) | (la << (4 + 2 * i)) | (lb << (5 + 2 * i));
+        lvbits |= (lv2 << qs) | (la << (4 + 2 * qs)) | (lb << (5 + 2 * qs));
         const float qa = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + la)));
         const float qb = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lb)));
         const float da = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + la) - 2));
@@ -659,7 +672,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       uint32_t nib[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        // pair q = values 2q, 2q+1 of the 32, both in quarter q / 2
+        // pair q = values 2q, 2q+1 of slot q / 4, both in its half q / 2
         const float2 t = __fadd2_rn(__fmul2_rn(a[q], qm4[q >> 1]), make_float2(0.5f, 0.5f));
         const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
         float2 f = __fadd2_rn(r, make_float2(-8388608.0f, -8388608.0f));
@@ -677,14 +690,18 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
       if (live) {
         if (o.qdq) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col);
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col;
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          for (int sl = 0; sl < 4; ++sl)
+            *reinterpret_cast<uint4*>(dst + 8 * ((sl - rot) & 3)) =
+                make_uint4(packed[4 * sl], packed[4 * sl + 1], packed[4 * sl + 2], packed[4 * sl + 3]);
         }
         if constexpr (CODES) {
-          if (o.codes)
-            *reinterpret_cast<uint4*>(o.codes + row * (k / 2) + col / 2) = make_uint4(nib[0], nib[1], nib[2], nib[3]);
+          if (o.codes) {
+            uint32_t* cdst = reinterpret_cast<uint32_t*>(o.codes + row * (k / 2) + col / 2);
+#pragma unroll
+            for (int sl = 0; sl < 4; ++sl) cdst[(sl - rot) & 3] = nib[sl];
+          }
         }
         if (o.meta && half == 0) o.meta[row * (k / 64) + task / 2] = mb | sc.code;
       }
