@@ -168,11 +168,19 @@ class FakeQuantLinear(nn.Module):
         if not x.is_cuda:
             raise RuntimeError("faquant_b200.FakeQuantLinear runs on CUDA tensors only")
         signs, perm, block = self._rotation()
+        # the reference moves its rotation buffers to the input's device per call (quantization.py:208-209)
+        if signs is not None and signs.device != x.device:
+            signs = signs.to(x.device)
+        if perm is not None and perm.device != x.device:
+            perm = perm.to(x.device)
+        scale = self.input_scale
+        if scale is not None and scale.device != x.device:
+            scale = scale.to(x.device)
         shape = x.shape
         qdq, _, _ = ops.hif4_quantize(
             x.reshape(-1, shape[-1]),
             levels=ops.default_levels("act"),
-            input_scale=self.input_scale,
+            input_scale=scale,
             signs=signs,
             permutation=perm,
             rot_block=block,

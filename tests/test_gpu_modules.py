@@ -176,7 +176,7 @@ def test_wan_hif4_linear_with_fused_reader_rotation() -> None:
     mod = HiF4Linear(lin, weight_qdq=faquant_qdq("123"), input_qdq=qdq, device=DEV).to(DEV)
     x = torch.randn(300, 5120, generator=torch.Generator().manual_seed(62))
     y = mod(x.to(DEV)).float().cpu().numpy()
-    ref = olin.fake_quant_linear(x.numpy(), mod.weight.float().cpu().numpy(), lin.bias.float().numpy(),
+    ref = olin.fake_quant_linear(x.numpy(), mod.weight.float().cpu().numpy(), lin.bias.detach().float().numpy(),
                                  levels="123", dtype="f32", signs=rot.signs.numpy(),
                                  permutation=rot.permutation.numpy(), block=64)
     assert np.all(np.abs(y - ref) <= 2.0**-8 * np.abs(ref) + 1e-3 * np.abs(ref).max())
