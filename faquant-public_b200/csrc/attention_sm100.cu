@@ -5,22 +5,25 @@
 // bottom-right causal mask, online softmax against the running max that includes
 // the current tile, P = exp(s - max) HiF4-quantized (unsigned) along the tile's keys
 // in two groups of 64, the denominator from the quantized P (P-Reordering) or the
-// raw P, O = alpha * O + P.V, out = O / denominator. Fully-future tiles are skipped
-// (bitwise identical, simulated_flash_attention.py:676-699).
+// raw P, O = alpha * O + P.V, out = O / denominator.
 //
-// One CTA per (128-query tile, q head, batch), 192 threads:
-//   warp 0      TMA producer: Q [128 x 128] once, then K and V tiles [128 x 128]
-//               (two 64-column 128-byte-swizzled chunks each) into a 2-stage ring;
-//   warp 1      TMEM allocation (512 columns: S0, S1, O) and the single MMA-issuing
-//               lane: S[j%2] = Q.K_j^T (M=N=128, 8 x K=16), then O += P_j.V_j with V
-//               as an MN-major operand; tcgen05.commit signals the consumers;
-//   warps 2..5  one query row per thread: tcgen05.ld of the S row, mask, running max,
-//               exp2, HiF4 quantization of both 64-key groups inside the thread, the
-//               row sum, P written to shared memory in the swizzled K-major layout the
-//               MMA reads, O rescaled in TMEM when the max moved (alpha != 1), and at
-//               the end O / denominator stored as bf16.
-// The QK^T of tile j+1 runs on the tensor cores while tile j is in softmax. Every wait
-// is bounded (common.cuh).
+// One CTA per (256 queries = two 128-query tiles A and B, q head, batch), 320 threads:
+//   warp 0      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
+//               64-column 128-byte-swizzled chunks each) into 2-stage rings;
+//   warp 1      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
+//               MMA-issuing lane: S_t = Q_t.K_j^T (SS form), O_t += P_t.V_j (TS form:
+//               P is read from tensor memory, written over the first 64 columns of
+//               S_t; V is an MN-major shared-memory operand);
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per
+//               thread: tcgen05.ld of the S row, mask, running max, exp2, HiF4
+//               quantization of both 64-key groups inside the thread on FP32x2 pairs,
+//               row sums, O rescaled in TMEM when the max moved (alpha == 1 is exact
+//               and skipped), P stored to TMEM as packed bf16, and at the end
+//               O / denominator stored as bf16.
+// The two tiles ping-pong: while the softmax warps of one tile work, the tensor core
+// runs the other tile's QK^T and PV. With causal masking both tiles walk the key tiles
+// of tile B; the extra tile of tile A is fully masked (P = 0, alpha = 1: no effect).
+// Every wait is bounded (common.cuh) and warp-uniform for whole-warp roles.
 #include <algorithm>
 
 #include "common.cuh"
@@ -30,29 +33,29 @@
 namespace faq {
 namespace attn {
 
-constexpr int BM = 128;   // queries per CTA
+constexpr int BM = 128;   // queries per tile
 constexpr int BN = 128;   // keys per tile
 constexpr int D = 128;    // head dim
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;
 constexpr int TILE_BYTES = BM * D * 2;      // 32 KB (two 16 KB chunks)
 constexpr int CHUNK_BYTES = 128 * 128;      // 128 rows x 128 B
 constexpr int KV_STAGES = 2;
 constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, false, false);
 constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, D, false, true);
 constexpr int TMEM_COLS = 512;
-constexpr int S_COL0 = 0, O_COL = 256;
-// smem: Q | K[2] | V[2] | P | barriers
+__device__ __forceinline__ uint32_t s_col(int t) { return t ? 128u : 0u; }
+__device__ __forceinline__ uint32_t o_col(int t) { return t ? 384u : 256u; }
+// smem: Q_A | Q_B | K[2] | V[2] | barriers
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;
+constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + KV_STAGES * TILE_BYTES;
-constexpr int OFF_P = OFF_V + KV_STAGES * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + BM * BN * 2;
+constexpr int OFF_BAR = OFF_V + KV_STAGES * TILE_BYTES;
 constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + 256;
 
 struct Params {
   int64_t sq, sk;
   int hq, hkv, group;  // group = hq / hkv
-  int m_tiles;
+  int m_tiles;         // CTAs along the queries (256 queries each)
   float scale_log2;    // scale * log2(e)
   int causal;
   int p_levels;        // 0: P not quantized
@@ -67,19 +70,18 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// HiF4 quantization (unsigned) of one 64-key group held by this thread, in place;
-// returns the sum of the quantized values. Same arithmetic as hif4_quant8.
-__device__ __forceinline__ float quantize_p64(float* p, int levels) {
+// HiF4 quantization (unsigned) of one 64-key group held by this thread as 32 float2
+// pairs, in place; returns the pair-sum of the quantized values. Same arithmetic as
+// hif4_quant8 (floor on the FP32 adder, single roundings, no fused multiply-add).
+__device__ __forceinline__ float2 quantize_p64(float2* p, int levels) {
   float m3[16], m2[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) m3[i] = fmaxf(fmaxf(p[4 * i], p[4 * i + 1]), fmaxf(p[4 * i + 2], p[4 * i + 3]));
+  for (int i = 0; i < 16; ++i) m3[i] = fmaxf(fmaxf(p[2 * i].x, p[2 * i].y), fmaxf(p[2 * i + 1].x, p[2 * i + 1].y));
 #pragma unroll
   for (int i = 0; i < 8; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
-  float m1 = m2[0];
-#pragma unroll
-  for (int i = 1; i < 8; ++i) m1 = fmaxf(m1, m2[i]);
+  const float m1 = fmaxf(fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3])), fmaxf(fmaxf(m2[4], m2[5]), fmaxf(m2[6], m2[7])));
   const Hif4Scale sc = hif4_scale(m1, levels);
-  float sum = 0.0f;
+  float2 sum = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     int lv2 = 0, lv3a = 0, lv3b = 0;
@@ -98,12 +100,16 @@ __device__ __forceinline__ float quantize_p64(float* p, int levels) {
     for (int h = 0; h < 2; ++h) {
       const int sh = lv2 + (h ? lv3b : lv3a);
       const float qm4 = __fmul_rn(sc.rec, pow2f(2 - sh));  // 4 * qm, exact
-      const float ds4 = __fmul_rn(sc.s, pow2f(sh - 2));
+      const float ds4 = __fmul_rn(sc.s, pow2f(sh - 2));    // ds / 4, exact
+      const float2 qm2 = make_float2(qm4, qm4), ds2 = make_float2(ds4, ds4);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        float& v = p[8 * i + 4 * h + t];
-        v = __fmul_rn(hif4_code4(v, qm4), ds4);
-        sum = __fadd_rn(sum, v);
+      for (int t = 0; t < 2; ++t) {
+        float2& v = p[4 * i + 2 * h + t];
+        const float2 y = __fadd2_rn(__fmul2_rn(v, qm2), make_float2(0.5f, 0.5f));
+        float2 f = __fadd2_rn(__fadd2_rz(y, make_float2(8388608.0f, 8388608.0f)), make_float2(-8388608.0f, -8388608.0f));
+        f = make_float2(fminf(f.x, 7.0f), fminf(f.y, 7.0f));
+        v = __fmul2_rn(f, ds2);
+        sum = __fadd2_rn(sum, v);
       }
     }
   }
@@ -121,21 +127,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
   uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
+  uint64_t* s_full = bars + 9;   // [2 tiles]
+  uint64_t* p_full = bars + 11;  // [2 tiles]
+  uint64_t* o_done = bars + 13;  // [2 tiles]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // longest causal rows first: the last query tile has the most key tiles
+  // longest causal rows first: the last query tiles have the most key tiles
   const int m_tile = p.causal ? (p.m_tiles - 1 - static_cast<int>(blockIdx.x)) : static_cast<int>(blockIdx.x);
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / p.group;
-  const int64_t q0 = static_cast<int64_t>(m_tile) * BM;
+  const int64_t q0 = static_cast<int64_t>(m_tile) * (2 * BM);
   const int64_t offset = p.sk - p.sq;  // bottom-right causal alignment
   int64_t kv_end = p.sk;
-  if (p.causal) kv_end = std::min<int64_t>(p.sk, q0 + BM - 1 + offset + 1);
+  if (p.causal) kv_end = std::min<int64_t>(p.sk, q0 + 2 * BM - 1 + offset + 1);
   const int n_tiles = kv_end <= 0 ? 0 : static_cast<int>((kv_end + BN - 1) / BN);
 
   if (threadIdx.x == 0) {
@@ -146,10 +151,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_addr(&v_full[i]), 1);
       mbar_init(smem_addr(&v_empty[i]), 1);
       mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&s_empty[i]), 4);
+      mbar_init(smem_addr(&p_full[i]), 4);
+      mbar_init(smem_addr(&o_done[i]), 1);
     }
-    mbar_init(smem_addr(p_full), 4);
-    mbar_init(smem_addr(o_done), 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
@@ -168,10 +172,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(smem_addr(q_full), TILE_BYTES);
-      for (int c = 0; c < 2; ++c)
-        tma_load_4d(smem_addr(base + OFF_Q + c * CHUNK_BYTES), &tmap_q, smem_addr(q_full), c * 64,
-                    static_cast<int>(q0), h, b);
+      mbar_arrive_expect_tx(smem_addr(q_full), 2 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t)
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(smem_addr(base + OFF_Q + t * TILE_BYTES + c * CHUNK_BYTES), &tmap_q, smem_addr(q_full), c * 64,
+                      static_cast<int>(q0 + t * BM), h, b);
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
@@ -202,161 +207,182 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0 && n_tiles > 0) {
       bool ok = mbar_wait_site(smem_addr(q_full), 0, 4, 0);
       const uint32_t q_base = smem_addr(base + OFF_Q);
-      auto issue_qk = [&](int j) -> bool {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait_site(smem_addr(&k_full[st]), ph, 5, j)) return false;
-        if (!mbar_wait_site(smem_addr(&s_empty[st]), ph ^ 1, 6, j)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_addr(base + OFF_K + st * TILE_BYTES);
-        const uint32_t d_tmem = tmem + S_COL0 + st * BN;
+      // S_t = Q_t . K_j^T
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t k_base = smem_addr(base + OFF_K + (j & 1) * TILE_BYTES);
+        const uint32_t qb = q_base + t * TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          tc_mma_f16(d_tmem, sw128_kmajor_desc(q_base + off), sw128_kmajor_desc(k_base + off), IDESC_QK, kk != 0);
+          tc_mma_f16(tmem + s_col(t), sw128_kmajor_desc(qb + off), sw128_kmajor_desc(k_base + off), IDESC_QK, kk != 0);
         }
-        tc_commit(smem_addr(&s_full[st]));
-        tc_commit(smem_addr(&k_empty[st]));
-        return true;
+        tc_commit(smem_addr(&s_full[t]));
       };
-      if (ok) ok = issue_qk(0);
+      // O_t += P_t . V_j, P_t from tensor memory (64 columns of packed bf16 over S_t)
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = smem_addr(base + OFF_V + (j & 1) * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          tc_mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8, sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES),
+                        IDESC_PV, (j | kk) != 0);
+        tc_commit(smem_addr(&o_done[t]));
+      };
+      if (ok) ok = mbar_wait_site(smem_addr(&k_full[0]), 0, 5, 0);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        issue_qk(1, 0);
+        tc_commit(smem_addr(&k_empty[0]));
+      }
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
         const int st = j & 1;
-        if (!mbar_wait_site(smem_addr(p_full), j & 1, 7, j)) break;
+        const bool next = j + 1 < n_tiles;
+        // tile A
+        if (!mbar_wait_site(smem_addr(&p_full[0]), j & 1, 7, j)) break;
         if (!mbar_wait_site(smem_addr(&v_full[st]), (j >> 1) & 1, 8, j)) break;
         tc_fence_after();
-        const uint32_t p_base = smem_addr(base + OFF_P);
-        const uint32_t v_base = smem_addr(base + OFF_V + st * TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          // A = P [128 q x 128 keys] K-major: chunk kk/4, +32 B per 16 keys
-          const uint32_t a_off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          // B = V [128 keys x 128 d] MN-major: 16 key rows = 2048 B per step
-          tc_mma_f16(tmem + O_COL, sw128_kmajor_desc(p_base + a_off), sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES),
-                     IDESC_PV, (j | kk) != 0);
+        issue_pv(0, j);
+        if (next) {
+          if (!mbar_wait_site(smem_addr(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, 5, j + 1)) break;
+          tc_fence_after();
+          issue_qk(0, j + 1);  // overwrites S_A after PV_A(j) read P_A from it (tcgen05.mma run in order)
         }
-        tc_commit(smem_addr(o_done));
+        // tile B
+        if (!mbar_wait_site(smem_addr(&p_full[1]), j & 1, 9, j)) break;
+        tc_fence_after();
+        issue_pv(1, j);
         tc_commit(smem_addr(&v_empty[st]));
+        if (next) {
+          issue_qk(1, j + 1);
+          tc_commit(smem_addr(&k_empty[(j + 1) & 1]));
+        }
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ softmax warps
+    // ------------------------------------------------------------ softmax warpgroups
+    const int t = warp >= 6 ? 1 : 0;              // query tile of this warpgroup
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;          // TMEM lane == query row in tile
-    const int64_t qpos = q0 + row;                // query index
+    const int row = quarter * 32 + lane;          // TMEM lane == query row in the tile
+    const int64_t qpos = q0 + t * BM + row;       // query index
     const int64_t anchor = qpos + offset;         // last visible key (causal)
+    const int64_t tile_first = q0 + t * BM + offset;  // smallest anchor of this tile
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_addr + s_col(t);
+    const uint32_t o_addr = tmem + lane_addr + o_col(t);
+    const float2 c2 = make_float2(p.scale_log2, p.scale_log2);
     float m_run = -INFINITY, l_run = 0.0f;
-    uint8_t* p_row = base + OFF_P + row * 128;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait_warp(smem_addr(&s_full[st]), (j >> 1) & 1, 9, j)) { ok = false; break; }
+      if (!mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j)) { ok = false; break; }
       tc_fence_after();
-      float s[BN];
+      float2 s[BN / 2];
       {
         uint32_t r0[32], r1[32], r2[32], r3[32];
-        const uint32_t sa = tmem + lane_addr + S_COL0 + st * BN;
-        tmem_ld32(sa, r0);
-        tmem_ld32(sa + 32, r1);
-        tmem_ld32(sa + 64, r2);
-        tmem_ld32(sa + 96, r3);
+        tmem_ld32(s_addr, r0);
+        tmem_ld32(s_addr + 32, r1);
+        tmem_ld32(s_addr + 64, r2);
+        tmem_ld32(s_addr + 96, r3);
         tc_wait_ld();
         reg_fence32(r0);
         reg_fence32(r1);
         reg_fence32(r2);
         reg_fence32(r3);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = __uint_as_float(r0[i]);
-          s[32 + i] = __uint_as_float(r1[i]);
-          s[64 + i] = __uint_as_float(r2[i]);
-          s[96 + i] = __uint_as_float(r3[i]);
+        for (int i = 0; i < 16; ++i) {
+          s[i] = __fmul2_rn(make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1])), c2);
+          s[16 + i] = __fmul2_rn(make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1])), c2);
+          s[32 + i] = __fmul2_rn(make_float2(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1])), c2);
+          s[48 + i] = __fmul2_rn(make_float2(__uint_as_float(r3[2 * i]), __uint_as_float(r3[2 * i + 1])), c2);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&s_empty[st]));
       // scores in the log2 domain; mask future / out-of-range keys
       const int64_t key0 = static_cast<int64_t>(j) * BN;
-      const bool need_mask = (key0 + BN > p.sk) || (p.causal && key0 + BN - 1 > q0 + offset);
+      const bool need_mask = (key0 + BN > p.sk) || (p.causal && key0 + BN - 1 > tile_first);
+      if (need_mask) {
+        const int64_t lim = p.causal ? std::min<int64_t>(anchor, p.sk - 1) : p.sk - 1;  // last visible key
+#pragma unroll
+        for (int i = 0; i < BN / 2; ++i) {
+          if (key0 + 2 * i > lim) s[i].x = -INFINITY;
+          if (key0 + 2 * i + 1 > lim) s[i].y = -INFINITY;
+        }
+      }
       float tmax = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        float t = __fmul_rn(s[i], p.scale_log2);
-        if (need_mask) {
-          const int64_t key = key0 + i;
-          if (key >= p.sk || (p.causal && key > anchor)) t = -INFINITY;
-        }
-        s[i] = t;
-        tmax = fmaxf(tmax, t);
-      }
+      for (int i = 0; i < BN / 2; ++i) tmax = fmaxf(tmax, fmaxf(s[i].x, s[i].y));
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = m_run == -INFINITY ? 0.0f : ex2(__fsub_rn(m_run, m_use));
-      float raw_sum = 0.0f;
+      const float2 mneg = make_float2(-m_use, -m_use);
+      const bool want_raw = !p.norm_quantized || p.p_levels == 0;
+      float2 raw = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        s[i] = ex2(__fsub_rn(s[i], m_use));
-        raw_sum = __fadd_rn(raw_sum, s[i]);
+      for (int i = 0; i < BN / 2; ++i) {
+        const float2 d = __fadd2_rn(s[i], mneg);
+        s[i] = make_float2(ex2(d.x), ex2(d.y));
+        if (want_raw) raw = __fadd2_rn(raw, s[i]);
       }
-      float q_sum = raw_sum;
-      if (p.p_levels != 0) q_sum = __fadd_rn(quantize_p64(s, p.p_levels), quantize_p64(s + 64, p.p_levels));
-      l_run = __fadd_rn(__fmul_rn(alpha, l_run), p.norm_quantized ? q_sum : raw_sum);
+      float tile_sum;
+      if (p.p_levels != 0) {
+        const float2 q0s = quantize_p64(s, p.p_levels);
+        const float2 q1s = quantize_p64(s + 32, p.p_levels);
+        tile_sum = p.norm_quantized ? __fadd_rn(__fadd_rn(q0s.x, q0s.y), __fadd_rn(q1s.x, q1s.y))
+                                    : __fadd_rn(raw.x, raw.y);
+      } else {
+        tile_sum = __fadd_rn(raw.x, raw.y);
+      }
+      l_run = __fadd_rn(__fmul_rn(alpha, l_run), tile_sum);
       m_run = m_new;
-      // P and O may be touched only after PV of the previous tile finished
+      // O and the P columns may be touched only after PV of the previous tile finished
       if (j > 0) {
-        if (!mbar_wait_warp(smem_addr(o_done), (j - 1) & 1, 10, j)) { ok = false; break; }
+        if (!mbar_wait_warp(smem_addr(&o_done[t]), (j - 1) & 1, 14 + t, j)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+          const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t r[32];
-            tmem_ld32(tmem + lane_addr + O_COL + c * 32, r);
+            tmem_ld32(o_addr + c * 32, r);
             tc_wait_ld();
             reg_fence32(r);
             float o[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __fmul_rn(__uint_as_float(r[i]), alpha);
-            tmem_st32(tmem + lane_addr + O_COL + c * 32, o);
+            for (int i = 0; i < 16; ++i) {
+              const float2 v = __fmul2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), a2);
+              o[2 * i] = v.x;
+              o[2 * i + 1] = v.y;
+            }
+            tmem_st32(o_addr + c * 32, o);
           }
-          tc_wait_st();
         }
       }
-      // P (bf16, exact for quantized values) into the 128-byte swizzled K-major layout
+      // P as packed bf16 (exact for quantized values) into the first 64 columns of S_t
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
+        float w[32];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float* v = s + c * 64 + u * 8;
-          uint32_t w[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const __nv_bfloat162 pr = __floats2bfloat162_rn(v[2 * t], v[2 * t + 1]);
-            w[t] = *reinterpret_cast<const uint32_t*>(&pr);
-          }
-          const int phys = u ^ (row & 7);
-          *reinterpret_cast<uint4*>(p_row + c * CHUNK_BYTES + phys * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int i = 0; i < 32; ++i) {
+          const __nv_bfloat162 pr = __float22bfloat162_rn(s[32 * c + i]);
+          w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
         }
+        tmem_st32(s_addr + c * 32, w);
       }
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(p_full));
+      if (lane == 0) mbar_arrive(smem_addr(&p_full[t]));
     }
-    if (ok && n_tiles > 0 && mbar_wait_warp(smem_addr(o_done), (n_tiles - 1) & 1, 11, n_tiles)) {
+    if (ok && n_tiles > 0 && mbar_wait_warp(smem_addr(&o_done[t]), (n_tiles - 1) & 1, 16 + t, n_tiles)) {
       tc_fence_after();
-      // tcgen05.ld is .sync.aligned: every lane of the warp loads, even the lanes of
-      // query rows past the end (a tile can end mid-warp); only the stores are predicated.
+      // tcgen05.ld is .sync.aligned: every lane loads, even the lanes of query rows
+      // past the end (a tile can end mid-warp); only the stores are predicated.
       const bool store = qpos < p.sq;
       __nv_bfloat16* dst = p.out + b * p.ob + (store ? qpos : 0) * p.os + static_cast<int64_t>(h) * p.oh;
       const bool has_mass = l_run > 0.0f;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_addr + O_COL + c * 32, r);
+        tmem_ld32(o_addr + c * 32, r);
         tc_wait_ld();
         reg_fence32(r);
         uint32_t w[16];
@@ -435,7 +461,7 @@ extern "C" int faq_hif4_attention(const void* q, const void* k, const void* v, i
   p.hq = static_cast<int>(hq);
   p.hkv = static_cast<int>(hkv);
   p.group = static_cast<int>(hq / hkv);
-  p.m_tiles = static_cast<int>((sq + BM - 1) / BM);
+  p.m_tiles = static_cast<int>((sq + 2 * BM - 1) / (2 * BM));
   p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
   p.causal = causal;
   p.p_levels = p_levels;
