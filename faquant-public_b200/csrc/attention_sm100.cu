@@ -7,15 +7,17 @@
 // in two groups of 64, the denominator from the quantized P (P-Reordering) or the
 // raw P, O = alpha * O + P.V, out = O / denominator.
 //
-// One CTA per (256 queries = two 128-query tiles A and B, q head, batch), 320 threads:
-//   warp 0      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
+// One CTA per (256 queries = two 128-query tiles A and B, q head, batch), 384 threads
+// in three warpgroups; setmaxnreg moves registers from the third to the first two
+// (launch 168 x 384 = 224 x 256 + 56 x 128, exactly):
+//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B (224 registers);
+//   warp 8      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
 //               64-column 128-byte-swizzled chunks each) into 2-stage rings;
-//   warp 1      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
+//   warp 9      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
 //               MMA-issuing lane: S_t = Q_t.K_j^T (SS form), O_t += P_t.V_j (TS form:
 //               P is read from tensor memory, written over the first 64 columns of
-//               S_t; V is an MN-major shared-memory operand);
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per
-//               thread: tcgen05.ld of the S row, mask, running max, exp2, HiF4
+//               S_t; V is an MN-major shared-memory operand); warps 10, 11 idle;
+//   softmax     one query row per thread: tcgen05.ld of the S row, mask, running max, exp2, HiF4
 //               quantization of both 64-key groups inside the thread on FP32x2 pairs,
 //               row sums, O rescaled in TMEM when the max moved (alpha == 1 is exact
 //               and skipped), P stored to TMEM as packed bf16, and at the end
@@ -36,7 +38,8 @@ namespace attn {
 constexpr int BM = 128;   // queries per tile
 constexpr int BN = 128;   // keys per tile
 constexpr int D = 128;    // head dim
-constexpr int THREADS = 320;
+constexpr int THREADS = 384;
+constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
 constexpr int TILE_BYTES = BM * D * 2;      // 32 KB (two 16 KB chunks)
 constexpr int CHUNK_BYTES = 128 * 128;      // 128 rows x 128 B
 constexpr int KV_STAGES = 2;
@@ -70,27 +73,29 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// HiF4 quantization (unsigned) of one 64-key group held by this thread as 32 float2
-// pairs, in place; returns the pair-sum of the quantized values. Same arithmetic as
-// hif4_quant8 (floor on the FP32 adder, single roundings, no fused multiply-add).
-__device__ __forceinline__ float2 quantize_p64(float2* p, int levels) {
+// HiF4 quantization (unsigned) of one 64-key group held by this thread (f[0..63]), in
+// place; returns the sum of the quantized values. Same arithmetic as hif4_quant8 (floor
+// on the FP32 adder, single roundings, no fused multiply-add), on FP32x2 pairs, with the
+// maxima and the sum as trees so the dependency chains stay short.
+template <int LEVELS>
+__device__ __forceinline__ float quantize_p64(float* f) {
   float m3[16], m2[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) m3[i] = fmaxf(fmaxf(p[2 * i].x, p[2 * i].y), fmaxf(p[2 * i + 1].x, p[2 * i + 1].y));
+  for (int i = 0; i < 16; ++i) m3[i] = fmaxf(fmaxf(f[4 * i], f[4 * i + 1]), fmaxf(f[4 * i + 2], f[4 * i + 3]));
 #pragma unroll
   for (int i = 0; i < 8; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
   const float m1 = fmaxf(fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3])), fmaxf(fmaxf(m2[4], m2[5]), fmaxf(m2[6], m2[7])));
-  const Hif4Scale sc = hif4_scale(m1, levels);
-  float2 sum = make_float2(0.0f, 0.0f);
+  const Hif4Scale sc = hif4_scale(m1, LEVELS);
+  float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     int lv2 = 0, lv3a = 0, lv3b = 0;
-    if (levels == 123) {
+    if constexpr (LEVELS == 123) {
       lv2 = __fmul_rn(m2[i], sc.rec) >= 4.0f;
       const float thr = lv2 ? 4.0f : 2.0f;
       lv3a = __fmul_rn(m3[2 * i], sc.rec) >= thr;
       lv3b = __fmul_rn(m3[2 * i + 1], sc.rec) >= thr;
-    } else if (levels == 12) {
+    } else if constexpr (LEVELS == 12) {
       lv2 = __fmul_rn(m2[i], sc.rec) >= 2.0f;
     } else {
       lv3a = __fmul_rn(m3[2 * i], sc.rec) >= 2.0f;
@@ -104,18 +109,24 @@ __device__ __forceinline__ float2 quantize_p64(float2* p, int levels) {
       const float2 qm2 = make_float2(qm4, qm4), ds2 = make_float2(ds4, ds4);
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        float2& v = p[4 * i + 2 * h + t];
-        const float2 y = __fadd2_rn(__fmul2_rn(v, qm2), make_float2(0.5f, 0.5f));
-        float2 f = __fadd2_rn(__fadd2_rz(y, make_float2(8388608.0f, 8388608.0f)), make_float2(-8388608.0f, -8388608.0f));
-        f = make_float2(fminf(f.x, 7.0f), fminf(f.y, 7.0f));
-        v = __fmul2_rn(f, ds2);
-        sum = __fadd2_rn(sum, v);
+        float* v = f + 8 * i + 4 * h + 2 * t;
+        const float2 y = __fadd2_rn(__fmul2_rn(make_float2(v[0], v[1]), qm2), make_float2(0.5f, 0.5f));
+        float2 c = __fadd2_rn(__fadd2_rz(y, make_float2(8388608.0f, 8388608.0f)), make_float2(-8388608.0f, -8388608.0f));
+        c = make_float2(fminf(c.x, 7.0f), fminf(c.y, 7.0f));
+        const float2 q = __fmul2_rn(c, ds2);
+        v[0] = q.x;
+        v[1] = q.y;
+        part[(2 * h + t)] = __fadd2_rn(part[2 * h + t], q);
       }
     }
   }
-  return sum;
+  const float2 s01 = __fadd2_rn(part[0], part[1]), s23 = __fadd2_rn(part[2], part[3]);
+  const float2 s = __fadd2_rn(s01, s23);
+  return __fadd_rn(s.x, s.y);
 }
 
+// PLEV: HiF4 levels of P (0 = P not quantized); RAW: the denominator sums the raw P
+template <int PLEV, bool RAW>
 __global__ void __launch_bounds__(THREADS, 1)
     hif4_attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                           const __grid_constant__ CUtensorMap tmap_v, Params p) {
@@ -159,7 +170,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tmem_alloc(smem_addr(tmem_slot), TMEM_COLS);
     tmem_relinquish();
   }
@@ -167,8 +178,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
+  // Register split by warpgroup. The setmaxnreg of a role sits at the top of that
+  // role's own branch: code after a merge point is compiled for the smaller budget.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+    if (warp == PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
       bool ok = true;
@@ -202,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+    } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       bool ok = mbar_wait_site(smem_addr(q_full), 0, 4, 0);
@@ -211,7 +225,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto issue_qk = [&](int t, int j) {
         const uint32_t k_base = smem_addr(base + OFF_K + (j & 1) * TILE_BYTES);
         const uint32_t qb = q_base + t * TILE_BYTES;
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
           tc_mma_f16(tmem + s_col(t), sw128_kmajor_desc(qb + off), sw128_kmajor_desc(k_base + off), IDESC_QK, kk != 0);
@@ -221,7 +235,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // O_t += P_t . V_j, P_t from tensor memory (64 columns of packed bf16 over S_t)
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_base = smem_addr(base + OFF_V + (j & 1) * TILE_BYTES);
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < BN / 16; ++kk)
           tc_mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8, sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES),
                         IDESC_PV, (j | kk) != 0);
@@ -259,9 +273,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
+    }  // warps 10 and 11 have no role
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
     // ------------------------------------------------------------ softmax warpgroups
-    const int t = warp >= 6 ? 1 : 0;              // query tile of this warpgroup
+    const int t = warp >> 2;                      // query tile of this warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;          // TMEM lane == query row in the tile
     const int64_t qpos = q0 + t * BM + row;       // query index
@@ -276,60 +292,64 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j)) { ok = false; break; }
       tc_fence_after();
-      float2 s[BN / 2];
-      {
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(s_addr, r0);
-        tmem_ld32(s_addr + 32, r1);
-        tmem_ld32(s_addr + 64, r2);
-        tmem_ld32(s_addr + 96, r3);
-        tc_wait_ld();
-        reg_fence32(r0);
-        reg_fence32(r1);
-        reg_fence32(r2);
-        reg_fence32(r3);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          s[i] = __fmul2_rn(make_float2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1])), c2);
-          s[16 + i] = __fmul2_rn(make_float2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1])), c2);
-          s[32 + i] = __fmul2_rn(make_float2(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1])), c2);
-          s[48 + i] = __fmul2_rn(make_float2(__uint_as_float(r3[2 * i]), __uint_as_float(r3[2 * i + 1])), c2);
-        }
-      }
+      float f[BN];  // the S row, then P, in place
+      tmem_ld32f(s_addr, f);
+      tmem_ld32f(s_addr + 32, f + 32);
+      tmem_ld32f(s_addr + 64, f + 64);
+      tmem_ld32f(s_addr + 96, f + 96);
+      tc_wait_ld();
+      reg_fence32f(f);
+      reg_fence32f(f + 32);
+      reg_fence32f(f + 64);
+      reg_fence32f(f + 96);
       // scores in the log2 domain; mask future / out-of-range keys
       const int64_t key0 = static_cast<int64_t>(j) * BN;
       const bool need_mask = (key0 + BN > p.sk) || (p.causal && key0 + BN - 1 > tile_first);
-      if (need_mask) {
-        const int64_t lim = p.causal ? std::min<int64_t>(anchor, p.sk - 1) : p.sk - 1;  // last visible key
+      const int lim = need_mask ? static_cast<int>(std::max<int64_t>(
+                                      -1, std::min<int64_t>(BN - 1, (p.causal ? std::min<int64_t>(anchor, p.sk - 1)
+                                                                             : p.sk - 1) - key0)))
+                                : BN - 1;  // last visible key of the tile, relative
+      float mx[8];
 #pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
-          if (key0 + 2 * i > lim) s[i].x = -INFINITY;
-          if (key0 + 2 * i + 1 > lim) s[i].y = -INFINITY;
+      for (int g = 0; g < 8; ++g) mx[g] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) {
+        float2 v = __fmul2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2);
+        if (need_mask) {
+          if (2 * i > lim) v.x = -INFINITY;
+          if (2 * i + 1 > lim) v.y = -INFINITY;
         }
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
+        mx[i & 7] = fmaxf(mx[i & 7], fmaxf(v.x, v.y));
       }
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BN / 2; ++i) tmax = fmaxf(tmax, fmaxf(s[i].x, s[i].y));
+      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float m_new = fmaxf(m_run, tmax);
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = m_run == -INFINITY ? 0.0f : ex2(__fsub_rn(m_run, m_use));
       const float2 mneg = make_float2(-m_use, -m_use);
-      const bool want_raw = !p.norm_quantized || p.p_levels == 0;
-      float2 raw = make_float2(0.0f, 0.0f);
+      float2 raw[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < BN / 2; ++i) {
-        const float2 d = __fadd2_rn(s[i], mneg);
-        s[i] = make_float2(ex2(d.x), ex2(d.y));
-        if (want_raw) raw = __fadd2_rn(raw, s[i]);
+        const float2 d = __fadd2_rn(make_float2(f[2 * i], f[2 * i + 1]), mneg);
+        const float2 e = make_float2(ex2(d.x), ex2(d.y));
+        f[2 * i] = e.x;
+        f[2 * i + 1] = e.y;
+        if constexpr (RAW) raw[i & 3] = __fadd2_rn(raw[i & 3], e);
       }
       float tile_sum;
-      if (p.p_levels != 0) {
-        const float2 q0s = quantize_p64(s, p.p_levels);
-        const float2 q1s = quantize_p64(s + 32, p.p_levels);
-        tile_sum = p.norm_quantized ? __fadd_rn(__fadd_rn(q0s.x, q0s.y), __fadd_rn(q1s.x, q1s.y))
-                                    : __fadd_rn(raw.x, raw.y);
+      if constexpr (PLEV != 0) {
+        const float qs0 = quantize_p64<PLEV>(f);
+        const float qs1 = quantize_p64<PLEV>(f + 64);
+        if constexpr (RAW) {
+          const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
+          tile_sum = __fadd_rn(r.x, r.y);
+        } else {
+          tile_sum = __fadd_rn(qs0, qs1);
+        }
       } else {
-        tile_sum = __fadd_rn(raw.x, raw.y);
+        const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
+        tile_sum = __fadd_rn(r.x, r.y);
       }
       l_run = __fadd_rn(__fmul_rn(alpha, l_run), tile_sum);
       m_run = m_new;
@@ -341,18 +361,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(o_addr + c * 32, r);
-            tc_wait_ld();
-            reg_fence32(r);
             float o[32];
+            tmem_ld32f(o_addr + c * 32, o);
+            tc_wait_ld();
+            reg_fence32f(o);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float2 v = __fmul2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), a2);
+              const float2 v = __fmul2_rn(make_float2(o[2 * i], o[2 * i + 1]), a2);
               o[2 * i] = v.x;
               o[2 * i + 1] = v.y;
             }
-            tmem_st32(o_addr + c * 32, o);
+            tmem_st32f(o_addr + c * 32, o);
           }
         }
       }
@@ -362,10 +381,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         float w[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const __nv_bfloat162 pr = __float22bfloat162_rn(s[32 * c + i]);
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[64 * c + 2 * i], f[64 * c + 2 * i + 1]);
           w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
         }
-        tmem_st32(s_addr + c * 32, w);
+        tmem_st32f(s_addr + c * 32, w);
       }
       tc_wait_st();
       tc_fence_before();
@@ -407,7 +426,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -470,9 +489,14 @@ extern "C" int faq_hif4_attention(const void* q, const void* k, const void* v, i
   p.ob = ob;
   p.os = os;
   p.oh = oh;
-  FAQ_CUDA(cudaFuncSetAttribute(hif4_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(SMEM_BYTES)));
+  const bool raw = !normalizer_quantized || p_levels == 0;
+  auto kern = hif4_attention_kernel<123, false>;
+  if (p_levels == 123) kern = raw ? hif4_attention_kernel<123, true> : hif4_attention_kernel<123, false>;
+  else if (p_levels == 12) kern = raw ? hif4_attention_kernel<12, true> : hif4_attention_kernel<12, false>;
+  else if (p_levels == 13) kern = raw ? hif4_attention_kernel<13, true> : hif4_attention_kernel<13, false>;
+  else kern = hif4_attention_kernel<0, true>;
+  FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES)));
   dim3 grid(p.m_tiles, static_cast<unsigned>(hq), static_cast<unsigned>(batch));
-  hif4_attention_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return launch_status("hif4_attention_kernel");
 }
