@@ -67,6 +67,12 @@ struct Params {
   int64_t ob, os, oh;
 };
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -74,9 +80,12 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // HiF4 quantization (unsigned) of one 64-key group held by this thread (f[0..63]), in
-// place; returns the sum of the quantized values. Same arithmetic as hif4_quant8 (floor
-// on the FP32 adder, single roundings, no fused multiply-add), on FP32x2 pairs, with the
-// maxima and the sum as trees so the dependency chains stay short.
+// place; returns the sum of the quantized values. The same arithmetic as hif4_quant8,
+// rearranged only where exact, on FP32x2 pairs:
+//   t = min(fl(fl(p * 4qm) + 0.5), 7.5)      (== the reference's clamp of the code to 7)
+//   r = t + 2^23 rounded toward zero          (== 2^23 + floor(t))
+//   q = fma(r, ds/4, -2^23 * ds/4)           (exact: the result code * ds/4 has <= 6 bits)
+// Maxima and the sum are trees, so the dependency chains stay short.
 template <int LEVELS>
 __device__ __forceinline__ float quantize_p64(float* f) {
   float m3[16], m2[8];
@@ -107,16 +116,17 @@ __device__ __forceinline__ float quantize_p64(float* f) {
       const float qm4 = __fmul_rn(sc.rec, pow2f(2 - sh));  // 4 * qm, exact
       const float ds4 = __fmul_rn(sc.s, pow2f(sh - 2));    // ds / 4, exact
       const float2 qm2 = make_float2(qm4, qm4), ds2 = make_float2(ds4, ds4);
+      const float2 off2 = make_float2(-8388608.0f * ds4, -8388608.0f * ds4);
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         float* v = f + 8 * i + 4 * h + 2 * t;
-        const float2 y = __fadd2_rn(__fmul2_rn(make_float2(v[0], v[1]), qm2), make_float2(0.5f, 0.5f));
-        float2 c = __fadd2_rn(__fadd2_rz(y, make_float2(8388608.0f, 8388608.0f)), make_float2(-8388608.0f, -8388608.0f));
-        c = make_float2(fminf(c.x, 7.0f), fminf(c.y, 7.0f));
-        const float2 q = __fmul2_rn(c, ds2);
+        float2 y = __fadd2_rn(__fmul2_rn(make_float2(v[0], v[1]), qm2), make_float2(0.5f, 0.5f));
+        y = make_float2(fminf(y.x, 7.5f), fminf(y.y, 7.5f));
+        const float2 r = __fadd2_rz(y, make_float2(8388608.0f, 8388608.0f));
+        const float2 q = __ffma2_rn(r, ds2, off2);
         v[0] = q.x;
         v[1] = q.y;
-        part[(2 * h + t)] = __fadd2_rn(part[2 * h + t], q);
+        part[2 * h + t] = __fadd2_rn(part[2 * h + t], q);
       }
     }
   }
@@ -302,36 +312,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       reg_fence32f(f + 32);
       reg_fence32f(f + 64);
       reg_fence32f(f + 96);
-      // scores in the log2 domain; mask future / out-of-range keys
+      // mask future / out-of-range keys; the row max is taken on the raw scores (the
+      // scale is positive, so max(fl(s * c)) == fl(max(s) * c))
       const int64_t key0 = static_cast<int64_t>(j) * BN;
       const bool need_mask = (key0 + BN > p.sk) || (p.causal && key0 + BN - 1 > tile_first);
-      const int lim = need_mask ? static_cast<int>(std::max<int64_t>(
-                                      -1, std::min<int64_t>(BN - 1, (p.causal ? std::min<int64_t>(anchor, p.sk - 1)
-                                                                             : p.sk - 1) - key0)))
-                                : BN - 1;  // last visible key of the tile, relative
+      if (need_mask) {
+        const int lim = static_cast<int>(std::max<int64_t>(
+            -1, std::min<int64_t>(BN - 1, (p.causal ? std::min<int64_t>(anchor, p.sk - 1) : p.sk - 1) - key0)));
+#pragma unroll
+        for (int i = 0; i < BN; ++i)
+          if (i > lim) f[i] = -INFINITY;
+      }
       float mx[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) mx[g] = -INFINITY;
+      for (int g = 0; g < 8; ++g) mx[g] = fmax3(f[16 * g], f[16 * g + 1], f[16 * g + 2]);
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
-        float2 v = __fmul2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2);
-        if (need_mask) {
-          if (2 * i > lim) v.x = -INFINITY;
-          if (2 * i + 1 > lim) v.y = -INFINITY;
-        }
-        f[2 * i] = v.x;
-        f[2 * i + 1] = v.y;
-        mx[i & 7] = fmaxf(mx[i & 7], fmaxf(v.x, v.y));
+      for (int g = 0; g < 8; ++g) {
+#pragma unroll
+        for (int i = 3; i < 15; i += 2) mx[g] = fmax3(mx[g], f[16 * g + i], f[16 * g + i + 1]);
+        mx[g] = fmaxf(mx[g], f[16 * g + 15]);
       }
-      const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_new = fmaxf(m_run, tmax);
+      const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float m_new = fmaxf(m_run, __fmul_rn(tmax, p.scale_log2));  // log2 domain
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = m_run == -INFINITY ? 0.0f : ex2(__fsub_rn(m_run, m_use));
       const float2 mneg = make_float2(-m_use, -m_use);
       float2 raw[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int i = 0; i < BN / 2; ++i) {
-        const float2 d = __fadd2_rn(make_float2(f[2 * i], f[2 * i + 1]), mneg);
+        const float2 d = __ffma2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2, mneg);  // s * c - m, one rounding
         const float2 e = make_float2(ex2(d.x), ex2(d.y));
         f[2 * i] = e.x;
         f[2 * i + 1] = e.y;

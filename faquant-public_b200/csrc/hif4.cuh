@@ -30,18 +30,29 @@ struct Hif4Scale {
   uint32_t code;  // (e + 48) << 2 | t
 };
 
+// The E6M2 rounding and the reciprocal work on the bit pattern of the clamped scale
+// (a positive normal float, low 16 bits zero after the bf16 rounding):
+//  * rint(s * 2^(2-e)) * 2^(e-2) keeps two mantissa bits with round-half-to-even; an
+//    integer add of 2^20 - 1 + (bit 21) followed by clearing bits 0..20 does exactly
+//    that, and a carry out of the mantissa is the reference's move to the next octave.
+//  * s = m * 2^e with m in {1, 1.25, 1.5, 1.75}, so bf16(fp32(1/s)) = bf16(fp32(1/m)) *
+//    2^-e exactly (both roundings commute with power-of-two scaling in the normal range,
+//    and 1/s stays in [2^-16, 2^48]). bf16(fp32(1/m)) for the four mantissas is
+//    0x3F80 (1), 0x3F4D (fp32 0x3F4CCCCD rounded up), 0x3F2B (0x3F2AAAAB up) and
+//    0x3F12 (0x3F124925 down); the exponent is then lowered by e.
+//  * the E6M2 code (e + 48) << 2 | t is the top bits of the pattern minus (127-48) << 2.
 __device__ __forceinline__ Hif4Scale hif4_scale(float max64, int levels) {
   float s = bf16_round(__fmul_rn(max64, divisor_reciprocal(levels)));
   s = fminf(fmaxf(s, 3.552713678800501e-15f), 49152.0f);  // [2^-48, 49152]
-  int e = exponent_of(s);
-  const float q = rintf(__fmul_rn(s, pow2f(2 - e)));  // exact scaling, rint half-to-even
-  s = __fmul_rn(q, pow2f(e - 2));
-  e = exponent_of(s);  // q == 8 moves to the next octave
-  const uint32_t t = static_cast<uint32_t>(__fmul_rn(s, pow2f(2 - e))) - 4u;
+  uint32_t b = __float_as_uint(s);
+  b = (b + 0x000FFFFFu + ((b >> 21) & 1u)) & 0xFFE00000u;
+  const uint32_t t = (b >> 21) & 3u;
+  // bytes 2t, 2t+1 of the table {0x3F123F2B : 0x3F4D3F80} are bf16(fp32(1/m_t))
+  const uint32_t rb = __byte_perm(0x3F4D3F80u, 0x3F123F2Bu, 34u * t + 16u) << 16;
   Hif4Scale r;
-  r.s = s;
-  r.rec = bf16_round(__fdiv_rn(1.0f, s));
-  r.code = (static_cast<uint32_t>(e + 48) << 2) | t;
+  r.s = __uint_as_float(b);
+  r.rec = __uint_as_float(rb - (b & 0x7F800000u) + 0x3F800000u);
+  r.code = (b >> 21) - ((127u - 48u) << 2);
   return r;
 }
 

@@ -450,9 +450,13 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 //   - butterflies (the reference's stage order, rotation.py:22-28): stride 1 inside a
 //     float2, strides 2..16 on float2 pairs (packed FP32x2 adds), a 32x34 shared-memory
 //     transpose, then strides 32..block/2 the same way;
-//   - normalization by an exact power of two as ffma2(v, 2^-k, +0), which also maps
-//     -0.0 to +0.0; that changes no output (the reference's sign(-0.0) is 0) and lets
-//     the quantization pass copy sign bits instead of comparing;
+//   - normalization by an exact power of two as one ffma2(v, 2^-k, +0) per pair: the
+//     reference's correctly rounded division, subnormals included, up to the sign of a
+//     zero, which the quantization below does not look at;
+//   - the quantization pass takes sign bits from the bf16 pattern, cleared where the
+//     magnitude is zero: a -0.0 (an input zero, an underflow of the scaling, or a tiny
+//     negative value rounded to zero in bf16) quantizes to +0 as the reference's
+//     sign(-0.0) == 0 does;
 //   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
 //     block maximum, per-4/per-8 maxima in registers, the element code on FP32x2.
 __device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
@@ -588,7 +592,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
         float2 r;
         if constexpr ((LOG2B & 1) == 0) {
           const float c = pow2f(-(LOG2B / 2));
-          r = __ffma2_rn(p[q], make_float2(c, c), make_float2(0.0f, 0.0f));  // exact; -0 -> +0
+          r = __ffma2_rn(p[q], make_float2(c, c), make_float2(0.0f, 0.0f));  // == p / 2^(LOG2B/2)
         } else {
           const float sq = static_cast<float>(LOG2B == 5 ? 5.656854249492381 : LOG2B == 7 ? 11.313708498984761
                                                 : 22.627416997969522);
@@ -616,7 +620,7 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       const bool live = task < tasks;
       const int col = (live ? task : 0) * 32;
       const int rot = (task >> 1) & 3;
-      uint32_t sgn[16];  // sign bits of each bf16 pair (no -0.0 here)
+      uint32_t sgn[16];  // sign bits of each bf16 pair, clear on a zero half
       float2 a[16];      // |x| pairs, slot-major
       {
         const uint4* src = reinterpret_cast<const uint4*>(s_out + col);
@@ -627,8 +631,10 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             const uint32_t w = w4[h];
-            sgn[4 * q + h] = w & 0x80008000u;
             const uint32_t m = w & 0x7FFF7FFFu;
+            // bit 15 of each half of m + 0x7FFF is set iff that half's magnitude is nonzero
+            // (no carry crosses the halves: 0x7FFF + 0x7FFF < 2^16)
+            sgn[4 * q + h] = w & (m + 0x7FFF7FFFu) & 0x80008000u;
             a[4 * q + h] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
           }
         }

@@ -131,6 +131,36 @@ def test_config1_activation_path_full_size() -> None:
     assert np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
 
 
+@pytest.mark.parametrize("levels", ["123", "12", "13"])
+def test_scale_sweep_every_bf16_block_maximum(levels: str) -> None:
+    """One 64-block per positive finite bf16 value v (subnormals to the largest), holding
+    +-v and values below it: every E6M2 scale, reciprocal and lv2/lv3 decision the bf16
+    grid can reach, both clamp ends included, bit-exact -- directly, and through the
+    rotated bf16 path for the blocks whose 1024-point Hadamard cannot overflow."""
+    ops = _ops()
+    rng = np.random.default_rng(77)
+    v = (np.arange(1, 0x7F80, dtype=np.uint32) << 16).view(np.float32)
+    n = v.size
+    blocks = rng.uniform(-1, 1, (n, 64)).astype(np.float32) * v[:, None]
+    blocks[np.arange(n), rng.integers(0, 64, n)] = v * rng.choice([-1, 1], n).astype(np.float32)
+    blocks = np.concatenate([blocks, np.zeros((-n % 16, 64), np.float32)])
+    x = oh.bf16_round(blocks).reshape(-1, 1024)
+    qdq, codes, meta = ops.hif4_quantize(torch.from_numpy(x).to(torch.bfloat16).to(DEV), levels=levels,
+                                         want_codes=True)
+    ocodes, ometa = oh.hif4_encode(x, levels)
+    assert np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
+    assert np.array_equal(codes.cpu().numpy(), ocodes)
+    assert np.array_equal(_bits(qdq), oh.f32_to_bf16_bits(oh.fake_quantize(x, levels)))
+    q32, _, _ = ops.hif4_quantize(torch.from_numpy(x).to(DEV), levels=levels)
+    assert np.array_equal(_bits(q32), oh.fake_quantize(x, levels).view(np.uint32))
+    safe = x[np.abs(x).max(axis=1) < 1e30]
+    signs = rng.choice([-1, 1], 1024).astype(np.int8)
+    rq, _, _ = ops.hif4_quantize(torch.from_numpy(safe).to(torch.bfloat16).to(DEV), levels=levels,
+                                 signs=torch.from_numpy(signs).to(DEV), rot_block=1024)
+    expect = olin.quantize_activations(safe, levels=levels, dtype="bf16", signs=signs, block=1024)
+    assert np.array_equal(_bits(rq), oh.f32_to_bf16_bits(expect))
+
+
 def test_input_scale_strided_rows_and_empty() -> None:
     ops = _ops()
     rng = np.random.default_rng(5)
