@@ -7,21 +7,27 @@
 // in two groups of 64, the denominator from the quantized P (P-Reordering) or the
 // raw P, O = alpha * O + P.V, out = O / denominator.
 //
-// One CTA per (256 queries = two 128-query tiles A and B, q head, batch), 384 threads
-// in three warpgroups; setmaxnreg moves registers from the third to the first two
-// (launch 168 x 384 = 224 x 256 + 56 x 128, exactly):
-//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B (224 registers);
-//   warp 8      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
-//               64-column 128-byte-swizzled chunks each) into 2-stage rings;
-//   warp 9      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
-//               MMA-issuing lane: S_t = Q_t.K_j^T (SS form), O_t += P_t.V_j (TS form:
-//               P is read from tensor memory, written over the first 64 columns of
-//               S_t; V is an MN-major shared-memory operand); warps 10, 11 idle;
-//   softmax     one query row per thread: tcgen05.ld of the S row, mask, running max, exp2, HiF4
-//               quantization of both 64-key groups inside the thread on FP32x2 pairs,
-//               row sums, O rescaled in TMEM when the max moved (alpha == 1 is exact
-//               and skipped), P stored to TMEM as packed bf16, and at the end
-//               O / denominator stored as bf16.
+// One CTA per (256 queries = two 128-query tiles A and B, q head, batch), 640 threads
+// in five warpgroups; setmaxnreg moves registers from the fifth to the first four
+// (launch 96 x 640 = 112 x 512 + 32 x 128, exactly):
+//   warps 0..7   softmax of tile A, warps 8..15 softmax of tile B; within a tile the
+//                first four warps take keys 0..63 of every key tile and the other four
+//                keys 64..127 -- one HiF4 group each -- for the same query rows (a
+//                warp reaches the tensor-memory lanes 32 (warp % 4) .. + 31);
+//   warp 16      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
+//                64-column 128-byte-swizzled chunks each) into 2-stage rings;
+//   warp 17      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
+//                MMA-issuing lane: S_t = Q_t.K_j^T (SS form), O_t += P_t.V_j (TS form:
+//                P is read from tensor memory, V is an MN-major shared-memory operand);
+//                warps 18, 19 have no role.
+// Softmax, per key tile and query row, split over the two key halves: tcgen05.ld of the
+// half row of S, mask, partial max; the halves swap partial maxima through shared
+// memory behind a named barrier (which also ANDs their wait results, so a timed-out
+// wait ends both halves at the same iteration); exp2, HiF4 quantization of the half's
+// 64-key group on FP32x2 pairs, a running sum per half (same maxima, so the two sums
+// add up at the end), this half's 64 columns of O rescaled when the max moved (alpha ==
+// 1 is exact and skipped), P stored as packed bf16 over the half's first 32 S columns
+// (keys 64h + 2c, 64h + 2c + 1 in column 64h + c), and at the end O / (sum_0 + sum_1).
 // The two tiles ping-pong: while the softmax warps of one tile work, the tensor core
 // runs the other tile's QK^T and PV. With causal masking both tiles walk the key tiles
 // of tile B; the extra tile of tile A is fully masked (P = 0, alpha = 1: no effect).
@@ -38,8 +44,9 @@ namespace attn {
 constexpr int BM = 128;   // queries per tile
 constexpr int BN = 128;   // keys per tile
 constexpr int D = 128;    // head dim
-constexpr int THREADS = 384;
-constexpr int PRODUCER_WARP = 8, MMA_WARP = 9;
+constexpr int THREADS = 640;
+constexpr int SOFTMAX_WARPS = 16;
+constexpr int PRODUCER_WARP = 16, MMA_WARP = 17;
 constexpr int TILE_BYTES = BM * D * 2;      // 32 KB (two 16 KB chunks)
 constexpr int CHUNK_BYTES = 128 * 128;      // 128 rows x 128 B
 constexpr int KV_STAGES = 2;
@@ -48,12 +55,34 @@ constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, D, false, true);
 constexpr int TMEM_COLS = 512;
 __device__ __forceinline__ uint32_t s_col(int t) { return t ? 128u : 0u; }
 __device__ __forceinline__ uint32_t o_col(int t) { return t ? 384u : 256u; }
-// smem: Q_A | Q_B | K[2] | V[2] | barriers
+// smem: Q_A | Q_B | K[2] | V[2] | row exchange [2 parities][2 tiles][2 halves][128] f32 | barriers
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
 constexpr int OFF_V = OFF_K + KV_STAGES * TILE_BYTES;
-constexpr int OFF_BAR = OFF_V + KV_STAGES * TILE_BYTES;
+constexpr int OFF_RED = OFF_V + KV_STAGES * TILE_BYTES;
+constexpr int RED_PARITY = 2 * 2 * BM;  // floats per parity
+constexpr int OFF_BAR = OFF_RED + 2 * RED_PARITY * 4;
 constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + 256;
+
+// Named barrier over the `count` threads of one tile's softmax warps that also ANDs a
+// predicate across them (bar.red orders their shared-memory accesses like bar.sync).
+__device__ __forceinline__ bool bar_and(int id, int count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 struct Params {
   int64_t sq, sk;
@@ -152,6 +181,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* p_full = bars + 11;  // [2 tiles]
   uint64_t* o_done = bars + 13;  // [2 tiles]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* red = reinterpret_cast<float*>(base + OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // longest causal rows first: the last query tiles have the most key tiles
@@ -172,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_addr(&v_full[i]), 1);
       mbar_init(smem_addr(&v_empty[i]), 1);
       mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&p_full[i]), 4);
+      mbar_init(smem_addr(&p_full[i]), 8);  // the eight softmax warps of the tile
       mbar_init(smem_addr(&o_done[i]), 1);
     }
     fence_barrier_init();
@@ -190,8 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   // Register split by warpgroup. The setmaxnreg of a role sits at the top of that
   // role's own branch: code after a merge point is compiled for the smaller budget.
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+  if (warp >= SOFTMAX_WARPS) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 32;\n" ::: "memory");
     if (warp == PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_tiles > 0) {
@@ -242,13 +272,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc_commit(smem_addr(&s_full[t]));
       };
-      // O_t += P_t . V_j, P_t from tensor memory (64 columns of packed bf16 over S_t)
+      // O_t += P_t . V_j; keys 16 kk .. 16 kk + 15 of P_t sit in the 8 packed columns
+      // 64 (kk / 4) + 8 (kk % 4) of S_t (each key half wrote its own first 32 columns)
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_base = smem_addr(base + OFF_V + (j & 1) * TILE_BYTES);
 #pragma unroll 1
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + kk * 8, sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES),
-                        IDESC_PV, (j | kk) != 0);
+          tc_mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + (kk >> 2) * 64 + (kk & 3) * 8,
+                        sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES), IDESC_PV, (j | kk) != 0);
         tc_commit(smem_addr(&o_done[t]));
       };
       if (ok) ok = mbar_wait_site(smem_addr(&k_full[0]), 0, 5, 0);
@@ -283,154 +314,169 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
-    }  // warps 10 and 11 have no role
+    }  // warps 18 and 19 have no role
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
-    // ------------------------------------------------------------ softmax warpgroups
-    const int t = warp >> 2;                      // query tile of this warpgroup
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 112;\n" ::: "memory");
+    // ------------------------------------------------------------ softmax warps 0..15
+    const int t = warp >> 3;                      // query tile of this warp
+    const int hh = (warp >> 2) & 1;               // key half: keys 64 hh .. 64 hh + 63 of a key tile
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;          // TMEM lane == query row in the tile
-    const int64_t qpos = q0 + t * BM + row;       // query index
-    const int64_t anchor = qpos + offset;         // last visible key (causal)
-    const int64_t tile_first = q0 + t * BM + offset;  // smallest anchor of this tile
+    // Masking in 32 bits (sequence lengths are below 2^31, as the TMA coordinates are):
+    // key tile j needs a mask from j_mask on, and the last visible key of this half of
+    // tile j is lk - 128 j (relative to the half's first key).
+    int j_mask, lk;
+    {
+      const int64_t qpos = q0 + t * BM + row;
+      const int64_t last_key = p.causal ? std::min<int64_t>(qpos + offset, p.sk - 1) : p.sk - 1;
+      auto first_j = [](int64_t num) -> int64_t { return num < 0 ? 0 : num / BN + 1; };  // least j: BN j > num
+      int64_t jm = first_j(p.sk - 64 - 64 * hh);  // keys past the end
+      if (p.causal) jm = std::min<int64_t>(jm, first_j(q0 + t * BM + offset - 63 - 64 * hh));  // future keys
+      j_mask = static_cast<int>(std::min<int64_t>(jm, n_tiles));
+      lk = static_cast<int>(std::max<int64_t>(-1, last_key - 64 * hh));
+    }
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_addr + s_col(t);
-    const uint32_t o_addr = tmem + lane_addr + o_col(t);
+    const uint32_t s_addr = tmem + lane_addr + s_col(t) + 64 * hh;  // this half's S columns
+    const uint32_t o_addr = tmem + lane_addr + o_col(t) + 64 * hh;  // this half's head dims of O
+    const uint32_t my_red = smem_addr(red + (t * 2 + hh) * BM + row);
+    const uint32_t peer_red = smem_addr(red + (t * 2 + (hh ^ 1)) * BM + row);
+    const int bar_id = 1 + t;  // 0 is __syncthreads
     const float2 c2 = make_float2(p.scale_log2, p.scale_log2);
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j)) { ok = false; break; }
-      tc_fence_after();
-      float f[BN];  // the S row, then P, in place
-      tmem_ld32f(s_addr, f);
-      tmem_ld32f(s_addr + 32, f + 32);
-      tmem_ld32f(s_addr + 64, f + 64);
-      tmem_ld32f(s_addr + 96, f + 96);
-      tc_wait_ld();
-      reg_fence32f(f);
-      reg_fence32f(f + 32);
-      reg_fence32f(f + 64);
-      reg_fence32f(f + 96);
-      // mask future / out-of-range keys; the row max is taken on the raw scores (the
-      // scale is positive, so max(fl(s * c)) == fl(max(s) * c))
-      const int64_t key0 = static_cast<int64_t>(j) * BN;
-      const bool need_mask = (key0 + BN > p.sk) || (p.causal && key0 + BN - 1 > tile_first);
-      if (need_mask) {
-        const int lim = static_cast<int>(std::max<int64_t>(
-            -1, std::min<int64_t>(BN - 1, (p.causal ? std::min<int64_t>(anchor, p.sk - 1) : p.sk - 1) - key0)));
+      const bool w_ok = mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j);
+      float f[64];  // the half row of S, then P, in place
+      if (w_ok) {
+        tc_fence_after();
+        tmem_ld32f(s_addr, f);
+        tmem_ld32f(s_addr + 32, f + 32);
+        tc_wait_ld();
+        reg_fence32f(f);
+        reg_fence32f(f + 32);
+      }
+      // mask future / out-of-range keys; the max is taken on the raw scores (the scale is
+      // positive, so max(fl(s * c)) == fl(max(s) * c))
+      if (j >= j_mask) {
+        const int lim = std::max(-1, std::min(63, lk - BN * j));
 #pragma unroll
-        for (int i = 0; i < BN; ++i)
+        for (int i = 0; i < 64; ++i)
           if (i > lim) f[i] = -INFINITY;
       }
-      float mx[8];
+      float mx[4];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) mx[g] = fmax3(f[16 * g], f[16 * g + 1], f[16 * g + 2]);
+      for (int g = 0; g < 4; ++g) mx[g] = fmax3(f[16 * g], f[16 * g + 1], f[16 * g + 2]);
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
+      for (int g = 0; g < 4; ++g) {
 #pragma unroll
         for (int i = 3; i < 15; i += 2) mx[g] = fmax3(mx[g], f[16 * g + i], f[16 * g + i + 1]);
         mx[g] = fmaxf(mx[g], f[16 * g + 15]);
       }
-      const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+      const float pmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      st_shared_f32(my_red + (j & 1) * RED_PARITY * 4, pmax);
+      if (!bar_and(bar_id, 256, w_ok)) { ok = false; break; }
+      const float tmax = fmaxf(pmax, ld_shared_f32(peer_red + (j & 1) * RED_PARITY * 4));
       const float m_new = fmaxf(m_run, __fmul_rn(tmax, p.scale_log2));  // log2 domain
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = m_run == -INFINITY ? 0.0f : ex2(__fsub_rn(m_run, m_use));
       const float2 mneg = make_float2(-m_use, -m_use);
       float2 raw[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float2 d = __ffma2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2, mneg);  // s * c - m, one rounding
         const float2 e = make_float2(ex2(d.x), ex2(d.y));
         f[2 * i] = e.x;
         f[2 * i + 1] = e.y;
         if constexpr (RAW) raw[i & 3] = __fadd2_rn(raw[i & 3], e);
       }
-      float tile_sum;
+      float half_sum;
       if constexpr (PLEV != 0) {
-        const float qs0 = quantize_p64<PLEV>(f);
-        const float qs1 = quantize_p64<PLEV>(f + 64);
+        const float qs = quantize_p64<PLEV>(f);
         if constexpr (RAW) {
           const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
-          tile_sum = __fadd_rn(r.x, r.y);
+          half_sum = __fadd_rn(r.x, r.y);
         } else {
-          tile_sum = __fadd_rn(qs0, qs1);
+          half_sum = qs;
         }
       } else {
         const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
-        tile_sum = __fadd_rn(r.x, r.y);
+        half_sum = __fadd_rn(r.x, r.y);
       }
-      l_run = __fadd_rn(__fmul_rn(alpha, l_run), tile_sum);
+      l_run = __fadd_rn(__fmul_rn(alpha, l_run), half_sum);
       m_run = m_new;
-      // O and the P columns may be touched only after PV of the previous tile finished
-      if (j > 0) {
-        if (!mbar_wait_warp(smem_addr(&o_done[t]), (j - 1) & 1, 14 + t, j)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-          const float2 a2 = make_float2(alpha, alpha);
+      // s_full(j) completes after PV_t(j-1) (tcgen05 operations complete in issue order),
+      // so O may be rescaled here
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            tmem_ld32f(o_addr + c * 32, o);
-            tc_wait_ld();
-            reg_fence32f(o);
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32f(o_addr + c * 32, o);
+          tc_wait_ld();
+          reg_fence32f(o);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float2 v = __fmul2_rn(make_float2(o[2 * i], o[2 * i + 1]), a2);
-              o[2 * i] = v.x;
-              o[2 * i + 1] = v.y;
-            }
-            tmem_st32f(o_addr + c * 32, o);
+          for (int i = 0; i < 16; ++i) {
+            const float2 v = __fmul2_rn(make_float2(o[2 * i], o[2 * i + 1]), a2);
+            o[2 * i] = v.x;
+            o[2 * i + 1] = v.y;
           }
+          tmem_st32f(o_addr + c * 32, o);
         }
       }
-      // P as packed bf16 (exact for quantized values) into the first 64 columns of S_t
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      // P as packed bf16 (exact for quantized values) over the half's first 32 S columns
+      {
         float w[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[64 * c + 2 * i], f[64 * c + 2 * i + 1]);
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
           w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
         }
-        tmem_st32f(s_addr + c * 32, w);
+        tmem_st32f(s_addr, w);
       }
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&p_full[t]));
     }
-    if (ok && n_tiles > 0 && mbar_wait_warp(smem_addr(&o_done[t]), (n_tiles - 1) & 1, 16 + t, n_tiles)) {
-      tc_fence_after();
-      // tcgen05.ld is .sync.aligned: every lane loads, even the lanes of query rows
-      // past the end (a tile can end mid-warp); only the stores are predicated.
-      const bool store = qpos < p.sq;
-      __nv_bfloat16* dst = p.out + b * p.ob + (store ? qpos : 0) * p.os + static_cast<int64_t>(h) * p.oh;
-      const bool has_mass = l_run > 0.0f;
+    if (n_tiles > 0) {
+      // every warp of the tile takes this barrier once more, whatever happened above
+      const bool e_ok = ok && mbar_wait_warp(smem_addr(&o_done[t]), (n_tiles - 1) & 1, 16 + t, n_tiles);
+      st_shared_f32(my_red + (n_tiles & 1) * RED_PARITY * 4, l_run);
+      if (bar_and(bar_id, 256, e_ok)) {
+        tc_fence_after();
+        const float l_sum = __fadd_rn(l_run, ld_shared_f32(peer_red + (n_tiles & 1) * RED_PARITY * 4));
+        const int64_t qpos = q0 + t * BM + row;
+        // tcgen05.ld is .sync.aligned: every lane loads, even the lanes of query rows
+        // past the end (a tile can end mid-warp); only the stores are predicated.
+        const bool store = qpos < p.sq;
+        __nv_bfloat16* dst = p.out + b * p.ob + (store ? qpos : 0) * p.os + static_cast<int64_t>(h) * p.oh + 64 * hh;
+        const bool has_mass = l_sum > 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(o_addr + c * 32, r);
-        tc_wait_ld();
-        reg_fence32(r);
-        uint32_t w[16];
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(o_addr + c * 32, r);
+          tc_wait_ld();
+          reg_fence32(r);
+          uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float a0 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i]), l_run) : 0.0f;
-          const float a1 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i + 1]), l_run) : 0.0f;
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
-          w[i] = *reinterpret_cast<const uint32_t*>(&pr);
-        }
-        if (store) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+          for (int i = 0; i < 16; ++i) {
+            const float a0 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i]), l_sum) : 0.0f;
+            const float a1 = has_mass ? __fdiv_rn(__uint_as_float(r[2 * i + 1]), l_sum) : 0.0f;
+            const __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+            w[i] = *reinterpret_cast<const uint32_t*>(&pr);
+          }
+          if (store) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          }
         }
       }
-    } else if (n_tiles == 0 && qpos < p.sq) {
+    } else if (q0 + t * BM + row < p.sq) {
       // no visible key at all: the reference's output is zero
-      __nv_bfloat16* dst = p.out + b * p.ob + qpos * p.os + static_cast<int64_t>(h) * p.oh;
-      for (int i = 0; i < D; ++i) dst[i] = __float2bfloat16_rn(0.0f);
+      const int64_t qpos = q0 + t * BM + row;
+      __nv_bfloat16* dst = p.out + b * p.ob + qpos * p.os + static_cast<int64_t>(h) * p.oh + 64 * hh;
+      for (int i = 0; i < 64; ++i) dst[i] = __float2bfloat16_rn(0.0f);
     }
     tc_fence_before();
   }
@@ -453,6 +499,8 @@ extern "C" int faq_hif4_attention(const void* q, const void* k, const void* v, i
   using namespace faq::attn;
   FAQ_CHECK_ARG(q && k && v && out, "null pointer");
   FAQ_CHECK_ARG(batch >= 0 && hq > 0 && hkv > 0 && sq >= 0 && sk >= 0, "bad shape");
+  FAQ_CHECK_ARG(sq < (int64_t(1) << 31) - 512 && sk < (int64_t(1) << 31) - 512,
+                "sequence lengths must be below 2^31 - 512 (32-bit tile coordinates)");
   FAQ_CHECK_ARG(hq % hkv == 0, "query heads must be divisible by key/value heads");
   if (d != 128) return fail(FAQ_ERR_UNSUPPORTED, "head_dim must be 128");
   FAQ_CHECK_ARG(p_levels == 0 || p_levels == 123 || p_levels == 12 || p_levels == 13, "p_levels must be 0/123/12/13");
