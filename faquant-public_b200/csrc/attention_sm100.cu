@@ -260,26 +260,39 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       bool ok = mbar_wait_site(smem_addr(q_full), 0, 4, 0);
-      const uint32_t q_base = smem_addr(base + OFF_Q);
+      // Shared-memory descriptors built once; every MMA adds a compile-time offset to a
+      // base (the 14-bit start-address field holds addr >> 4 and cannot carry: shared
+      // addresses stay below 2^18). Unrolled, so an MMA issues every few cycles instead
+      // of waiting on a descriptor chain -- one N = 128 MMA runs only 64 cycles.
+      const uint32_t q_desc = sw128_desc_lo(smem_addr(base + OFF_Q), 16);  // LBO unused (K-major SW128)
+      const uint32_t k_desc = sw128_desc_lo(smem_addr(base + OFF_K), 16);
+      const uint32_t v_desc = sw128_desc_lo(smem_addr(base + OFF_V), CHUNK_BYTES);
+      constexpr uint32_t TILE_D = TILE_BYTES >> 4;
+      // an opaque copy keeps the compiler from hoisting every per-MMA descriptor of the
+      // loop into registers (the issuing warp runs on 32)
+      auto pin = [](uint32_t v) {
+        asm volatile("mov.b32 %0, %0;" : "+r"(v));
+        return v;
+      };
       // S_t = Q_t . K_j^T
       auto issue_qk = [&](int t, int j) {
-        const uint32_t k_base = smem_addr(base + OFF_K + (j & 1) * TILE_BYTES);
-        const uint32_t qb = q_base + t * TILE_BYTES;
-#pragma unroll 1
+        const uint32_t a = pin(q_desc + t * TILE_D), b = pin(k_desc + (j & 1) * TILE_D);
+        const uint32_t d = tmem + s_col(t);
+#pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          tc_mma_f16(tmem + s_col(t), sw128_kmajor_desc(qb + off), sw128_kmajor_desc(k_base + off), IDESC_QK, kk != 0);
+          const uint32_t off = static_cast<uint32_t>((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;
+          tc_mma_f16_lo(d, a + off, b + off, IDESC_QK, kk != 0);
         }
         tc_commit(smem_addr(&s_full[t]));
       };
       // O_t += P_t . V_j; keys 16 kk .. 16 kk + 15 of P_t sit in the 8 packed columns
       // 64 (kk / 4) + 8 (kk % 4) of S_t (each key half wrote its own first 32 columns)
       auto issue_pv = [&](int t, int j) {
-        const uint32_t v_base = smem_addr(base + OFF_V + (j & 1) * TILE_BYTES);
-#pragma unroll 1
+        const uint32_t b = pin(v_desc + (j & 1) * TILE_D);
+        const uint32_t d = tmem + o_col(t), a = pin(tmem + s_col(t));
+#pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_f16_ts(tmem + o_col(t), tmem + s_col(t) + (kk >> 2) * 64 + (kk & 3) * 8,
-                        sw128_mnmajor_desc(v_base + kk * 2048, CHUNK_BYTES), IDESC_PV, (j | kk) != 0);
+          tc_mma_f16_ts_lo(d, a + (kk >> 2) * 64 + (kk & 3) * 8, b + ((kk * 2048) >> 4), IDESC_PV, (j | kk) != 0);
         tc_commit(smem_addr(&o_done[t]));
       };
       if (ok) ok = mbar_wait_site(smem_addr(&k_full[0]), 0, 5, 0);

@@ -303,6 +303,33 @@ __device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr, uint32_t 
   d |= static_cast<uint64_t>(2) << 61;
   return d;
 }
+// The upper 32 bits of every 128-byte-swizzled descriptor above (stride byte offset
+// 1024, version, layout); the lower 32 bits hold the start address and the leading
+// byte offset.
+constexpr uint32_t SW128_DESC_HI = (1024u >> 4) | (1u << (46 - 32)) | (2u << (61 - 32));
+__device__ __forceinline__ uint32_t sw128_desc_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+}
+// tcgen05.mma forms taking the low descriptor words only (the upper words are
+// SW128_DESC_HI): fewer registers for an issuer that keeps many descriptors live.
+__device__ __forceinline__ void tc_mma_f16_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 ad, bd; setp.ne.b32 p, %4, 0;\n"
+      "mov.b64 ad, {%1, %5}; mov.b64 bd, {%2, %5};\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %3, p; }" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(SW128_DESC_HI)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 bd; setp.ne.b32 p, %4, 0;\n"
+      "mov.b64 bd, {%2, %5};\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %3, p; }" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(SW128_DESC_HI)
+      : "memory");
+}
 // Instruction descriptor: kind::f16 with bf16 A/B, fp32 D, dense.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                                  // D format: F32
