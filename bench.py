@@ -17,6 +17,11 @@ shipped to the GPU box), on a bounded sample of the same workload.
 Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
 ``torch.distributed.run`` (one process per GPU, replicas: the linear set does not
 shard, so every rank runs its own copy and no collective is on the data path).
+
+The same line carries the two sharded workloads, strong scaling over the N ranks:
+``wan22_block`` (the Wan2.2 DiT block, attention sharded by heads,
+row-parallel o / ffn.2 with an NCCL all-reduce) and ``qwen3_32b_prefill`` (config 5:
+the 64-layer Qwen3-32B prefill, tensor-parallel with two NCCL all-reduces per layer).
 """
 
 from __future__ import annotations
@@ -374,6 +379,14 @@ def main_arm(args) -> None:
             "gpu_launches_per_step": launches_att,
         }
 
+    # ---------------- sharded workloads (configs 4 and 5), strong scaling over the ranks
+    tp_lines = {}
+    if not args.no_tp:
+        del layers, A
+        torch.cuda.empty_cache()
+        tp_lines = run_tp_workloads(args, rank, world, device, pk, barrier, dist)
+        layers = build_linear_set(device, seed=rank) if not args.no_e2e else None
+
     # ---------------- e2e through FakeQuantLinear with host buffers
     e2e = None
     if not args.no_e2e:
@@ -449,6 +462,7 @@ def main_arm(args) -> None:
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "attention": att,
+            **tp_lines,
             "e2e": e2e,
         }
         if not args.no_cpu_baseline:
@@ -457,6 +471,72 @@ def main_arm(args) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _timed(fn, steps: int, warmup: int, barrier, dist, device) -> float:
+    """Device time of ``fn`` per step in ms, max over ranks (barrier + synchronize around)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=device)
+    if dist is not None:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    return float(ms.item())
+
+
+def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dist) -> dict:
+    """BASELINE configs 4 (Wan2.2 block, heads sharded) and 5 (Qwen3-32B TP prefill)."""
+    import torch
+
+    from faquant_b200.tensor_parallel import (Qwen3TPConfig, Qwen3TPPrefill, TPGroup, WanBlockConfig, WanBlockTP,
+                                              default_input_ids)
+
+    tp = TPGroup(rank, world, None)
+    out = {}
+    wcfg = WanBlockConfig()
+    block = WanBlockTP(wcfg, tp, device)
+    g = torch.Generator(device=device).manual_seed(7)
+    x = torch.randn(wcfg.seq, wcfg.dim, generator=g, device=device).to(torch.bfloat16)
+    w_ms = _timed(lambda: block(x), args.tp_steps, 1, barrier, dist, device)
+    wf = wcfg.flops()
+    out["wan22_block"] = {
+        "workload": "Wan2.2-A14B DiT block, S=75600 (21x45x80), 40 heads, self-attention + FFN (BASELINE config 4)",
+        "parallelism": f"heads/tensor-parallel x{world}", "scaling": "strong", "ms_per_step": w_ms,
+        "tflops": wf["total"] / (w_ms * 1e-3) / 1e12, "frac_of_bf16_peak":
+        wf["total"] / (w_ms * 1e-3) / 1e12 / (pk["bf16_tflops"] * world),
+        "tokens_per_s": wcfg.seq / (w_ms * 1e-3), "flops": wf, "steps": args.tp_steps,
+        "rotation": "rbhn_r64 readers (column-parallel), signs r64 (row-parallel)", "levels": wcfg.levels,
+    }
+    del block, x
+    torch.cuda.empty_cache()
+    qcfg = Qwen3TPConfig(layers=args.qwen_layers)
+    model = Qwen3TPPrefill(qcfg, tp, device)
+    ids = default_input_ids(4, 8192, qcfg.vocab, device)
+    q_ms = _timed(lambda: model(ids), args.tp_steps, 1, barrier, dist, device)
+    qf = qcfg.flops(4, 8192)
+    out["qwen3_32b_prefill"] = {
+        "workload": f"Qwen3-32B prefill, {qcfg.layers} layers, batch 4 x 8192 tokens (BASELINE config 5)",
+        "parallelism": f"tensor-parallel x{world}", "scaling": "strong", "ms_per_forward": q_ms,
+        "tokens_per_s": 4 * 8192 / (q_ms * 1e-3), "tflops": qf["total"] / (q_ms * 1e-3) / 1e12,
+        "frac_of_bf16_peak": qf["total"] / (q_ms * 1e-3) / 1e12 / (pk["bf16_tflops"] * world),
+        "flops": qf, "steps": args.tp_steps, "bf16_layers": list(qcfg.bf16_layers),
+        "rotation": "hisq1024 per norm (column-parallel), signs r64 (row-parallel)",
+        "logits": "last position of each sequence", "weights": "RTN HiF4 of N(0,0.02)",
+    }
+    del model
+    torch.cuda.empty_cache()
+    return out
 
 
 def kernel_case(name: str, reps: int) -> None:
@@ -505,6 +585,9 @@ def main() -> None:
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
+    ap.add_argument("--tp-steps", type=int, default=2)
+    ap.add_argument("--qwen-layers", type=int, default=64)
     ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention"],
                     help="run one kernel on a profiling-sized case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)

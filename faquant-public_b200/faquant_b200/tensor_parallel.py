@@ -1,0 +1,452 @@
+"""Tensor-parallel HiF4 W4A4 prefill over NCCL: the multi-GPU form of the two hot paths.
+
+Megatron-style sharding, one process per GPU (``torch.distributed``, backend ``nccl``):
+
+* column-parallel projections (Qwen3 q/k/v and gate/up; Wan q/k/v and ffn.0) keep a
+  contiguous slice of output rows. Their input is replicated, so K1 quantizes the whole
+  input with its full HiSQ rotation -- bit-identical to the single-GPU module -- and the
+  GEMM runs on the local rows. Projections that read the same normalized input share
+  one rotation and one K1 launch (the reference's ``hisq_rotation_source`` sharing
+  ``"norm"``, ``hisq_rotation.py:204-212``) and one GEMM over their concatenated rows.
+* row-parallel projections (o_proj, down_proj; Wan o and ffn.2) keep the input columns
+  of their shard and end in one NCCL all-reduce (sum, bf16) of the partial outputs. The
+  rotation of a row-parallel input must stay inside the shard: it uses the reference's
+  ``"signs"`` construction (``restrict_hisq_rotation``, ``hisq_rotation.py:156-167``:
+  sign flips, no permutation) with 64-channel Hadamard blocks, so HiF4 groups and
+  rotation blocks never straddle a shard at 1/2/4/8 GPUs.
+
+Only the GEMM accumulation order depends on the number of ranks (partial sums meet in
+the all-reduce); every quantized activation and weight code is the same at any TP size.
+"""
+
+from __future__ import annotations
+
+import hashlib
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+from . import ops
+from .hisq_rotation import derive_hisq_rotation, hisq_rotation_source, restrict_hisq_rotation
+
+HIF4_GROUP = 64
+
+
+@dataclass
+class TPGroup:
+    """This rank's place in the tensor-parallel group (``world == 1``: no collective)."""
+
+    rank: int = 0
+    world: int = 1
+    group: object | None = None
+
+    def shard(self, n: int, unit: int) -> tuple[int, int]:
+        """(start, size) of this rank's even share of ``n`` items in whole ``unit``s."""
+        if n % (self.world * unit):
+            raise ValueError(f"{n} does not split into {self.world} shards of whole {unit}-blocks")
+        size = n // self.world
+        return self.rank * size, size
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        return t
+
+
+def _seed(*parts: object) -> int:
+    """Deterministic 63-bit seed of a weight's name (identical on every rank and TP size)."""
+    return int.from_bytes(hashlib.sha256("::".join(map(str, parts)).encode()).digest()[:8], "little") >> 1
+
+
+def random_weight(shape: tuple[int, int], seed: int, device: torch.device, std: float = 0.02) -> torch.Tensor:
+    """``N(0, std)`` weight drawn in full on ``device`` (every rank draws the same matrix)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+
+@dataclass
+class Rotation:
+    """Input rotation of a projection as K1 takes it (``signs`` None: no rotation)."""
+
+    signs: torch.Tensor | None = None
+    permutation: torch.Tensor | None = None
+    block: int = 0
+
+    def to(self, device: torch.device) -> "Rotation":
+        return Rotation(None if self.signs is None else self.signs.to(device),
+                        None if self.permutation is None else self.permutation.to(device), self.block)
+
+
+def column_rotation(name: str, k: int, *, seed: int, block: int, sharing: str = "norm") -> Rotation:
+    """Full HiSQ rotation of a column-parallel projection's (replicated) input."""
+    source, source_seed = hisq_rotation_source(name, sharing, seed=seed, global_seed=seed)
+    rot = derive_hisq_rotation(source, k, seed=source_seed, block_size=block)
+    return Rotation(rot.signs, rot.permutation, block)
+
+
+def row_rotation(name: str, k: int, tp: TPGroup, *, seed: int, block: int = HIF4_GROUP) -> Rotation:
+    """Shard-local ``"signs"`` rotation of a row-parallel projection's input slice."""
+    rot = restrict_hisq_rotation(derive_hisq_rotation(name, k, seed=seed, block_size=block), "signs")
+    start, size = tp.shard(k, block)
+    return Rotation(rot.signs[start:start + size].clone(), None, block)
+
+
+class TPHiF4Linear(nn.Module):
+    """One rank's shard of a HiF4 W4A4 projection (or a plain bf16 one).
+
+    ``weight`` is the local ``[n_local, k_local]`` bf16 slice; when ``quantize`` is set it
+    is RTN-quantized to the HiF4 grid here (groups of 64 along k stay whole in a slice)
+    and the input goes through K1 with ``rotation``. ``reduce`` makes it row-parallel.
+    """
+
+    def __init__(self, weight: torch.Tensor, *, rotation: Rotation | None, quantize: bool, levels: str = "123",
+                 bias: torch.Tensor | None = None, reduce: TPGroup | None = None) -> None:
+        super().__init__()
+        if quantize:
+            weight = ops.hif4_quantize(weight.to(torch.bfloat16), levels=levels)[0]
+        self.register_buffer("weight", weight.to(torch.bfloat16).contiguous())
+        self.register_buffer("bias", None if bias is None else bias.to(torch.bfloat16).contiguous())
+        self.rotation = (rotation or Rotation()).to(weight.device)
+        self.quantize = quantize
+        self.levels = levels
+        self.reduce = reduce
+
+    def quantize_input(self, x: torch.Tensor) -> torch.Tensor:
+        if not self.quantize:
+            return x
+        r = self.rotation
+        return ops.hif4_quantize(x, levels=self.levels, signs=r.signs, permutation=r.permutation,
+                                 rot_block=r.block if r.signs is not None else None)[0]
+
+    def forward(self, x: torch.Tensor, *, quantized: bool = False) -> torch.Tensor:
+        xq = x if quantized else self.quantize_input(x)
+        y = ops.gemm_bf16(xq, self.weight, self.bias)
+        return y if self.reduce is None else self.reduce.all_reduce_(y)
+
+
+# ---------------------------------------------------------------- elementwise glue (torch)
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """``Qwen3RMSNorm``: fp32 mean of squares, rsqrt, cast back, times the weight."""
+    h = x.float()
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * h.to(x.dtype)
+
+
+def rope_tables(seq: int, dim: int, theta: float, device: torch.device, dtype=torch.bfloat16):
+    """cos/sin ``[seq, dim]`` of HF's default rotary embedding (``rotate_half`` layout)."""
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim))
+    freqs = torch.outer(torch.arange(seq, device=device, dtype=torch.float32), inv)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """``x [B, S, H, D]``: ``x * cos + rotate_half(x) * sin`` (HF ``apply_rotary_pos_emb``)."""
+    half = x.shape[-1] // 2
+    rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+    return x * cos[None, :, None, :] + rot * sin[None, :, None, :]
+
+
+# ---------------------------------------------------------------- Qwen3 tensor-parallel prefill
+@dataclass
+class Qwen3TPConfig:
+    """Qwen3-32B shapes; smaller values for tests."""
+
+    hidden: int = 5120
+    layers: int = 64
+    heads: int = 64
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 25600
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+    bf16_layers: tuple[int, ...] = (39, 40, 42, 45, 46)
+    levels: str = "123"
+    hisq_seed: int = 17
+    column_block: int = 1024
+    seed: int = 0
+
+    def flops(self, batch: int, seq: int) -> dict[str, float]:
+        """Algorithmic FLOPs of one prefill (last-token logits only)."""
+        t = batch * seq
+        per_layer = self.hidden * (self.heads + 2 * self.kv_heads) * self.head_dim \
+            + self.heads * self.head_dim * self.hidden + 3 * self.hidden * self.ffn
+        linear = 2.0 * t * per_layer * self.layers
+        attention = 4.0 * self.head_dim * self.heads * batch * seq * (seq + 1) / 2.0 * self.layers
+        lm_head = 2.0 * batch * self.hidden * self.vocab
+        return {"linear": linear, "attention": attention, "lm_head": lm_head,
+                "total": linear + attention + lm_head}
+
+
+def qwen3_shard_slices(cfg: Qwen3TPConfig, tp: TPGroup) -> dict[str, slice]:
+    """This rank's rows of q / k,v (column-parallel), input columns of o_proj and the FFN
+    channels (gate/up rows, down_proj columns) -- head-aligned and 64-aligned."""
+    if cfg.heads % tp.world or cfg.kv_heads % tp.world:
+        raise ValueError("heads and kv_heads must divide by the TP size")
+    d = cfg.head_dim
+    hq, hkv = cfg.heads // tp.world, cfg.kv_heads // tp.world
+    f0, fl = tp.shard(cfg.ffn, HIF4_GROUP)
+    q = slice(tp.rank * hq * d, (tp.rank + 1) * hq * d)
+    return {"q_rows": q, "kv_rows": slice(tp.rank * hkv * d, (tp.rank + 1) * hkv * d), "o_cols": q,
+            "ffn": slice(f0, f0 + fl)}
+
+
+@dataclass
+class _Qwen3Layer:
+    qkv: TPHiF4Linear
+    o: TPHiF4Linear
+    gate_up: TPHiF4Linear
+    down: TPHiF4Linear
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    heads: int
+    kv_heads: int
+    ffn: int
+
+
+class Qwen3TPPrefill(nn.Module):
+    """One rank of a Qwen3 prefill forward with HiF4 W4A4 projections and HiF4 QK/PV
+    attention (``qwen3._attention_forward``, ``qwen3.py:56-172``, with the decoder layer
+    of HF ``Qwen3DecoderLayer``), random-initialized ``N(0, 0.02)`` weights, RTN HiF4.
+
+    Attention per rank: ``heads / world`` query heads and ``kv_heads / world`` KV heads,
+    the post-RoPE Hadamard over head_dim with HiF4 Q/K/V (K4) and the HiF4 attention
+    kernel (K5, causal, P-Reordering). Layers in ``bf16_layers`` keep bf16 projections.
+    The logits are those of the last position of every sequence. ``trace``, when set,
+    is called as ``trace(stage, layer, tensor)`` at every stage boundary (tests compare
+    each stage with the oracle on that stage's own input: 4-bit quantization is
+    discontinuous, so differences between two implementations are only comparable one
+    stage at a time).
+    """
+
+    def __init__(self, cfg: Qwen3TPConfig, tp: TPGroup, device: torch.device) -> None:
+        super().__init__()
+        self.cfg, self.tp, self.device = cfg, tp, device
+        self.trace = None
+        d = cfg.head_dim
+        sl = qwen3_shard_slices(cfg, tp)
+        hq, hkv = cfg.heads // tp.world, cfg.kv_heads // tp.world
+        q_rows, kv_rows, o_cols, ffn = sl["q_rows"], sl["kv_rows"], sl["o_cols"], sl["ffn"]
+        fl = ffn.stop - ffn.start
+        self.embed = random_weight((cfg.vocab, cfg.hidden), _seed(cfg.seed, "embed"), device)
+        self.lm_head = random_weight((cfg.vocab, cfg.hidden), _seed(cfg.seed, "lm_head"), device)
+        self.final_norm = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=device)
+        self.layers: list[_Qwen3Layer] = []
+        for i in range(cfg.layers):
+            quant = i not in cfg.bf16_layers
+            name = f"model.layers.{i}"
+
+            def w(proj: str, n: int, k: int) -> torch.Tensor:
+                return random_weight((n, k), _seed(cfg.seed, name, proj), device)
+
+            wq = w("self_attn.q_proj", cfg.heads * d, cfg.hidden)[q_rows]
+            wk = w("self_attn.k_proj", cfg.kv_heads * d, cfg.hidden)[kv_rows]
+            wv = w("self_attn.v_proj", cfg.kv_heads * d, cfg.hidden)[kv_rows]
+            wo = w("self_attn.o_proj", cfg.hidden, cfg.heads * d)[:, o_cols]
+            wg = w("mlp.gate_proj", cfg.ffn, cfg.hidden)[ffn]
+            wu = w("mlp.up_proj", cfg.ffn, cfg.hidden)[ffn]
+            wd = w("mlp.down_proj", cfg.hidden, cfg.ffn)[:, ffn]
+            rot = dict(seed=cfg.hisq_seed, block=cfg.column_block)
+            layer = _Qwen3Layer(
+                qkv=TPHiF4Linear(torch.cat([wq, wk, wv]), quantize=quant, levels=cfg.levels,
+                                 rotation=column_rotation(f"{name}.self_attn.q_proj", cfg.hidden, **rot)),
+                o=TPHiF4Linear(wo, quantize=quant, levels=cfg.levels, reduce=tp,
+                               rotation=row_rotation(f"{name}.self_attn.o_proj", cfg.heads * d, tp,
+                                                     seed=cfg.hisq_seed)),
+                gate_up=TPHiF4Linear(torch.cat([wg, wu]), quantize=quant, levels=cfg.levels,
+                                     rotation=column_rotation(f"{name}.mlp.gate_proj", cfg.hidden, **rot)),
+                down=TPHiF4Linear(wd, quantize=quant, levels=cfg.levels, reduce=tp,
+                                  rotation=row_rotation(f"{name}.mlp.down_proj", cfg.ffn, tp, seed=cfg.hisq_seed)),
+                input_norm=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=device),
+                post_norm=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=device),
+                q_norm=torch.ones(d, dtype=torch.bfloat16, device=device),
+                k_norm=torch.ones(d, dtype=torch.bfloat16, device=device),
+                heads=hq, kv_heads=hkv, ffn=fl,
+            )
+            self.layers.append(layer)
+
+    def _t(self, stage: str, index: int, t: torch.Tensor) -> torch.Tensor:
+        if self.trace is not None:
+            self.trace(stage, index, t)
+        return t
+
+    def _attention(self, layer: _Qwen3Layer, h: torch.Tensor, batch: int, seq: int, cos, sin,
+                   index: int = 0) -> torch.Tensor:
+        cfg, d = self.cfg, self.cfg.head_dim
+        qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
+        nq, nk = layer.heads * d, layer.kv_heads * d
+        q = rms_norm(qkv[:, :nq].view(batch, seq, layer.heads, d), layer.q_norm, cfg.eps)
+        k = rms_norm(qkv[:, nq:nq + nk].view(batch, seq, layer.kv_heads, d), layer.k_norm, cfg.eps)
+        v = qkv[:, nq + nk:].view(batch, seq, layer.kv_heads, d)
+        q = self._t("q_rope", index, apply_rope(q, cos, sin))
+        k = self._t("k_rope", index, apply_rope(k, cos, sin))
+        qd = ops.qk_prep(q.transpose(1, 2), levels=cfg.levels, rotate=True)[0]
+        kd = ops.qk_prep(k.transpose(1, 2), levels=cfg.levels, rotate=True)[0]
+        vd = ops.qk_prep(v.transpose(1, 2), levels=cfg.levels, rotate=False)[0]
+        out = ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=True, p_levels=cfg.levels,
+                                 quantized_normalizer=True)  # [B, S, hq, d]
+        return self._t("o", index, layer.o(self._t("attention", index, out).view(batch * seq, nq)))
+
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        batch, seq = input_ids.shape
+        cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
+        x = torch.nn.functional.embedding(input_ids.reshape(-1), self.embed)  # [T, hidden]
+        for i, layer in enumerate(self.layers):
+            x = x + self._attention(layer, rms_norm(x, layer.input_norm, cfg.eps), batch, seq, cos, sin, i)
+            gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, rms_norm(x, layer.post_norm, cfg.eps))))
+            a = self._t("act", i, torch.nn.functional.silu(gu[:, :layer.ffn]) * gu[:, layer.ffn:])
+            x = x + self._t("down", i, layer.down(a))
+        last = self._t("final", len(self.layers), x.view(batch, seq, -1)[:, -1])
+        return torch.nn.functional.linear(rms_norm(last, self.final_norm, cfg.eps), self.lm_head).float()
+
+
+def default_input_ids(batch: int, seq: int, vocab: int, device: torch.device, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randint(0, vocab, (batch, seq), generator=g, device=device)
+
+
+# ---------------------------------------------------------------- Wan2.2 DiT block, heads sharded
+@dataclass
+class WanBlockConfig:
+    """Wan2.2-A14B DiT block shapes; smaller values for tests."""
+
+    dim: int = 5120
+    heads: int = 40
+    head_dim: int = 128
+    ffn: int = 13824
+    grid: tuple[int, int, int] = (21, 45, 80)  # latent frames x height x width
+    eps: float = 1e-6
+    rope_theta: float = 10000.0
+    levels: str = "123"
+    hisq_seed: int = 17
+    seed: int = 0
+
+    @property
+    def seq(self) -> int:
+        return self.grid[0] * self.grid[1] * self.grid[2]
+
+    def flops(self) -> dict[str, float]:
+        s = self.seq
+        attention = 4.0 * self.head_dim * self.heads * s * s
+        linear = 2.0 * s * (4 * self.dim * self.dim + 2 * self.dim * self.ffn)
+        return {"attention": attention, "linear": linear, "total": attention + linear}
+
+
+def rope3d_tables(grid: tuple[int, int, int], head_dim: int, theta: float, device: torch.device):
+    """cos/sin ``[F*H*W, head_dim/2]`` of the 3-axis rotary embedding of Wan's DiT: the
+    ``head_dim/2`` complex pairs are split ``[c - 2(c//3), c//3, c//3]`` over (frame,
+    height, width), each band with its own ``theta^(-2i/d_band)`` frequencies, and a token
+    at grid position (f, h, w) rotates band pairs by (f, h, w) times those frequencies."""
+    c = head_dim // 2
+    bands = [c - 2 * (c // 3), c // 3, c // 3]
+    angles = []
+    for axis, (n, pairs) in enumerate(zip(grid, bands)):
+        dim = 2 * pairs
+        inv = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float64) / dim))
+        pos = torch.arange(n, device=device, dtype=torch.float64)
+        shape = [1, 1, 1, pairs]
+        shape[axis] = n
+        a = torch.outer(pos, inv).reshape(shape).expand(grid[0], grid[1], grid[2], pairs)
+        angles.append(a)
+    ang = torch.cat(angles, dim=-1).reshape(-1, c)
+    return ang.cos().float(), ang.sin().float()
+
+
+def apply_rope3d(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """``x [L, H, D]`` with channel pairs (2i, 2i+1) as complex numbers, rotated in fp64-built
+    fp32 tables; returns ``x.dtype``."""
+    xf = x.float().reshape(*x.shape[:-1], -1, 2)
+    re, im = xf[..., 0], xf[..., 1]
+    c, s = cos[:, None, :], sin[:, None, :]
+    out = torch.stack([re * c - im * s, re * s + im * c], dim=-1)
+    return out.reshape(x.shape).to(x.dtype)
+
+
+class WanBlockTP(nn.Module):
+    """One rank of a Wan2.2 DiT block (self-attention + FFN; the text cross-attention and
+    the time modulation are not part of the benchmarked block) with every Linear HiF4
+    W4A4 and HiF4 QK/PV attention, ``heads / world`` heads on this rank.
+
+    Column-parallel q/k/v and ffn.0 read the LayerNorm outputs with the ``rbhn_r64``
+    reader rotation (one HiSQ rotation per norm, 64-channel blocks; shared, so one K1 per
+    norm); row-parallel o and ffn.2 use shard-local ``"signs"`` rotations. Wan normalizes
+    q and k over all heads (RMSNorm over ``dim``), so the head-sharded form all-reduces the
+    per-token sum of squares (``[L]`` fp32) -- attention itself needs no collective.
+    """
+
+    def __init__(self, cfg: WanBlockConfig, tp: TPGroup, device: torch.device, index: int = 0) -> None:
+        super().__init__()
+        self.cfg, self.tp, self.device = cfg, tp, device
+        self.trace = None  # trace(stage, 0, tensor) at each stage boundary, as in Qwen3TPPrefill
+        if cfg.heads % tp.world:
+            raise ValueError("heads must divide by the TP size")
+        d = cfg.head_dim
+        self.h_local = cfg.heads // tp.world
+        rows = slice(tp.rank * self.h_local * d, (tp.rank + 1) * self.h_local * d)
+        f0, fl = tp.shard(cfg.ffn, HIF4_GROUP)
+        self.ffn_local = fl
+        name = f"blocks.{index}"
+
+        def w(proj: str, n: int, k: int) -> torch.Tensor:
+            return random_weight((n, k), _seed(cfg.seed, name, proj), device)
+
+        def b(proj: str, n: int) -> torch.Tensor:
+            return random_weight((1, n), _seed(cfg.seed, name, proj, "bias"), device)[0]
+
+        rot1 = column_rotation(f"{name}.norm1", cfg.dim, seed=cfg.hisq_seed, block=64, sharing="linear")
+        rot2 = column_rotation(f"{name}.norm2", cfg.dim, seed=cfg.hisq_seed, block=64, sharing="linear")
+        wq, wk, wv = (w(f"self_attn.{p}", cfg.dim, cfg.dim)[rows] for p in "qkv")
+        bq, bk, bv = (b(f"self_attn.{p}", cfg.dim)[rows] for p in "qkv")
+        self.qkv = TPHiF4Linear(torch.cat([wq, wk, wv]), bias=torch.cat([bq, bk, bv]), rotation=rot1,
+                                quantize=True, levels=cfg.levels)
+        self.o = TPHiF4Linear(w("self_attn.o", cfg.dim, cfg.dim)[:, rows],
+                              bias=b("self_attn.o", cfg.dim) if tp.rank == 0 else None, quantize=True,
+                              levels=cfg.levels, reduce=tp,
+                              rotation=row_rotation(f"{name}.self_attn.o", cfg.dim, tp, seed=cfg.hisq_seed))
+        self.ffn0 = TPHiF4Linear(w("ffn.0", cfg.ffn, cfg.dim)[f0:f0 + fl], bias=b("ffn.0", cfg.ffn)[f0:f0 + fl],
+                                 rotation=rot2, quantize=True, levels=cfg.levels)
+        self.ffn2 = TPHiF4Linear(w("ffn.2", cfg.dim, cfg.ffn)[:, f0:f0 + fl],
+                                 bias=b("ffn.2", cfg.dim) if tp.rank == 0 else None, quantize=True,
+                                 levels=cfg.levels, reduce=tp,
+                                 rotation=row_rotation(f"{name}.ffn.2", cfg.ffn, tp, seed=cfg.hisq_seed))
+        self.norm_q = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows]
+        self.norm_k = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows]
+        self.cos, self.sin = rope3d_tables(cfg.grid, d, cfg.rope_theta, device)
+
+    def _qk_norm(self, t: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+        """Wan's RMSNorm over all ``dim`` channels of q or k, from this rank's head slice."""
+        tf = t.float()
+        ss = tf.pow(2).sum(-1, keepdim=True)
+        self.tp.all_reduce_(ss)
+        return (tf * torch.rsqrt(ss / self.cfg.dim + self.cfg.eps) * weight).to(t.dtype)
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """``x [L, dim]`` bf16 (batch 1) -> ``[L, dim]``."""
+        cfg, d, hl = self.cfg, self.cfg.head_dim, self.h_local
+        seq = x.shape[0]
+        tr = (lambda stage, t: (self.trace(stage, 0, t), t)[1]) if self.trace is not None else (lambda stage, t: t)
+        h = tr("norm1", torch.nn.functional.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps).to(x.dtype))
+        qkv = tr("qkv", self.qkv(h))
+        n = hl * d
+        q = tr("q_rope", apply_rope3d(self._qk_norm(qkv[:, :n], self.norm_q).view(seq, hl, d), self.cos, self.sin))
+        k = tr("k_rope", apply_rope3d(self._qk_norm(qkv[:, n:2 * n], self.norm_k).view(seq, hl, d), self.cos, self.sin))
+        v = qkv[:, 2 * n:].view(seq, hl, d)
+        qd = ops.qk_prep(q.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=True)[0]
+        kd = ops.qk_prep(k.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=True)[0]
+        vd = ops.qk_prep(v.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=False)[0]
+        att = tr("attention", ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=False, p_levels=cfg.levels,
+                                                 quantized_normalizer=True))  # [1, L, hl, d]
+        x = x + tr("o", self.o(att.view(seq, n)))
+        h = tr("norm2", torch.nn.functional.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps).to(x.dtype))
+        f0 = tr("ffn0", self.ffn0(h))
+        a = tr("act", torch.nn.functional.gelu(f0.float(), approximate="tanh").to(x.dtype))
+        return x + tr("ffn2", self.ffn2(a))

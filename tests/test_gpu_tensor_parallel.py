@@ -1,0 +1,257 @@
+"""GPU tests of the tensor-parallel prefill (configs 4 and 5 in their sharded form).
+
+* Sharding is exact where it should be: column-parallel shards reproduce the unsharded
+  projection bit for bit, and the shard-local quantized inputs of a row-parallel
+  projection are, concatenated, bit-identical to the unsharded quantized input; only
+  the partial-sum order differs (tolerance on the outputs).
+* A small Qwen3 prefill and a small Wan2.2 block at TP 1, stage by stage: each stage's
+  GPU output against the oracle (rotation + HiF4 quantization, HiF4 attention, fp32
+  matmuls) applied to that stage's own GPU input. 4-bit quantization is discontinuous:
+  a last-bit difference before a K1 can re-code a whole 64-block, so two implementations
+  are only comparable one stage at a time (an end-to-end comparison through several
+  quantized stages measures that amplification, not the kernels).
+* With two or more GPUs, TP 2 over NCCL against TP 1 on the first layer.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import hif4 as oh
+from oracle import linear as olin
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def _rel(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _bf16(x: np.ndarray) -> np.ndarray:
+    return oh.bf16_round(np.asarray(x, np.float32))
+
+
+def _qwen_cfg():
+    from faquant_b200.tensor_parallel import Qwen3TPConfig
+
+    return Qwen3TPConfig(hidden=512, layers=2, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000,
+                         bf16_layers=(1,), column_block=512)
+
+
+def _wan_cfg():
+    from faquant_b200.tensor_parallel import WanBlockConfig
+
+    return WanBlockConfig(dim=512, heads=4, head_dim=128, ffn=1024, grid=(2, 6, 16))
+
+
+def test_shards_reproduce_the_unsharded_projection() -> None:
+    from faquant_b200.tensor_parallel import TPGroup, TPHiF4Linear, column_rotation, random_weight, row_rotation
+
+    x = torch.randn(300, 1024, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16).to(DEV)
+    w = random_weight((768, 1024), 5, DEV)
+    rot = column_rotation("model.layers.0.self_attn.q_proj", 1024, seed=17, block=1024)
+    y = TPHiF4Linear(w, rotation=rot, quantize=True)(x)
+    cols = [TPHiF4Linear(w[r * 384:(r + 1) * 384], rotation=rot, quantize=True)(x) for r in range(2)]
+    assert torch.equal(torch.cat(cols, dim=1), y)
+
+    w2 = random_weight((512, 1024), 6, DEV)
+    full = TPHiF4Linear(w2, rotation=row_rotation("m.o_proj", 1024, TPGroup(0, 1), seed=17), quantize=True)
+    parts = [TPHiF4Linear(w2[:, r * 512:(r + 1) * 512], quantize=True,
+                          rotation=row_rotation("m.o_proj", 1024, TPGroup(r, 2), seed=17)) for r in range(2)]
+    xs = [x[:, r * 512:(r + 1) * 512] for r in range(2)]
+    assert torch.equal(torch.cat([p.quantize_input(s) for p, s in zip(parts, xs)], dim=1), full.quantize_input(x))
+    y1 = full(x).float()
+    p0, p1 = parts[0](xs[0]), parts[1](xs[1])
+    y2 = (p0 + p1).float()  # what the bf16 all-reduce adds
+    # each partial and their sum round to bf16 once (<= 2^-9 relative each), the full
+    # product once; the fp32 sums differ only in order
+    bound = 2.0**-8 * (p0.float().abs() + p1.float().abs() + y1.abs()) + 1e-4 * y1.abs().max()
+    assert torch.all((y2 - y1).abs() <= bound)
+
+
+def _oracle_linear(h: np.ndarray, lin, quantize: bool) -> np.ndarray:
+    """bf16(Xq @ Wq^T + b) with the oracle's rotation + HiF4 quantization of the input."""
+    w = lin.weight.float().cpu().numpy()
+    if quantize:
+        r = lin.rotation
+        h = olin.quantize_activations(
+            h, levels=lin.levels, dtype="bf16",
+            signs=None if r.signs is None else r.signs.cpu().numpy(),
+            permutation=None if r.permutation is None else r.permutation.cpu().numpy(),
+            block=r.block if r.signs is not None else None)
+    y = h @ w.T
+    if lin.bias is not None:
+        y = y + lin.bias.float().cpu().numpy()
+    return _bf16(y)
+
+
+ATT_REL_FRO = 5e-3  # HiF4 attention kernel vs the oracle on identical operands
+ATT_MAX_ABS = 6e-2
+
+
+def _close_linear(got: np.ndarray, ref: np.ndarray) -> None:
+    """bf16 output of a GEMM vs the fp32 oracle product rounded to bf16: the two fp32 sums
+    differ only in order, so the bf16 results differ by at most an ulp or so."""
+    assert np.all(np.abs(got - ref) <= 2.0**-7 * np.abs(ref) + 1e-3 * np.abs(ref).max())
+
+
+def _close_attention(got: np.ndarray, ref: np.ndarray) -> None:
+    err = got - ref
+    assert _rel(got, ref) <= ATT_REL_FRO and float(np.abs(err).max()) <= ATT_MAX_ABS
+
+
+def _traced(module):
+    trace = {}
+
+    def hook(stage, index, t):
+        trace[(stage, index)] = t.detach().float().cpu()
+
+    module.trace = hook
+    return trace
+
+
+def test_qwen3_prefill_stages_match_the_oracle() -> None:
+    """Every stage of a 2-layer prefill (one HiF4 layer, one bf16 layer) against the oracle
+    applied to that stage's own GPU input: the W4A4 projections (K1 + GEMM), the torch glue
+    (q/k RMSNorm, RoPE, SiLU), the HiF4 attention (K4 + K5) and the logits."""
+    from faquant_b200.tensor_parallel import (Qwen3TPPrefill, TPGroup, apply_rope, default_input_ids, rms_norm,
+                                              rope_tables)
+
+    model = Qwen3TPPrefill(_qwen_cfg(), TPGroup(), DEV)
+    cfg, d = model.cfg, model.cfg.head_dim
+    tr = _traced(model)
+    ids = default_input_ids(2, 192, cfg.vocab, DEV, seed=3)
+    logits = model(ids).cpu().numpy()
+    b, s = ids.shape
+    cos, sin = rope_tables(s, d, cfg.rope_theta, torch.device("cpu"))
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    for i, L in enumerate(model.layers):
+        quant = i not in cfg.bf16_layers
+        qkv = tr[("qkv", i)]
+        _close_linear(qkv.numpy(), _oracle_linear(tr[("input_norm", i)].numpy(), L.qkv, quant))
+        nq, nk = L.heads * d, L.kv_heads * d
+        q = apply_rope(rms_norm(bf(qkv[:, :nq]).view(b, s, L.heads, d), L.q_norm.cpu(), cfg.eps), cos, sin)
+        k = apply_rope(rms_norm(bf(qkv[:, nq:nq + nk]).view(b, s, L.kv_heads, d), L.k_norm.cpu(), cfg.eps), cos, sin)
+        assert _rel(tr[("q_rope", i)].numpy(), q.float().numpy()) <= 1e-3
+        assert _rel(tr[("k_rope", i)].numpy(), k.float().numpy()) <= 1e-3
+        qr, kr = oatt.qk_pretransform(tr[("q_rope", i)].transpose(1, 2).numpy(),
+                                      tr[("k_rope", i)].transpose(1, 2).numpy())
+        v = qkv[:, nq + nk:].view(b, s, L.kv_heads, d).transpose(1, 2).numpy()
+        att = oatt.attention(qr, kr, v, causal=True, scale=d**-0.5, normalizer="quantized_same")
+        _close_attention(tr[("attention", i)].numpy(), att)
+        _close_linear(tr[("o", i)].numpy(), _oracle_linear(tr[("attention", i)].reshape(b * s, nq).numpy(), L.o, quant))
+        gu = tr[("gate_up", i)]
+        _close_linear(gu.numpy(), _oracle_linear(tr[("post_norm", i)].numpy(), L.gate_up, quant))
+        act = torch.nn.functional.silu(bf(gu[:, :L.ffn])) * bf(gu[:, L.ffn:])
+        assert _rel(tr[("act", i)].numpy(), act.float().numpy()) <= 1e-3
+        _close_linear(tr[("down", i)].numpy(), _oracle_linear(tr[("act", i)].numpy(), L.down, quant))
+    final = bf(tr[("final", len(model.layers))])
+    ref = torch.nn.functional.linear(rms_norm(final, model.final_norm.cpu(), cfg.eps), model.lm_head.cpu())
+    assert logits.shape == (2, cfg.vocab) and _rel(logits, ref.float().numpy()) <= 1e-2
+
+
+def test_wan_block_stages_match_the_oracle() -> None:
+    from faquant_b200.tensor_parallel import TPGroup, WanBlockTP, apply_rope3d
+
+    block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
+    cfg, d, hl = block.cfg, block.cfg.head_dim, block.h_local
+    tr = _traced(block)
+    x = torch.randn(cfg.seq, cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+    y = block(x.to(DEV)).float().cpu().numpy()
+    assert np.isfinite(y).all()
+    seq, n = cfg.seq, hl * d
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    qkv = tr[("qkv", 0)]
+    _close_linear(qkv.numpy(), _oracle_linear(tr[("norm1", 0)].numpy(), block.qkv, True))
+
+    def qk_norm(z, w):
+        zf = bf(z).float()
+        return (zf * torch.rsqrt(zf.pow(2).sum(-1, keepdim=True) / cfg.dim + cfg.eps) * w.cpu()).to(torch.bfloat16)
+
+    cos, sin = block.cos.cpu(), block.sin.cpu()
+    q = apply_rope3d(qk_norm(qkv[:, :n], block.norm_q).view(seq, hl, d), cos, sin)
+    assert _rel(tr[("q_rope", 0)].numpy(), q.float().numpy()) <= 1e-3
+    qr, kr = oatt.qk_pretransform(tr[("q_rope", 0)].transpose(0, 1)[None].numpy(),
+                                  tr[("k_rope", 0)].transpose(0, 1)[None].numpy())
+    v = qkv[:, 2 * n:].view(seq, hl, d).transpose(0, 1)[None].numpy()
+    att = oatt.attention(qr, kr, v, causal=False, scale=d**-0.5, normalizer="quantized_same")
+    _close_attention(tr[("attention", 0)].numpy(), att)
+    _close_linear(tr[("o", 0)].numpy(), _oracle_linear(tr[("attention", 0)].reshape(seq, n).numpy(), block.o, True))
+    _close_linear(tr[("ffn0", 0)].numpy(), _oracle_linear(tr[("norm2", 0)].numpy(), block.ffn0, True))
+    act = torch.nn.functional.gelu(tr[("ffn0", 0)], approximate="tanh")
+    assert _rel(tr[("act", 0)].numpy(), act.numpy()) <= 1e-2
+    _close_linear(tr[("ffn2", 0)].numpy(), _oracle_linear(tr[("act", 0)].numpy(), block.ffn2, True))
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_rank(rank: int, world: int, port: int, results) -> None:
+    import torch.distributed as dist
+
+    from faquant_b200.tensor_parallel import Qwen3TPPrefill, TPGroup, WanBlockTP, default_input_ids
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        tp = TPGroup(rank, world)
+        model = Qwen3TPPrefill(_qwen_cfg(), tp, dev)
+        tq = _traced(model)
+        model(default_input_ids(2, 192, model.cfg.vocab, dev, seed=3))
+        block = WanBlockTP(_wan_cfg(), tp, dev)
+        tw = _traced(block)
+        x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+        block(x.to(dev))
+        results[rank] = {("qwen",) + k: v.numpy() for k, v in tq.items() if k[1] == 0 and k[0] in ("qkv", "attention", "o")}
+        results[rank].update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "attention", "o")})
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_over_nccl_matches_tp1() -> None:
+    """TP 2 over NCCL against TP 1, first layer: the column-parallel projections and the
+    attention of each rank are bit-identical slices of the TP 1 results (same quantized
+    inputs, same kernels); the row-parallel o_proj after the all-reduce differs only by
+    the order of its partial sums. (Later stages re-quantize those last-bit differences,
+    so they are checked against the oracle stage by stage instead.)"""
+    import torch.multiprocessing as mp
+
+    from faquant_b200.tensor_parallel import Qwen3TPPrefill, TPGroup, WanBlockTP, default_input_ids
+
+    results = mp.Manager().dict()
+    mp.spawn(_tp_rank, args=(2, _free_port(), results), nprocs=2, join=True)
+    model = Qwen3TPPrefill(_qwen_cfg(), TPGroup(), DEV)
+    tq = _traced(model)
+    model(default_input_ids(2, 192, model.cfg.vocab, DEV, seed=3))
+    block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
+    tw = _traced(block)
+    x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
+    block(x.to(DEV))
+    for tag, tr, hq, hkv in (("qwen", tq, 8, 2), ("wan", tw, 4, 4)):
+        d = 128
+        qkv1 = tr[("qkv", 0)].numpy()
+        att1 = tr[("attention", 0)].numpy()
+        for r in range(2):
+            got = results[r]
+            nq, nk = hq // 2 * d, hkv // 2 * d
+            q1 = qkv1[:, r * nq:(r + 1) * nq]
+            k1 = qkv1[:, hq * d + r * nk:hq * d + (r + 1) * nk]
+            v1 = qkv1[:, hq * d + hkv * d + r * nk:hq * d + hkv * d + (r + 1) * nk]
+            assert np.array_equal(got[(tag, "qkv", 0)], np.concatenate([q1, k1, v1], axis=1)), (tag, r)
+            assert np.array_equal(got[(tag, "attention", 0)], att1[..., r * hq // 2:(r + 1) * hq // 2, :]), (tag, r)
+            o1 = tr[("o", 0)].numpy()
+            assert np.all(np.abs(got[(tag, "o", 0)] - o1) <= 2.0**-6 * np.abs(o1) + 2e-3 * np.abs(o1).max()), (tag, r)
