@@ -214,8 +214,9 @@ def _tp_rank(rank: int, world: int, port: int, results) -> None:
         tw = _traced(block)
         x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
         block(x.to(dev))
-        results[rank] = {("qwen",) + k: v.numpy() for k, v in tq.items() if k[1] == 0 and k[0] in ("qkv", "attention", "o")}
-        results[rank].update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "attention", "o")})
+        mine = {("qwen",) + k: v.numpy() for k, v in tq.items() if k[1] == 0 and k[0] in ("qkv", "attention", "o")}
+        mine.update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "attention", "o")})
+        results[rank] = mine  # one assignment: a managed dict hands out copies of its values
         dist.barrier()
     finally:
         dist.destroy_process_group()
