@@ -1,0 +1,132 @@
+// Decoder-layer glue around the two hot paths, fused to one HBM pass each:
+//   faq_rms_norm   Qwen3RMSNorm over the last axis (modeling_qwen3.Qwen3RMSNorm as the
+//                  reference's Qwen3 models use it): h = fp32(x), h * rsqrt(mean(h^2) +
+//                  eps), rounded to bf16, times the bf16 weight, rounded.
+//   faq_silu_mul   the SwiGLU gate of Qwen3MLP on one [rows, 2f] gate|up tensor:
+//                  bf16(bf16(silu(g)) * u), silu(g) = g / (1 + exp(-g)) in fp32.
+// torch runs each as 4-8 elementwise kernels with fp32 temporaries; here one read and
+// one write of the tensor. Rounding points are torch's; the fp32 sums are not in
+// torch's order (tolerance, not bit-exactness, for these two).
+#include "common.cuh"
+
+namespace faq {
+
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {  // values already bf16-exact
+  return make_uint4(exact_bf16_bits(v[0]) | (exact_bf16_bits(v[1]) << 16),
+                    exact_bf16_bits(v[2]) | (exact_bf16_bits(v[3]) << 16),
+                    exact_bf16_bits(v[4]) | (exact_bf16_bits(v[5]) << 16),
+                    exact_bf16_bits(v[6]) | (exact_bf16_bits(v[7]) << 16));
+}
+
+// One CTA (256 threads) per row; up to CHUNKS 8-value chunks per thread stay in
+// registers between the reduction and the scaling (k <= 256 * 8 * CHUNKS).
+template <int CHUNKS>
+__global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
+                                                      int64_t ldx, const __nv_bfloat16* __restrict__ w, float eps,
+                                                      __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  __shared__ float partial[8];
+  const int tid = threadIdx.x, chunks = k / 8;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[CHUNKS][8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int ch = tid + c * 256;
+      if (ch < chunks) {
+        unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + ch * 8), v[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[c][i], v[c][i]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if ((tid & 31) == 0) partial[tid >> 5] = ss;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) total = __fadd_rn(total, partial[i]);
+    __syncthreads();  // partial[] is rewritten by the next row
+    const float r = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps));
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int ch = tid + c * 256;
+      if (ch < chunks) {
+        float wv[8], y[8];
+        unpack8(*reinterpret_cast<const uint4*>(w + ch * 8), wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(wv[i], bf16_round(__fmul_rn(v[c][i], r))));
+        *reinterpret_cast<uint4*>(out + row * ldo + ch * 8) = pack8(y);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int64_t rows, int64_t f,
+                                                       int64_t ld, __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t per_row = f / 8, total = rows * per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / per_row, col = (i % per_row) * 8;
+    float g[8], u[8], y[8];
+    unpack8(*reinterpret_cast<const uint4*>(gu + row * ld + col), g);
+    unpack8(*reinterpret_cast<const uint4*>(gu + row * ld + f + col), u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float s = bf16_round(__fdiv_rn(g[j], __fadd_rn(1.0f, expf(-g[j]))));
+      y[j] = bf16_round(__fmul_rn(s, u[j]));
+    }
+    *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
+  }
+}
+
+}  // namespace faq
+
+extern "C" int faq_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
+                            void* out, int64_t ldo, void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(rows >= 0 && k > 0 && k % 8 == 0 && k <= 32768, "k must be a positive multiple of 8, at most 32768");
+  if (rows == 0) return FAQ_OK;  // an empty tensor may have no storage
+  FAQ_CHECK_ARG(x && weight && out, "null pointer");
+  FAQ_CHECK_ARG(ldx >= k && ldo >= k && ldx % 8 == 0 && ldo % 8 == 0, "row strides must be >= k and multiples of 8");
+  FAQ_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(out), "tensors must be 16-byte aligned");
+  FAQ_CHECK_ARG(eps >= 0.0f, "eps must be non-negative");
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  const auto* wp = static_cast<const __nv_bfloat16*>(weight);
+  auto* op = static_cast<__nv_bfloat16*>(out);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = static_cast<int>(k / 8), per_thread = (chunks + 255) / 256;
+  if (per_thread <= 2)
+    rms_norm_kernel<2><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  else if (per_thread <= 4)
+    rms_norm_kernel<4><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  else if (per_thread <= 8)
+    rms_norm_kernel<8><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  else
+    rms_norm_kernel<16><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  return launch_status("rms_norm_kernel");
+}
+
+extern "C" int faq_silu_mul(const void* gate_up, int64_t rows, int64_t f, int64_t ld, void* out, int64_t ldo,
+                            void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(rows >= 0 && f > 0 && f % 8 == 0, "f must be a positive multiple of 8");
+  if (rows == 0) return FAQ_OK;  // an empty tensor may have no storage
+  FAQ_CHECK_ARG(gate_up && out, "null pointer");
+  FAQ_CHECK_ARG(ld >= 2 * f && ldo >= f && ld % 8 == 0 && ldo % 8 == 0, "bad row strides");
+  FAQ_CHECK_ARG(aligned16(gate_up) && aligned16(out), "tensors must be 16-byte aligned");
+  const int64_t total = rows * (f / 8);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+  silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(gate_up),
+                                                                        rows, f, ld, static_cast<__nv_bfloat16*>(out),
+                                                                        ldo);
+  return launch_status("silu_mul_kernel");
+}

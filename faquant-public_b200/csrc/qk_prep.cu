@@ -8,6 +8,12 @@
 // head_dim (simulated_flash_attention.py:588-619). Wan does the same
 // (wan22_attention.py:186-192, 221, 257-259).
 //
+// The fused entry point faq_qk_norm_rope_prep puts Qwen3's own steps in front
+// (qwen3.py:87-100 with HF Qwen3Attention): the per-head RMSNorm over head_dim
+// (Qwen3RMSNorm: fp32 mean of squares, rsqrt, cast to bf16, times the bf16 weight, cast)
+// and RoPE in bf16 as HF's apply_rotary_pos_emb does it (bf16(q cos) + bf16(rotate_half(q)
+// sin), rounded; rotate_half's partner channel is d/2 away, i.e. d/16 lanes).
+//
 // Mapping: d/8 lanes per (b, h, s) row, 8 consecutive channels per lane, so the
 // Hadamard strides 1, 2, 4 are inside a lane and 8 .. d/2 are lane shuffles, and
 // the HiF4 64-blocks are 8 aligned lanes (hif4_quant8). HBM-bound: one read and
@@ -32,6 +38,11 @@ struct QkPrepParams {
   uint8_t* codes;
   uint32_t* meta;
   bool x_vec, out_vec;
+  const __nv_bfloat16* norm_w;  // [d] or null: per-head RMSNorm first
+  float eps;
+  const __nv_bfloat16* cos;     // [seq, rope_ld] or null: RoPE after the norm
+  const __nv_bfloat16* sin;
+  int64_t rope_ld;
 };
 
 template <typename T, int D>
@@ -72,6 +83,40 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(QkPrepParams p) {
           v[i] = __bfloat162float(src[i]);
         else
           v[i] = src[i];
+      }
+    }
+    if (p.norm_w != nullptr) {
+      // Qwen3RMSNorm over the row: sum of squares across the row's lanes
+      float ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));  // h.pow(2), summed
+#pragma unroll
+      for (int ls = 1; ls < LANES; ls <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, ls));
+      const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), p.eps));
+      const uint4 wu = *reinterpret_cast<const uint4*>(p.norm_w + sub * 8);
+      const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float w = __uint_as_float(i & 1 ? ww[i >> 1] & 0xFFFF0000u : ww[i >> 1] << 16);
+        v[i] = bf16_round(__fmul_rn(w, bf16_round(__fmul_rn(v[i], r))));
+      }
+    }
+    if (p.cos != nullptr) {
+      // HF rotate_half: channel j pairs with j + d/2 (negated) below d/2, with j - d/2 above
+      constexpr int HALF_LANES = LANES / 2;
+      const __nv_bfloat16* cr = p.cos + s * p.rope_ld + sub * 8;
+      const __nv_bfloat16* sr = p.sin + s * p.rope_ld + sub * 8;
+      const uint4 cu = *reinterpret_cast<const uint4*>(cr);
+      const uint4 su = *reinterpret_cast<const uint4*>(sr);
+      const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
+      const bool low = sub < HALF_LANES;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[i], HALF_LANES);
+        const float rot = low ? -partner : partner;
+        const float c = __uint_as_float(i & 1 ? cw[i >> 1] & 0xFFFF0000u : cw[i >> 1] << 16);
+        const float sn = __uint_as_float(i & 1 ? sw[i >> 1] & 0xFFFF0000u : sw[i >> 1] << 16);
+        v[i] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(v[i], c)), bf16_round(__fmul_rn(rot, sn))));
       }
     }
     if (p.offset != nullptr) {
@@ -145,11 +190,39 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(QkPrepParams p) {
 
 }  // namespace faq
 
-extern "C" int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb,
-                           int64_t sh, int64_t ss, const float* offset, const float* smooth, int64_t smooth_head_stride,
-                           int smooth_mode, int rotate, int levels, void* out, int64_t ob, int64_t oh, int64_t os,
-                           uint8_t* codes, uint32_t* meta, void* stream) {
-  using namespace faq;
+namespace faq {
+static int qk_prep_launch(QkPrepParams& p, int x_dtype, int d, void* stream) {
+  const int64_t vec_elems = x_dtype == FAQ_BF16 ? 8 : 4;
+  const uint64_t xa = reinterpret_cast<uintptr_t>(p.x), oa = reinterpret_cast<uintptr_t>(p.out);
+  p.x_vec = (xa & 15) == 0 && p.sb % vec_elems == 0 && p.sh % vec_elems == 0 && p.ss % vec_elems == 0;
+  p.out_vec = (oa & 15) == 0 && p.ob % 8 == 0 && p.oh % 8 == 0 && p.os % 8 == 0;
+  const int64_t rows = p.batch * p.heads * p.seq;
+  const int rows_per_block = 8 * (32 / (d / 8));
+  const int64_t blocks = std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
+                                           static_cast<int64_t>(num_sms()) * 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+  if (x_dtype == FAQ_BF16) {
+    if (d == 128)
+      qk_prep_kernel<__nv_bfloat16, 128><<<g, 256, 0, st>>>(p);
+    else
+      qk_prep_kernel<__nv_bfloat16, 64><<<g, 256, 0, st>>>(p);
+  } else {
+    if (d == 128)
+      qk_prep_kernel<float, 128><<<g, 256, 0, st>>>(p);
+    else
+      qk_prep_kernel<float, 64><<<g, 256, 0, st>>>(p);
+  }
+  return launch_status("qk_prep_kernel");
+}
+}  // namespace faq
+
+namespace faq {
+static int qk_prep_checked(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb,
+                           int64_t sh, int64_t ss, const float* offset, const float* smooth,
+                           int64_t smooth_head_stride, int smooth_mode, int rotate, int levels, void* out, int64_t ob,
+                           int64_t oh, int64_t os, uint8_t* codes, uint32_t* meta, const void* norm_w, float eps,
+                           const void* cos, const void* sin, int64_t rope_ld, void* stream) {
   FAQ_CHECK_ARG(x && out, "null pointer");
   FAQ_CHECK_ARG(x_dtype == FAQ_BF16 || x_dtype == FAQ_F32, "x_dtype must be FAQ_BF16 or FAQ_F32");
   FAQ_CHECK_ARG(batch >= 0 && heads > 0 && seq >= 0, "bad shape");
@@ -159,6 +232,11 @@ extern "C" int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t he
   FAQ_CHECK_ARG(levels == 0 || levels == 123 || levels == 12 || levels == 13, "levels must be 0, 123, 12 or 13");
   FAQ_CHECK_ARG(levels != 0 || (codes == nullptr && meta == nullptr), "codes/meta need levels");
   FAQ_CHECK_ARG(!codes || (reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
+  FAQ_CHECK_ARG(!norm_w || aligned16(norm_w), "norm_weight must be 16-byte aligned");
+  FAQ_CHECK_ARG(!norm_w || eps >= 0.0f, "eps must be non-negative");
+  FAQ_CHECK_ARG((cos == nullptr) == (sin == nullptr), "cos and sin come together");
+  FAQ_CHECK_ARG(!cos || (aligned16(cos) && aligned16(sin) && rope_ld >= d && rope_ld % 8 == 0),
+                "cos/sin must be 16-byte aligned [seq, rope_ld >= d] tables with rope_ld % 8 == 0");
   if (batch == 0 || seq == 0) return FAQ_OK;
   QkPrepParams p;
   p.x = x;
@@ -180,25 +258,31 @@ extern "C" int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t he
   p.os = os;
   p.codes = codes;
   p.meta = meta;
-  const int64_t vec_elems = x_dtype == FAQ_BF16 ? 8 : 4;
-  p.x_vec = aligned16(x) && sb % vec_elems == 0 && sh % vec_elems == 0 && ss % vec_elems == 0;
-  p.out_vec = aligned16(out) && ob % 8 == 0 && oh % 8 == 0 && os % 8 == 0;
-  const int64_t rows = batch * heads * seq;
-  const int rows_per_block = 8 * (32 / (d / 8));
-  const int64_t blocks = std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
-                                           static_cast<int64_t>(num_sms()) * 16);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned g = static_cast<unsigned>(blocks);
-  if (x_dtype == FAQ_BF16) {
-    if (d == 128)
-      qk_prep_kernel<__nv_bfloat16, 128><<<g, 256, 0, st>>>(p);
-    else
-      qk_prep_kernel<__nv_bfloat16, 64><<<g, 256, 0, st>>>(p);
-  } else {
-    if (d == 128)
-      qk_prep_kernel<float, 128><<<g, 256, 0, st>>>(p);
-    else
-      qk_prep_kernel<float, 64><<<g, 256, 0, st>>>(p);
-  }
-  return launch_status("qk_prep_kernel");
+  p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  p.eps = eps;
+  p.cos = static_cast<const __nv_bfloat16*>(cos);
+  p.sin = static_cast<const __nv_bfloat16*>(sin);
+  p.rope_ld = rope_ld;
+  return qk_prep_launch(p, x_dtype, d, stream);
+}
+}  // namespace faq
+
+extern "C" int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb,
+                           int64_t sh, int64_t ss, const float* offset, const float* smooth, int64_t smooth_head_stride,
+                           int smooth_mode, int rotate, int levels, void* out, int64_t ob, int64_t oh, int64_t os,
+                           uint8_t* codes, uint32_t* meta, void* stream) {
+  return faq::qk_prep_checked(x, x_dtype, batch, heads, seq, d, sb, sh, ss, offset, smooth, smooth_head_stride,
+                              smooth_mode, rotate, levels, out, ob, oh, os, codes, meta, nullptr, 0.0f, nullptr,
+                              nullptr, 0, stream);
+}
+
+extern "C" int faq_qk_norm_rope_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d,
+                                     int64_t sb, int64_t sh, int64_t ss, const void* norm_weight, float eps,
+                                     const void* cos, const void* sin, int64_t rope_ld, const float* offset,
+                                     const float* smooth, int64_t smooth_head_stride, int smooth_mode, int rotate,
+                                     int levels, void* out, int64_t ob, int64_t oh, int64_t os, uint8_t* codes,
+                                     uint32_t* meta, void* stream) {
+  return faq::qk_prep_checked(x, x_dtype, batch, heads, seq, d, sb, sh, ss, offset, smooth, smooth_head_stride,
+                              smooth_mode, rotate, levels, out, ob, oh, os, codes, meta, norm_weight, eps, cos, sin,
+                              rope_ld, stream);
 }

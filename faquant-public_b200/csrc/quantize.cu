@@ -151,6 +151,87 @@ __global__ void __launch_bounds__(256) hif4_quantize_direct_kernel(const T* __re
   }
 }
 
+// ---------------------------------------------------------------- K1, signs-only rotation
+// A rotation without a permutation (the reference's "signs" construction, hisq_rotation.py:
+// 156-167) mixes channels only inside each block of B = 2^LOG2B <= 256 consecutive
+// channels, so no row needs staging: it streams like the direct kernel. A thread holds
+// 8 consecutive channels; the B/8 lanes of a block are consecutive lanes of one warp
+// (k is a multiple of max(64, B), so blocks never straddle a warp or a row). Element
+// pipeline as in the staged kernel below: input_scale rounded to x's dtype, the sign as
+// an exact fp32 negation, butterflies in the reference's stage order (strides 1, 2, 4
+// inside the thread, 8 .. B/2 across lanes), the normalization, one rounding to x's
+// dtype, then HiF4 on the 8-lane 64-blocks.
+template <typename T, int LOG2B>
+__global__ void __launch_bounds__(256) hif4_rotate_signs_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
+                                                                int64_t ldx, const T* __restrict__ input_scale,
+                                                                const int8_t* __restrict__ signs, int levels,
+                                                                QuantOut o) {
+  static_assert(LOG2B >= 3 && LOG2B <= 8, "blocks of 8 .. 256 channels");
+  const int64_t chunks_per_row = k / 8;
+  const int64_t total = rows * chunks_per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t total_warps = (total + 31) / 32 * 32;  // whole warps: every lane shuffles
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx - lane < total_warps;
+       idx += stride) {
+    const bool live = idx < total;
+    const int64_t row = live ? idx / chunks_per_row : 0;
+    const int64_t c = live ? idx % chunks_per_row : 0;
+    const int64_t col = c * 8;
+    float v[8];
+    load8<T>(x + row * ldx + col, v, true, live ? 8 : 0);
+    if (input_scale != nullptr) {
+      float sc[8];
+      load8<T>(input_scale + col, sc, true, live ? 8 : 0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = round_to<T>(__fmul_rn(v[i], sc[i]));
+    }
+    const uint2 sg = live ? *reinterpret_cast<const uint2*>(signs + col) : make_uint2(0, 0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t byte = ((i < 4 ? sg.x : sg.y) >> (8 * (i & 3))) & 0xFFu;
+      if (byte & 0x80u) v[i] = -v[i];  // int8 sign < 0: x * (-1), exact
+    }
+#pragma unroll
+    for (int st = 1; st < 8; st <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if ((i & st) == 0) {
+          const float l = v[i], r = v[i + st];
+          v[i] = __fadd_rn(l, r);
+          v[i + st] = __fsub_rn(l, r);
+        }
+      }
+    }
+#pragma unroll
+    for (int st = 1; st < (1 << (LOG2B - 3)); st <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[i], st);
+        v[i] = (lane & st) ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float r;
+      if constexpr ((LOG2B & 1) == 0)
+        r = __fmul_rn(v[i], pow2f(-(LOG2B / 2)));
+      else
+        r = __fdiv_rn(v[i], static_cast<float>(LOG2B == 3 ? 2.8284271247461903 : LOG2B == 5 ? 5.656854249492381
+                                                                                          : 11.313708498984761));
+      v[i] = round_to<T>(r);
+    }
+    float q[8];
+    uint32_t meta_word;
+    const uint32_t nib = hif4_quant8(v, levels, q, meta_word);
+    if (!live) continue;
+    const int64_t k64 = k;  // k is a multiple of 64 here
+    if (o.codes) reinterpret_cast<uint32_t*>(o.codes + row * (k64 / 2))[c] = nib;
+    if (o.meta && (threadIdx.x & 7) == 0) o.meta[row * (k64 / 64) + c / 8] = meta_word;
+    if (o.qdq) store8<T>(static_cast<T*>(o.qdq) + row * o.ldq + col, q, o.qdq_vec, 8);
+  }
+}
+
 // ---------------------------------------------------------------- K1, rotation
 template <typename T, int LOG2B>
 __global__ void __launch_bounds__(256) hif4_quantize_rotate_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
@@ -827,6 +908,31 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
   int block = rot_block == 0 ? 1 : rot_block;
   int log2b = 0;
   while ((1 << log2b) < block) ++log2b;
+  // signs without a permutation: blocks are independent, the row streams (no staging)
+  if (perm == nullptr && log2b >= 3 && log2b <= 8 && k % 64 == 0 && k % block == 0 && x_vec &&
+      (o.qdq == nullptr || o.qdq_vec) &&
+      (reinterpret_cast<uintptr_t>(signs) & 7) == 0 &&
+      (o.codes == nullptr || (reinterpret_cast<uintptr_t>(o.codes) & 3) == 0)) {
+    const int64_t threads = rows * (k / 8);
+    const int64_t blocks = std::min<int64_t>((threads + 255) / 256, static_cast<int64_t>(sms) * 16);
+    if (blocks == 0) return FAQ_OK;
+#define FAQ_ROTS_CASE(L)                                                                                       \
+  case L:                                                                                                      \
+    hif4_rotate_signs_kernel<T, L><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(                          \
+        static_cast<const T*>(x), rows, k, ldx, static_cast<const T*>(input_scale), signs, levels, o);          \
+    return launch_status("hif4_rotate_signs_kernel");
+    switch (log2b) {
+      FAQ_ROTS_CASE(3)
+      FAQ_ROTS_CASE(4)
+      FAQ_ROTS_CASE(5)
+      FAQ_ROTS_CASE(6)
+      FAQ_ROTS_CASE(7)
+      FAQ_ROTS_CASE(8)
+      default:
+        break;
+    }
+#undef FAQ_ROTS_CASE
+  }
   if constexpr (sizeof(T) == 2) {
     const bool v3 = k % 1024 == 0 && k <= 32768 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
                     (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;

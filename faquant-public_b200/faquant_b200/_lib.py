@@ -36,6 +36,11 @@ SIGNATURES: dict[str, list] = {
                          _c_void_p],
     "faq_qk_prep": [_c_void_p, _int, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _int,
                     _int, _int, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
+    "faq_qk_norm_rope_prep": [_c_void_p, _int, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p,
+                              ctypes.c_float, _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _int, _int,
+                              _int, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
+    "faq_rms_norm": [_c_void_p, _i64, _i64, _i64, _c_void_p, ctypes.c_float, _c_void_p, _i64, _c_void_p],
+    "faq_silu_mul": [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
     "faq_hif4_attention": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _int,
                            _int, _c_void_p, _i64, _i64, _i64, _c_void_p],

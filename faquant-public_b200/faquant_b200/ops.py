@@ -244,6 +244,74 @@ def qk_prep(
     return out, codes, meta
 
 
+def qk_norm_rope_prep(
+    x: torch.Tensor,
+    *,
+    norm_weight: torch.Tensor | None,
+    eps: float = 1e-6,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    levels: str | int | None = "123",
+    rotate: bool = True,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Qwen3 attention operand in one pass: per-head RMSNorm (``norm_weight [D]`` bf16),
+    RoPE (bf16 ``cos``/``sin`` ``[S, D]``, position = sequence index), Hadamard over D,
+    bf16, HiF4. ``x [B, H, S, D]`` bf16, any strides with D contiguous."""
+    device = _require_cuda(x, norm_weight, cos, sin)
+    if x.dim() != 4 or x.dtype != torch.bfloat16:
+        raise ValueError("qk_norm_rope_prep expects bf16 [batch, heads, seq, head_dim]")
+    b, h, s, d = x.shape
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=device)
+    if norm_weight is not None:
+        norm_weight = norm_weight.to(device=device, dtype=torch.bfloat16).contiguous()
+    rope_ld = 0
+    if cos is not None:
+        cos = cos.to(device=device, dtype=torch.bfloat16).contiguous()
+        sin = sin.to(device=device, dtype=torch.bfloat16).contiguous()
+        if cos.shape[0] < s or cos.shape[-1] != d:
+            raise ValueError("cos/sin must be [>= seq, head_dim]")
+        rope_ld = cos.stride(0)
+    lv = 0 if levels is None else levels_code(levels)
+    _lib.call("faq_qk_norm_rope_prep", x.data_ptr(), _dtype_code(x), b, h, s, d, x.stride(0), x.stride(1),
+              x.stride(2), _ptr(norm_weight), float(eps), _ptr(cos), _ptr(sin), rope_ld, None, None, 0, 0,
+              int(rotate), lv, out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), None, None,
+              _stream(device))
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3RMSNorm of bf16 ``x [..., k]`` in one pass."""
+    device = _require_cuda(x, weight)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("rms_norm takes bfloat16")
+    rows, ldx = _rows_view(x)
+    k = x.shape[-1]
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=device)
+    weight = weight.to(device=device, dtype=torch.bfloat16).contiguous()
+    _lib.call("faq_rms_norm", rows.data_ptr(), rows.shape[0], k, ldx, weight.data_ptr(), float(eps), out.data_ptr(),
+              k, _stream(device))
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate) * up`` of a bf16 ``[rows, 2f]`` gate|up tensor, one pass."""
+    device = _require_cuda(gate_up)
+    if gate_up.dtype != torch.bfloat16 or gate_up.dim() != 2 or gate_up.stride(1) != 1:
+        raise TypeError("silu_mul takes a bf16 [rows, 2f] tensor with contiguous rows")
+    rows, two_f = gate_up.shape
+    f = two_f // 2
+    if out is None:
+        out = torch.empty((rows, f), dtype=torch.bfloat16, device=device)
+    _lib.call("faq_silu_mul", gate_up.data_ptr(), rows, f, gate_up.stride(0), out.data_ptr(), out.stride(0),
+              _stream(device))
+    return out
+
+
 def hif4_attention(
     q: torch.Tensor,
     k: torch.Tensor,

@@ -281,14 +281,15 @@ class Qwen3TPPrefill(nn.Module):
         cfg, d = self.cfg, self.cfg.head_dim
         qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
         nq, nk = layer.heads * d, layer.kv_heads * d
-        q = rms_norm(qkv[:, :nq].view(batch, seq, layer.heads, d), layer.q_norm, cfg.eps)
-        k = rms_norm(qkv[:, nq:nq + nk].view(batch, seq, layer.kv_heads, d), layer.k_norm, cfg.eps)
-        v = qkv[:, nq + nk:].view(batch, seq, layer.kv_heads, d)
-        q = self._t("q_rope", index, apply_rope(q, cos, sin))
-        k = self._t("k_rope", index, apply_rope(k, cos, sin))
-        qd = ops.qk_prep(q.transpose(1, 2), levels=cfg.levels, rotate=True)[0]
-        kd = ops.qk_prep(k.transpose(1, 2), levels=cfg.levels, rotate=True)[0]
-        vd = ops.qk_prep(v.transpose(1, 2), levels=cfg.levels, rotate=False)[0]
+        # q_norm/k_norm, RoPE, Hadamard and HiF4 in one K4 pass per operand
+        q = qkv[:, :nq].view(batch, seq, layer.heads, d).transpose(1, 2)
+        k = qkv[:, nq:nq + nk].view(batch, seq, layer.kv_heads, d).transpose(1, 2)
+        v = qkv[:, nq + nk:].view(batch, seq, layer.kv_heads, d).transpose(1, 2)
+        qd = self._t("qd", index, ops.qk_norm_rope_prep(q, norm_weight=layer.q_norm, eps=cfg.eps, cos=cos, sin=sin,
+                                                        levels=cfg.levels))
+        kd = self._t("kd", index, ops.qk_norm_rope_prep(k, norm_weight=layer.k_norm, eps=cfg.eps, cos=cos, sin=sin,
+                                                        levels=cfg.levels))
+        vd = self._t("vd", index, ops.qk_prep(v, levels=cfg.levels, rotate=False)[0])
         out = ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=True, p_levels=cfg.levels,
                                  quantized_normalizer=True)  # [B, S, hq, d]
         return self._t("o", index, layer.o(self._t("attention", index, out).view(batch * seq, nq)))
@@ -300,9 +301,12 @@ class Qwen3TPPrefill(nn.Module):
         cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
         x = torch.nn.functional.embedding(input_ids.reshape(-1), self.embed)  # [T, hidden]
         for i, layer in enumerate(self.layers):
-            x = x + self._attention(layer, rms_norm(x, layer.input_norm, cfg.eps), batch, seq, cos, sin, i)
-            gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, rms_norm(x, layer.post_norm, cfg.eps))))
-            a = self._t("act", i, torch.nn.functional.silu(gu[:, :layer.ffn]) * gu[:, layer.ffn:])
+            x = x + self._attention(layer, ops.rms_norm(self._t("x", i, x), layer.input_norm, cfg.eps), batch, seq,
+                                    cos, sin, i)
+            x = self._t("x_mid", i, x)
+            gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, ops.rms_norm(x, layer.post_norm,
+                                                                                         cfg.eps))))
+            a = self._t("act", i, ops.silu_mul(gu))
             x = x + self._t("down", i, layer.down(a))
         last = self._t("final", len(self.layers), x.view(batch, seq, -1)[:, -1])
         return torch.nn.functional.linear(rms_norm(last, self.final_norm, cfg.eps), self.lm_head).float()

@@ -138,6 +138,36 @@ int faq_qk_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_
                 int64_t ob, int64_t oh, int64_t os, uint8_t* codes, uint32_t* meta, void* stream);
 
 /*
+ * K4 with Qwen3's pre-RoPE steps in front: the per-head RMSNorm of q_norm/k_norm
+ * (HF Qwen3RMSNorm over d: fp32 mean of squares, rsqrt, bf16, times the bf16
+ * `norm_weight` [d], bf16; skipped when null) and RoPE as HF apply_rotary_pos_emb
+ * computes it in bf16 (x cos + rotate_half(x) sin, each product and the sum rounded)
+ * with bf16 tables cos/sin [seq, rope_ld] indexed by the sequence position (skipped
+ * when null), then everything faq_qk_prep does. Replaces the q_norm/k_norm + RoPE +
+ * post-RoPE transform of qwen3._attention_forward (src/faquant/qwen3.py:87-130) in one
+ * HBM pass.
+ */
+int faq_qk_norm_rope_prep(const void* x, int x_dtype, int64_t batch, int64_t heads, int64_t seq, int d,
+                          int64_t sb, int64_t sh, int64_t ss, const void* norm_weight, float eps,
+                          const void* cos, const void* sin, int64_t rope_ld, const float* offset,
+                          const float* smooth, int64_t smooth_head_stride, int smooth_mode, int rotate,
+                          int levels, void* out, int64_t ob, int64_t oh, int64_t os, uint8_t* codes,
+                          uint32_t* meta, void* stream);
+
+/*
+ * Decoder glue, one HBM pass each (bf16, 16-byte aligned rows, strides in elements):
+ * faq_rms_norm: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) per row of k, as HF
+ *   Qwen3RMSNorm (the input_layernorm/post_attention_layernorm the reference's Qwen3
+ *   decoder layers apply before the projections K1 quantizes);
+ * faq_silu_mul: out[:, j] = bf16(bf16(silu(gu[:, j])) * gu[:, f + j]) for a gate|up
+ *   tensor of 2f columns, as Qwen3MLP's act_fn(gate) * up.
+ */
+int faq_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
+                 void* out, int64_t ldo, void* stream);
+int faq_silu_mul(const void* gate_up, int64_t rows, int64_t f, int64_t ld, void* out, int64_t ldo,
+                 void* stream);
+
+/*
  * K5 -- HiF4 QK/PV flash attention on pre-quantized bf16 operands (output of K4).
  * q [batch, hq, sq, 128], k/v [batch, hkv, sk, 128] with element strides, d contiguous;
  * out [batch, sq, hq, 128] bf16 with element strides (ob, os, oh).

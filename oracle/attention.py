@@ -78,8 +78,13 @@ def attention(
     key_chunk: int = 128,
     levels: dict[str, str] | None = None,
     return_f32: bool = False,
+    operands_quantized: bool = False,
 ) -> np.ndarray:
-    """Tiled HiF4 attention; ``q [B,H,Sq,D]``, ``k/v [B,KV,Sk,D]`` -> ``[B,Sq,H,D]``."""
+    """Tiled HiF4 attention; ``q [B,H,Sq,D]``, ``k/v [B,KV,Sk,D]`` -> ``[B,Sq,H,D]``.
+
+    ``operands_quantized``: Q/K/V are already HiF4 operands (a kernel's K4 output) and
+    are used as given (re-fitting HiF4 values is not idempotent); P is still quantized
+    when ``pv_quant``."""
     if normalizer not in ("unquantized", "quantized_same"):
         raise ValueError(f"unsupported normalizer {normalizer!r}")
     lv = {"q": "123", "k": "123", "p": "123", "v": "123"}
@@ -93,9 +98,9 @@ def attention(
         raise ValueError("query heads must be divisible by key/value heads")
     rep = h // kv
     scale = F32(scale if scale is not None else d**-0.5)
-    qo = _qdq_tail(q, lv["q"]) if qk_quant else q
-    ko = _qdq_tail(k, lv["k"]) if qk_quant else k
-    vo = _qdq_tail(v, lv["v"]) if pv_quant else v
+    qo = _qdq_tail(q, lv["q"]) if qk_quant and not operands_quantized else q
+    ko = _qdq_tail(k, lv["k"]) if qk_quant and not operands_quantized else k
+    vo = _qdq_tail(v, lv["v"]) if pv_quant and not operands_quantized else v
     ko = np.repeat(ko, rep, axis=1)
     vo = np.repeat(vo, rep, axis=1)
     out = np.zeros((b, h, sq, d), dtype=F32)

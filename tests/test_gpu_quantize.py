@@ -94,6 +94,33 @@ def test_rotation_blocks_bit_exact(block: int, dtype: torch.dtype, kind: str) ->
         assert np.array_equal(_bits(qdq), _oracle_bits(expect, dtype)), (block, levels)
 
 
+@pytest.mark.parametrize("block", [8, 16, 32, 64, 128, 256])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_signs_only_rotation_streaming_bit_exact(block: int, dtype: torch.dtype) -> None:
+    """Signs without a permutation (the "signs" construction of row-parallel shards): the
+    streaming kernel, with and without an input scale, codes and meta included."""
+    ops = _ops()
+    rng = np.random.default_rng(100 + block)
+    k = 25600 if block <= 256 and 25600 % block == 0 else 4096
+    x = torch.from_numpy(rng.standard_normal((23, k)).astype(np.float32) * 2).to(dtype)
+    x[:, rng.integers(0, k, 5)] *= 30
+    signs = rng.choice([-1, 1], k).astype(np.int8)
+    scale = torch.from_numpy(rng.uniform(0.5, 2.0, k).astype(np.float32)).to(dtype)
+    odt = "bf16" if dtype == torch.bfloat16 else "f32"
+    for levels, use_scale in (("123", False), ("12", True)):
+        qdq, codes, meta = ops.hif4_quantize(x.to(DEV), levels=levels, signs=torch.from_numpy(signs).to(DEV),
+                                             rot_block=block, want_codes=True,
+                                             input_scale=scale.to(DEV) if use_scale else None)
+        expect = olin.quantize_activations(x.float().numpy(), levels=levels, dtype=odt, signs=signs, block=block,
+                                           input_scale=scale.float().numpy() if use_scale else None)
+        assert np.array_equal(_bits(qdq), _oracle_bits(expect, dtype)), (block, levels)
+        xs = x.float().numpy()
+        if use_scale:
+            xs = olin.round_to(xs * scale.float().numpy(), odt)
+        ocodes, ometa = oh.hif4_encode(olin.rotate_input(xs, signs, np.arange(k), block, odt), levels)
+        assert np.array_equal(codes.cpu().numpy(), ocodes) and np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
+
+
 @pytest.mark.parametrize("levels", ["123", "12"])
 @pytest.mark.parametrize("case", LINEAR_CASES, ids=[c[0] for c in LINEAR_CASES])
 def test_linear_fixture_activations_bit_exact(levels: str, case) -> None:

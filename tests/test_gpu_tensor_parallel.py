@@ -117,10 +117,22 @@ def _traced(module):
     return trace
 
 
+def _within_ulp(got: np.ndarray, ref: np.ndarray) -> None:
+    assert np.all(np.abs(got - ref) <= 2.0**-7 * np.abs(ref) + 1e-30)
+
+
+def _mostly_equal(got: np.ndarray, ref: np.ndarray) -> None:
+    """HiF4 operands after a reduction (RMSNorm) whose sum order differs from torch's: a
+    one-ulp difference before K4 can move one 64-block's scale, so most -- not all --
+    values agree."""
+    assert np.mean(got == ref) >= 0.995 and _rel(got, ref) <= 2e-2
+
+
 def test_qwen3_prefill_stages_match_the_oracle() -> None:
-    """Every stage of a 2-layer prefill (one HiF4 layer, one bf16 layer) against the oracle
-    applied to that stage's own GPU input: the W4A4 projections (K1 + GEMM), the torch glue
-    (q/k RMSNorm, RoPE, SiLU), the HiF4 attention (K4 + K5) and the logits."""
+    """Every stage of a 2-layer prefill (one HiF4 layer, one bf16 layer) against the
+    reference's torch glue and the oracle, each applied to that stage's own GPU input:
+    the RMSNorms, the W4A4 projections (K1 + GEMM), the fused q/k norm + RoPE + Hadamard
+    + HiF4 (K4), the HiF4 attention (K5), SwiGLU and the logits."""
     from faquant_b200.tensor_parallel import (Qwen3TPPrefill, TPGroup, apply_rope, default_input_ids, rms_norm,
                                               rope_tables)
 
@@ -134,23 +146,27 @@ def test_qwen3_prefill_stages_match_the_oracle() -> None:
     bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
     for i, L in enumerate(model.layers):
         quant = i not in cfg.bf16_layers
+        _within_ulp(tr[("input_norm", i)].numpy(), rms_norm(bf(tr[("x", i)]), L.input_norm.cpu(), cfg.eps).float().numpy())
         qkv = tr[("qkv", i)]
         _close_linear(qkv.numpy(), _oracle_linear(tr[("input_norm", i)].numpy(), L.qkv, quant))
         nq, nk = L.heads * d, L.kv_heads * d
-        q = apply_rope(rms_norm(bf(qkv[:, :nq]).view(b, s, L.heads, d), L.q_norm.cpu(), cfg.eps), cos, sin)
-        k = apply_rope(rms_norm(bf(qkv[:, nq:nq + nk]).view(b, s, L.kv_heads, d), L.k_norm.cpu(), cfg.eps), cos, sin)
-        assert _rel(tr[("q_rope", i)].numpy(), q.float().numpy()) <= 1e-3
-        assert _rel(tr[("k_rope", i)].numpy(), k.float().numpy()) <= 1e-3
-        qr, kr = oatt.qk_pretransform(tr[("q_rope", i)].transpose(1, 2).numpy(),
-                                      tr[("k_rope", i)].transpose(1, 2).numpy())
-        v = qkv[:, nq + nk:].view(b, s, L.kv_heads, d).transpose(1, 2).numpy()
-        att = oatt.attention(qr, kr, v, causal=True, scale=d**-0.5, normalizer="quantized_same")
+        for name, cols, heads, w in (("qd", slice(0, nq), L.heads, L.q_norm), ("kd", slice(nq, nq + nk), L.kv_heads,
+                                                                               L.k_norm)):
+            r = apply_rope(rms_norm(bf(qkv[:, cols]).view(b, s, heads, d), w.cpu(), cfg.eps), cos, sin)
+            r = r.transpose(1, 2).float().numpy()
+            _mostly_equal(tr[(name, i)].numpy(), oh.fake_quantize(oatt.qk_pretransform(r, r)[0], cfg.levels))
+        v = qkv[:, nq + nk:].reshape(b, s, L.kv_heads, d).transpose(1, 2).numpy()
+        assert np.array_equal(tr[("vd", i)].numpy(), oh.fake_quantize(v, cfg.levels))
+        att = oatt.attention(tr[("qd", i)].numpy(), tr[("kd", i)].numpy(), tr[("vd", i)].numpy(), causal=True,
+                             scale=d**-0.5, normalizer="quantized_same", operands_quantized=True)
         _close_attention(tr[("attention", i)].numpy(), att)
         _close_linear(tr[("o", i)].numpy(), _oracle_linear(tr[("attention", i)].reshape(b * s, nq).numpy(), L.o, quant))
+        _within_ulp(tr[("post_norm", i)].numpy(),
+                    rms_norm(bf(tr[("x_mid", i)]), L.post_norm.cpu(), cfg.eps).float().numpy())
         gu = tr[("gate_up", i)]
         _close_linear(gu.numpy(), _oracle_linear(tr[("post_norm", i)].numpy(), L.gate_up, quant))
         act = torch.nn.functional.silu(bf(gu[:, :L.ffn])) * bf(gu[:, L.ffn:])
-        assert _rel(tr[("act", i)].numpy(), act.float().numpy()) <= 1e-3
+        _within_ulp(tr[("act", i)].numpy(), act.float().numpy())
         _close_linear(tr[("down", i)].numpy(), _oracle_linear(tr[("act", i)].numpy(), L.down, quant))
     final = bf(tr[("final", len(model.layers))])
     ref = torch.nn.functional.linear(rms_norm(final, model.final_norm.cpu(), cfg.eps), model.lm_head.cpu())
