@@ -37,11 +37,25 @@ constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
 struct Params {
   int m, n, k;
   int tiles_m, tiles_n, kblocks;
+  int group_m;  // M tiles per group of the L2-friendly tile order
   const __nv_bfloat16* bias;
   __nv_bfloat16* y;
   int64_t ldy;
   bool y_vec;
 };
+
+// Tile order: groups of group_m M-tiles; inside a group the M tile varies fastest and
+// the group sweeps all N tiles. A wave of 148 CTAs then reads group_m A panels and about
+// 148 / group_m B panels, instead of every A panel (the plain M-fastest order, whose A
+// re-reads from DRAM once per wave are the dominant traffic when A outgrows a die's L2).
+__device__ __forceinline__ void tile_coords(const Params& p, int tile, int& tm, int& tn) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int group = tile / per_group, in_group = tile - group * per_group;
+  const int first_m = group * p.group_m;
+  const int rows = min(p.group_m, p.tiles_m - first_m);
+  tm = first_m + in_group % rows;
+  tn = in_group / rows;
+}
 
 __device__ __forceinline__ void store_row32(const Params& p, int row, int col, const float (&v)[32]) {
   if (row >= p.m || col >= p.n) return;
@@ -114,7 +128,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait_site(smem_addr(&empty[stage]), phase ^ 1, 21, kb)) { ok = false; break; }
           mbar_arrive_expect_tx(smem_addr(&full[stage]), STAGE_BYTES);
@@ -165,7 +180,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_warp(smem_addr(&tfull[acc]), acc_phase, 25, it)) break;
       tc_fence_after();
-      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
       const int row = tm * BM + quarter * 32 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -229,6 +245,9 @@ extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64
   p.k = static_cast<int>(k);
   p.tiles_m = static_cast<int>((m + BM - 1) / BM);
   p.tiles_n = static_cast<int>((n + BN - 1) / BN);
+  // about sqrt(148 * B panel / A panel) = sqrt(148 * 2) ~ 17 M tiles per group minimizes
+  // the panels a wave reads (G A panels + 148 / G B panels, B panels twice as large)
+  p.group_m = std::max(1, std::min(p.tiles_m, 16));
   p.kblocks = static_cast<int>((k + BK - 1) / BK);
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.y = static_cast<__nv_bfloat16*>(y);
