@@ -541,7 +541,8 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 //   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
 //     block maximum, per-4/per-8 maxima in registers, the element code on FP32x2.
 __device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __fadd2_rn(a, make_float2(-b.x, -b.y)); }
+// a - b as one packed FMA: b * -1 + a, a single rounding of the exact difference
+__device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
 
 template <int LOG2B, bool CODES>
 __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
@@ -729,7 +730,9 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
       const Hif4Scale sc = hif4_scale(m1, levels);
       uint32_t lvbits = 0;  // bit qs: lv2 of logical sub-block qs, bit 4+j: lv3 of logical quarter j
-      float2 qm4[8], ds4[8];
+      float2 qm4[8], ds4[8], off4[8];
+      const uint32_t rec_q0 = __float_as_uint(sc.rec) + (2u << 23);  // 4 * rec
+      const uint32_t s_d0 = __float_as_uint(sc.s) - (2u << 23);      // s / 4
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int qs = (i - rot) & 3;
@@ -746,29 +749,33 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
         }
         lvbits |= (lv2 << qs) | (la << (4 + 2 * qs)) | (lb << (5 + 2 * qs));
-        const float qa = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + la)));
-        const float qb = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lb)));
-        const float da = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + la) - 2));
-        const float db = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lb) - 2));
-        qm4[2 * i] = make_float2(qa, qa);
-        qm4[2 * i + 1] = make_float2(qb, qb);
-        ds4[2 * i] = make_float2(da, da);
-        ds4[2 * i + 1] = make_float2(db, db);
+        // 4 qm = rec * 2^(2 - sh) and ds / 4 = s * 2^(sh - 2) by moving the exponent field
+        // (rec and s are normal and stay normal); off = -2^23 * ds / 4 likewise
+        const uint32_t ea = (lv2 + la) << 23, eb = (lv2 + lb) << 23;
+        const uint32_t qa = rec_q0 - ea, qb = rec_q0 - eb, da = s_d0 + ea, db = s_d0 + eb;
+        qm4[2 * i] = make_float2(__uint_as_float(qa), __uint_as_float(qa));
+        qm4[2 * i + 1] = make_float2(__uint_as_float(qb), __uint_as_float(qb));
+        ds4[2 * i] = make_float2(__uint_as_float(da), __uint_as_float(da));
+        ds4[2 * i + 1] = make_float2(__uint_as_float(db), __uint_as_float(db));
+        off4[2 * i] = make_float2(__uint_as_float(da + 0x8B800000u), __uint_as_float(da + 0x8B800000u));
+        off4[2 * i + 1] = make_float2(__uint_as_float(db + 0x8B800000u), __uint_as_float(db + 0x8B800000u));
       }
       uint32_t packed[16];
       uint32_t nib[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        // pair q = values 2q, 2q+1 of slot q / 4, both in its half q / 2
-        const float2 t = __fadd2_rn(__fmul2_rn(a[q], qm4[q >> 1]), make_float2(0.5f, 0.5f));
+        // pair q = values 2q, 2q+1 of slot q / 4, both in its half q / 2:
+        //   t = min(fl(fl(|x| 4qm) + 0.5), 7.5)  (== clamping the code to 7 after the floor)
+        //   r = t + 2^23 rounded toward zero    (== 2^23 + floor(t))
+        //   mag = r * ds/4 - 2^23 * ds/4        (one FMA, exact: code * ds/4 has <= 6 bits)
+        float2 t = __fadd2_rn(__fmul2_rn(a[q], qm4[q >> 1]), make_float2(0.5f, 0.5f));
+        t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
         const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
-        float2 f = __fadd2_rn(r, make_float2(-8388608.0f, -8388608.0f));
-        f = make_float2(fminf(f.x, 7.0f), fminf(f.y, 7.0f));
-        const float2 mag = __fmul2_rn(f, ds4[q >> 1]);
+        const float2 mag = __ffma2_rn(r, ds4[q >> 1], off4[q >> 1]);
         packed[q] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[q];
         if constexpr (CODES) {
-          const uint32_t na = static_cast<uint32_t>(f.x) | ((sgn[q] >> 12) & 8u);
-          const uint32_t nb = static_cast<uint32_t>(f.y) | ((sgn[q] >> 28) & 8u);
+          const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[q] >> 12) & 8u);  // r = 2^23 + code
+          const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[q] >> 28) & 8u);
           nib[q >> 2] |= (na | (nb << 4)) << (8 * (q & 3));
         }
       }
