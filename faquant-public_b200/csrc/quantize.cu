@@ -557,8 +557,10 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                                   // [k]
   unsigned char* s_in = smem_raw + 16 + static_cast<size_t>(k) * 4;                                // [2][k] bf16
-  uint16_t* s_out = reinterpret_cast<uint16_t*>(smem_raw + 16 + static_cast<size_t>(k) * 8);      // [k]
-  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 10);            // [NW][32*TS]
+  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);             // [NW][32*TS]
+  // the rotated row [k] bf16 reuses the transpose scratch once every warp is past its
+  // transpose (NW * 32 * TS * 4 >= 2 k bytes); each warp owns exactly one 1024-chunk
+  uint16_t* s_out = reinterpret_cast<uint16_t*>(s_tr);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
   const int nchunks = k >> 10;
@@ -603,8 +605,9 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       break;
     }
     const unsigned char* in = s_in + buf * row_bytes;
-    for (int ch = warp; ch < nchunks; ch += NW) {
-      float2 p[16];
+    const int ch = warp;  // nchunks <= NW: one chunk per warp (or none)
+    float2 p[16];
+    if (ch < nchunks) {
       const uint4* mrow = reinterpret_cast<const uint4*>(s_map) + (ch << 8) + lane;
 #pragma unroll
       for (int t4 = 0; t4 < 8; ++t4) {
@@ -660,6 +663,9 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
           }
         }
       }
+    }
+    __syncthreads();  // every warp is past its transpose: the scratch now holds the rotated row
+    if (ch < nchunks) {
       // s_out is stored with the 16-byte chunk index c rotated in its low 2 bits by
       // (c >> 3): chunk c of the row lives at (c & ~3) | ((c + (c >> 3)) & 3). Lane writes
       // stay contiguous, and the quantization pass's 16-byte reads (4 consecutive chunks
@@ -800,8 +806,10 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
         if (o.meta && half == 0) o.meta[row * (k / 64) + task / 2] = mb | sc.code;
       }
     }
-    __syncthreads();
+    // no barrier here: the next iteration opens with a CTA-wide one before the scratch is
+    // written again
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------- dequantize
@@ -941,11 +949,11 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
 #undef FAQ_ROTS_CASE
   }
   if constexpr (sizeof(T) == 2) {
-    const bool v3 = k % 1024 == 0 && k <= 32768 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
+    const bool v3 = k % 1024 == 0 && k <= 16384 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
                     (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
     if (v3) {
       const int warps3 = std::min(16, std::max(4, static_cast<int>(k / 1024)));
-      const size_t smem3 = 16 + static_cast<size_t>(k) * 10 + static_cast<size_t>(warps3) * 32 * 34 * 4;
+      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + static_cast<size_t>(warps3) * 32 * 34 * 4;
       if (smem3 <= 200 * 1024) {
         const int per_sm = std::max(1, std::min(8, static_cast<int>((224 * 1024) / (smem3 + 1024))));
         const int64_t blocks3 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
