@@ -55,6 +55,14 @@ class TPGroup:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
+    def comm_stream(self, device: torch.device) -> torch.cuda.Stream:
+        """The side stream the chunked all-reduces run on (one per rank and device)."""
+        key = ("stream", device.index)
+        cache = self.__dict__.setdefault("_streams", {})
+        if key not in cache:
+            cache[key] = torch.cuda.Stream(device=device)
+        return cache[key]
+
 
 def _seed(*parts: object) -> int:
     """Deterministic 63-bit seed of a weight's name (identical on every rank and TP size)."""
@@ -121,10 +129,34 @@ class TPHiF4Linear(nn.Module):
         return ops.hif4_quantize(x, levels=self.levels, signs=r.signs, permutation=r.permutation,
                                  rot_block=r.block if r.signs is not None else None)[0]
 
+    # row chunks of a row-parallel GEMM whose all-reduce overlaps the next chunk's GEMM
+    overlap_chunks = 4
+    overlap_min_rows = 4096
+
     def forward(self, x: torch.Tensor, *, quantized: bool = False) -> torch.Tensor:
         xq = x if quantized else self.quantize_input(x)
-        y = ops.gemm_bf16(xq, self.weight, self.bias)
-        return y if self.reduce is None else self.reduce.all_reduce_(y)
+        tp = self.reduce
+        if tp is None or tp.world == 1:
+            return ops.gemm_bf16(xq, self.weight, self.bias)
+        rows = xq.shape[0]
+        if rows < self.overlap_min_rows:
+            return tp.all_reduce_(ops.gemm_bf16(xq, self.weight, self.bias))
+        # chunk i's all-reduce (side stream, NCCL over NVLink) runs while chunk i + 1's GEMM
+        # computes; the sums are those of one all-reduce of the whole output
+        y = torch.empty((rows, self.weight.shape[0]), dtype=torch.bfloat16, device=xq.device)
+        compute = torch.cuda.current_stream(xq.device)
+        comm = tp.comm_stream(xq.device)
+        step = -(-rows // self.overlap_chunks)
+        step = (step + 127) // 128 * 128
+        for r0 in range(0, rows, step):
+            part = y[r0:r0 + step]
+            ops.gemm_bf16(xq[r0:r0 + step], self.weight, self.bias, out=part)
+            comm.wait_stream(compute)
+            with torch.cuda.stream(comm):
+                tp.all_reduce_(part)
+                part.record_stream(comm)
+        compute.wait_stream(comm)
+        return y
 
 
 # ---------------------------------------------------------------- elementwise glue (torch)

@@ -232,6 +232,17 @@ def _tp_rank(rank: int, world: int, port: int, results) -> None:
         block(x.to(dev))
         mine = {("qwen",) + k: v.numpy() for k, v in tq.items() if k[1] == 0 and k[0] in ("qkv", "attention", "o")}
         mine.update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "attention", "o")})
+        # a row-parallel projection large enough for the chunked, overlapped all-reduce:
+        # with two ranks each element sums two values, so it equals one whole all-reduce
+        from faquant_b200.tensor_parallel import TPHiF4Linear, random_weight, row_rotation
+
+        w = random_weight((768, 2048), 41, dev)[:, rank * 1024:(rank + 1) * 1024]
+        lin = TPHiF4Linear(w, rotation=row_rotation("chunked.o_proj", 2048, tp, seed=17), quantize=True, reduce=tp)
+        xr = torch.randn(5000, 2048, generator=torch.Generator().manual_seed(42)).to(torch.bfloat16)
+        xr = xr[:, rank * 1024:(rank + 1) * 1024].contiguous().to(dev)
+        chunked = lin(xr)
+        lin.overlap_min_rows = 1 << 30
+        mine["chunked_equal"] = bool(torch.equal(chunked, lin(xr)))
         results[rank] = mine  # one assignment: a managed dict hands out copies of its values
         dist.barrier()
     finally:
@@ -258,6 +269,7 @@ def test_tp2_over_nccl_matches_tp1() -> None:
     tw = _traced(block)
     x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
     block(x.to(DEV))
+    assert results[0]["chunked_equal"] and results[1]["chunked_equal"]
     for tag, tr, hq, hkv in (("qwen", tq, 8, 2), ("wan", tw, 4, 4)):
         d = 128
         qkv1 = tr[("qkv", 0)].numpy()
