@@ -98,6 +98,7 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
 #include "qk_prep.cu"
 #include "attention_sm100.cu"
 #include "glue.cu"
+#include "decode.cu"
 
 extern "C" int faq_version(void) { return 100; }
 

@@ -44,6 +44,9 @@ SIGNATURES: dict[str, list] = {
     "faq_hif4_attention": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _int,
                            _int, _c_void_p, _i64, _i64, _i64, _c_void_p],
+    "faq_hif4_decode_attention": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
+                                  _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int,
+                                  _int, _c_void_p, _i64, _i64, _i64, _c_void_p, ctypes.c_size_t, _c_void_p],
     "faq_selftest_wait_timeout": [_i64, _c_void_p],
     "faq_device_trace": [ctypes.POINTER(ctypes.c_uint), _int, _int],
 }
@@ -71,6 +74,9 @@ def load() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = ctypes.c_int
+            # size queries return size_t, not a status
+            lib.faq_hif4_decode_workspace_bytes.argtypes = [_i64, _i64, _i64, _i64, _i64, _int]
+            lib.faq_hif4_decode_workspace_bytes.restype = ctypes.c_size_t
             _lib = lib
         return _lib
 

@@ -351,3 +351,50 @@ def hif4_attention(
               v.stride(0), v.stride(1), v.stride(2), scale, int(causal), lv, int(quantized_normalizer),
               out.data_ptr(), out.stride(0), out.stride(1), out.stride(2), _stream(device))
     return out
+
+
+def hif4_decode_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    scale: float | None = None,
+    p_levels: str | int | None = "123",
+    quantized_normalizer: bool = True,
+    out: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Decode-step HiF4 attention: ``q [B, Hq, Sq, 128]`` (the last Sq positions, Sq small)
+    against ``k/v [B, Hkv, Sk, 128]`` (the whole cache), pre-quantized bf16 operands;
+    returns ``[B, Sq, Hq, 128]``. Same semantics as :func:`hif4_attention` with causal
+    masking; the keys are split over the GPU (exact running max per tile)."""
+    device = _require_cuda(q, k, v)
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.dim() != 4:
+            raise TypeError("hif4_decode_attention takes rank-4 bfloat16 Q/K/V")
+    b, hq, sq, d = q.shape
+    _, hkv, sk, _ = k.shape
+    if v.shape != k.shape:
+        raise ValueError("K and V shapes differ")
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+
+    def fix(t: torch.Tensor) -> torch.Tensor:
+        ok = t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+        return t if ok else t.contiguous()
+
+    k, v = fix(k), fix(v)
+    need = int(_lib.load().faq_hif4_decode_workspace_bytes(b, hq, hkv, sq, sk, d))
+    if need == 0:
+        raise ValueError("unsupported decode shape")
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    if out is None:
+        out = torch.empty((b, sq, hq, d), dtype=torch.bfloat16, device=device)
+    scale = float(scale if scale is not None else d**-0.5)
+    lv = 0 if p_levels is None else levels_code(p_levels)
+    _lib.call("faq_hif4_decode_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), b, hq, hkv, sq, sk, d,
+              q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+              v.stride(2), scale, lv, int(quantized_normalizer), out.data_ptr(), out.stride(0), out.stride(1),
+              out.stride(2), workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream(device))
+    return out

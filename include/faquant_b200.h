@@ -187,6 +187,26 @@ int faq_hif4_attention(const void* q, const void* k, const void* v, int64_t batc
                        int64_t vs, float scale, int causal, int p_levels, int normalizer_quantized,
                        void* out, int64_t ob, int64_t os, int64_t oh, void* stream);
 
+/*
+ * K6 -- HiF4 attention decode: sq (<= 32 / (hq / hkv)) new query positions against a
+ * cache of sk keys, the queries being the last sq positions (bottom-right causal).
+ * Same semantics and operand contract as faq_hif4_attention (pre-quantized bf16 Q/K/V;
+ * out [batch, sq, hq, 128]), the decode call of simulated_flash_attention_forward
+ * (simulated_flash_attention.py:457-909 with a growing cache). The keys are split over
+ * the GPU in three passes (scores and per-tile row maxima; P and P.V per split of 8 key
+ * tiles starting from the exact running max before the split, so every tile's HiF4 P is
+ * the sequential one; the join of the splits). `workspace` is a caller-owned device
+ * buffer of at least faq_hif4_decode_workspace_bytes(...) bytes (scores, tile maxima and
+ * per-split partial results); it needs no initialization.
+ */
+size_t faq_hif4_decode_workspace_bytes(int64_t batch, int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int d);
+int faq_hif4_decode_attention(const void* q, const void* k, const void* v, int64_t batch, int64_t hq,
+                              int64_t hkv, int64_t sq, int64_t sk, int d, int64_t qb, int64_t qh,
+                              int64_t qs, int64_t kb, int64_t kh, int64_t ks, int64_t vb, int64_t vh,
+                              int64_t vs, float scale, int p_levels, int normalizer_quantized, void* out,
+                              int64_t ob, int64_t os, int64_t oh, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* Diagnostics: copy up to max_records records of the waits that gave up (3 words
  * each: site | tile << 8, blockIdx.x | blockIdx.y << 16, blockIdx.z) into `records`
  * (host memory); returns the number of timeouts recorded (>= 0) or -FAQ_ERR_*.
