@@ -115,6 +115,38 @@ def _update_stats(module, b, h, kv, sq, sk, d, query_chunk, key_chunk, causal, q
         stats["pv_quantized_tiles"] += tiles
 
 
+DECODE_MAX_QUERIES = 16  # query positions up to which a causal call runs the decode kernel
+
+
+def _cached_decode_quantize(module, tensor: torch.Tensor, operand: str, enabled: bool, query_length: int):
+    """K/V HiF4 operands with the reference's append cache (``_cached_decode_quantize``,
+    ``simulated_flash_attention.py:243-289``): HiF4 groups run along head_dim only, so a
+    decode step quantizes just the appended position and concatenates it to the cached
+    operand -- identical to re-quantizing the whole cache."""
+    name = f"faquant_{operand}_matmul_qdq_cache"
+    if not enabled:
+        setattr(module, name, None)
+        return tensor.to(torch.bfloat16)
+    cached = getattr(module, name, None)
+    can_append = (
+        query_length == 1
+        and isinstance(cached, torch.Tensor)
+        and cached.device == tensor.device
+        and cached.dtype == torch.bfloat16
+        and cached.shape[:-2] == tensor.shape[:-2]
+        and cached.shape[-1] == tensor.shape[-1]
+        and cached.shape[-2] + 1 == tensor.shape[-2]
+    )
+    levels = ops.default_levels(operand)
+    if can_append:
+        tail = ops.qk_prep(tensor[..., cached.shape[-2]:, :], levels=levels, rotate=False)[0]
+        quantized = torch.cat((cached, tail), dim=-2)
+    else:
+        quantized = ops.qk_prep(tensor, levels=levels, rotate=False)[0]
+    setattr(module, name, quantized)
+    return quantized
+
+
 def simulated_flash_attention_forward(
     module: torch.nn.Module,
     query: torch.Tensor,
@@ -187,11 +219,16 @@ def simulated_flash_attention_forward(
         raise NotImplementedError("faquant_b200 attention needs head_dim 128")
 
     qo = ops.qk_prep(query, levels=ops.default_levels("q"), rotate=False)[0] if qk_quant else query.to(torch.bfloat16)
-    ko = ops.qk_prep(key, levels=ops.default_levels("k"), rotate=False)[0] if qk_quant else key.to(torch.bfloat16)
-    vo = ops.qk_prep(value, levels=ops.default_levels("v"), rotate=False)[0] if pv_quant else value.to(torch.bfloat16)
-    out = ops.hif4_attention(qo, ko, vo, scale=scale, causal=causal,
-                             p_levels=ops.default_levels("p") if pv_quant else None,
-                             quantized_normalizer=mode == "quantized_same")
+    ko = _cached_decode_quantize(module, key, "k", qk_quant, sq)
+    vo = _cached_decode_quantize(module, value, "v", pv_quant, sq)
+    p_levels = ops.default_levels("p") if pv_quant else None
+    if causal and sq <= DECODE_MAX_QUERIES and (h // kv) * sq <= 32:
+        # a decode step: K6 spreads the cache over the GPU with the same semantics
+        out = ops.hif4_decode_attention(qo, ko, vo, scale=scale, p_levels=p_levels,
+                                        quantized_normalizer=mode == "quantized_same")
+    else:
+        out = ops.hif4_attention(qo, ko, vo, scale=scale, causal=causal, p_levels=p_levels,
+                                 quantized_normalizer=mode == "quantized_same")
     _update_stats(module, b, h, kv, sq, sk, d, query_chunk, key_chunk, causal, qk_quant, pv_quant)
     return (out if out.dtype == query.dtype else out.to(query.dtype)), None
 

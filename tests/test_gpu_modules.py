@@ -117,6 +117,34 @@ def test_attention_backend_matches_reference_fixture(case) -> None:
     assert module.faquant_simulated_attention_stats == json.loads(bytes(g[f"{tag}_stats"]).decode())
 
 
+def test_attention_backend_decode_steps_with_qdq_cache() -> None:
+    """Prefill, then three decode steps through the backend: the K/V QDQ caches grow by
+    appending one quantized position (bit-identical to re-quantizing the whole cache, as
+    the reference's _cached_decode_quantize guarantees) and each step -- run by the decode
+    kernel -- matches the oracle over the whole cache."""
+    from faquant_b200 import ops
+    from faquant_b200.attention import simulated_flash_attention_forward
+
+    module = _module(True, "quantized_same", True, True)
+    g = torch.Generator().manual_seed(11)
+    b, h, kv, s0 = 1, 8, 2, 300
+    q = torch.randn(b, h, s0 + 3, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, kv, s0 + 3, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, kv, s0 + 3, 128, generator=g).to(torch.bfloat16)
+    simulated_flash_attention_forward(module, q[:, :, :s0].to(DEV), k[:, :, :s0].to(DEV), v[:, :, :s0].to(DEV), None)
+    for step in range(3):
+        n = s0 + step + 1
+        out, _ = simulated_flash_attention_forward(module, q[:, :, n - 1:n].to(DEV), k[:, :, :n].to(DEV),
+                                                   v[:, :, :n].to(DEV), None)
+        assert torch.equal(module.faquant_k_matmul_qdq_cache, ops.qk_prep(k[:, :, :n].to(DEV), levels="123",
+                                                                           rotate=False)[0])
+        assert torch.equal(module.faquant_v_matmul_qdq_cache, ops.qk_prep(v[:, :, :n].to(DEV), levels="123",
+                                                                           rotate=False)[0])
+        ref = oatt.attention(q[:, :, n - 1:n].float().numpy(), k[:, :, :n].float().numpy(),
+                             v[:, :, :n].float().numpy(), causal=True, normalizer="quantized_same")
+        _close_attention(out, ref)
+
+
 def test_attention_backend_all_valid_mask_is_the_unmasked_path() -> None:
     from faquant_b200.attention import simulated_flash_attention_forward
 
