@@ -365,3 +365,64 @@ extern "C" int faq_hif4_decode_attention(const void* q, const void* k, const voi
   FAQ_CHECK_ARG(workspace_bytes >= need, "workspace too small: faq_hif4_decode_workspace_bytes() bytes needed");
   return decode_launch(p, static_cast<float*>(workspace), stream);
 }
+
+// ---------------------------------------------------------------- allocation-free decode
+// A decode call for callers that cannot allocate device memory: a serving runtime that
+// plans all of its memory at start-up and forbids allocations while it serves, or a host
+// hot path where cudaMalloc would synchronize the device. Instead of a caller workspace
+// the three passes use one file-scope scratch array of FAQ_DECODE_STATIC_SCRATCH_BYTES
+// (16 MiB), which every GPU that loads this library holds until the process exits.
+//   - The kernels write every scratch word they read within the same call (scores and
+//     tile maxima in pass 1, partial results in pass 2), so nothing has to start at zero.
+//   - All calls on a device share the one array: calls that may overlap on that GPU
+//     (different streams without ordering between them) race; order them on one stream.
+//   - The array's device address is looked up (cudaGetSymbolAddress) on the first call on
+//     each device, with that device current, and cached; make that first call before
+//     any stream capture. No call allocates.
+namespace faq {
+namespace dec {
+constexpr size_t STATIC_SCRATCH_BYTES = size_t(16) << 20;
+static __device__ __align__(256) float g_static_scratch[STATIC_SCRATCH_BYTES / sizeof(float)];
+constexpr int MAX_DEVICES = 64;
+static float* g_static_scratch_ptr[MAX_DEVICES] = {};
+static std::mutex g_static_scratch_mutex;
+
+static int static_scratch(float** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (dev < 0 || dev >= MAX_DEVICES) return fail(FAQ_ERR_UNSUPPORTED, "device ordinal beyond 63");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(decode scratch)");
+    g_static_scratch_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_static_scratch_ptr[dev];
+  return FAQ_OK;
+}
+}  // namespace dec
+}  // namespace faq
+
+extern "C" int faq_hif4_decode_attention_static(const void* q, const void* k, const void* v, int64_t batch,
+                                                int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int d, int64_t qb,
+                                                int64_t qh, int64_t qs, int64_t kb, int64_t kh, int64_t ks,
+                                                int64_t vb, int64_t vh, int64_t vs, float scale, int p_levels,
+                                                int normalizer_quantized, void* out, int64_t ob, int64_t os,
+                                                int64_t oh, void* stream) {
+  using namespace faq;
+  dec::Params p;
+  int rc = decode_setup(p, q, k, v, batch, hq, hkv, sq, sk, d, qb, qh, qs, kb, kh, ks, vb, vh, vs, scale, p_levels,
+                        normalizer_quantized, out, ob, os, oh);
+  if (rc) return rc;
+  const size_t need = faq_hif4_decode_workspace_bytes(batch, hq, hkv, sq, sk, d);
+  if (need > dec::STATIC_SCRATCH_BYTES)
+    return fail(FAQ_ERR_ARG, "decode needs " + std::to_string(need) +
+                                 " bytes of scratch, more than the 16 MiB static array of "
+                                 "faq_hif4_decode_attention_static; use faq_hif4_decode_attention with a workspace");
+  float* scratch = nullptr;
+  rc = dec::static_scratch(&scratch);
+  if (rc) return rc;
+  return decode_launch(p, scratch, stream);
+}

@@ -207,6 +207,24 @@ int faq_hif4_decode_attention(const void* q, const void* k, const void* v, int64
                               int64_t ob, int64_t os, int64_t oh, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/*
+ * faq_hif4_decode_attention without a workspace argument, for callers that cannot
+ * allocate device memory (a runtime that plans all of its memory at start-up and forbids
+ * allocations while serving; a host hot path where cudaMalloc would synchronize the
+ * device). No counterpart in the reference: it is this library's allocation-free variant.
+ * Its scratch is one 16 MiB file-scope device array that every GPU loading the library
+ * holds until exit; problems whose faq_hif4_decode_workspace_bytes(...) exceeds 16 MiB
+ * are rejected with FAQ_ERR_ARG. The array's address is looked up on the first call on
+ * each device (make that call before any stream capture); nothing in it must start at
+ * zero; calls that may overlap on one GPU share the array and race -- order them.
+ */
+int faq_hif4_decode_attention_static(const void* q, const void* k, const void* v, int64_t batch,
+                                     int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int d,
+                                     int64_t qb, int64_t qh, int64_t qs, int64_t kb, int64_t kh,
+                                     int64_t ks, int64_t vb, int64_t vh, int64_t vs, float scale,
+                                     int p_levels, int normalizer_quantized, void* out, int64_t ob,
+                                     int64_t os, int64_t oh, void* stream);
+
 /* Diagnostics: copy up to max_records records of the waits that gave up (3 words
  * each: site | tile << 8, blockIdx.x | blockIdx.y << 16, blockIdx.z) into `records`
  * (host memory); returns the number of timeouts recorded (>= 0) or -FAQ_ERR_*.
