@@ -379,6 +379,11 @@ def main_arm(args) -> None:
             "gpu_launches_per_step": launches_att,
         }
 
+    # ---------------- decode step (K6): one new token per sequence against a 32K-key cache
+    dec = None
+    if A is not None:
+        dec = run_decode(args, device, pk, barrier, dist)
+
     # ---------------- sharded workloads (configs 4 and 5), strong scaling over the ranks
     tp_lines = {}
     if not args.no_tp:
@@ -462,6 +467,7 @@ def main_arm(args) -> None:
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "attention": att,
+            "decode": dec,
             **tp_lines,
             "e2e": e2e,
         }
@@ -493,6 +499,30 @@ def _timed(fn, steps: int, warmup: int, barrier, dist, device) -> float:
     if dist is not None:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     return float(ms.item())
+
+
+def run_decode(args, device, pk: dict, barrier, dist) -> dict:
+    """Config-3 shapes in decode: batch 1, 32 q / 8 kv heads, one new position against a
+    cache of 32768 keys (HiF4 operands prepared once, as the append cache keeps them)."""
+    import torch
+
+    from faquant_b200 import ops
+
+    b, hq, hkv, sk = 1, ATT["hq"], ATT["hkv"], ATT["seq"]
+    g = torch.Generator(device=device).manual_seed(11)
+    q = ops.qk_prep(torch.randn(b, hq, 1, 128, device=device, generator=g).to(torch.bfloat16), levels="123")[0]
+    k = ops.qk_prep(torch.randn(b, hkv, sk, 128, device=device, generator=g).to(torch.bfloat16), levels="123")[0]
+    v = ops.qk_prep(torch.randn(b, hkv, sk, 128, device=device, generator=g).to(torch.bfloat16), levels="123",
+                    rotate=False)[0]
+    ws = torch.empty(int(ops._lib.load().faq_hif4_decode_workspace_bytes(b, hq, hkv, 1, sk, 128)),
+                     dtype=torch.uint8, device=device)
+    out = torch.empty(b, 1, hq, 128, dtype=torch.bfloat16, device=device)
+    ms = _timed(lambda: ops.hif4_decode_attention(q, k, v, out=out, workspace=ws), 20, 3, barrier, dist, device)
+    kv_bytes = 2 * b * hkv * sk * 128 * 2
+    return {"workload": "qwen3-8b decode step: 1 token, 32/8 heads, 32768-key HiF4 K/V cache (config-3 shapes)",
+            "ms_per_step": ms, "tokens_per_s": b / (ms * 1e-3), "kv_bytes": kv_bytes,
+            "achieved_gbs": kv_bytes / (ms * 1e-3) / 1e9, "frac_of_hbm_peak": kv_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+            "gpu_launches_per_step": 3, "steps": 20}
 
 
 def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dist) -> dict:

@@ -62,56 +62,146 @@ __host__ __device__ inline size_t workspace_floats(int64_t bh, int64_t rows, int
 // row r of a group: query head g = r / sq, query position i = r % sq; its last visible key
 __device__ __forceinline__ int last_key(const Params& p, int r) { return p.sk - p.sq + (r % p.sq); }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---------------------------------------------------------------- pass 1
 // A half-warp per key (16 lanes x 8 channels), two keys per warp step; the R query rows
 // of the group sit in shared memory as fp32.
-__global__ void __launch_bounds__(THREADS) decode_scores_kernel(Params p) {
-  __shared__ __align__(16) float s_q[MAX_ROWS * D];
-  __shared__ float s_s[MAX_ROWS * TILE];
+constexpr int KS = D + 8;  // staged K row stride (elements): 16 bytes of padding per row
+                           // puts neighbouring keys on different banks
+// Scores of rows r0 .. r0 + RC - 1 for the whole tile: a half-warp per key (8 channels
+// per lane, keys from the staged tile), the rows' q channels in registers. The RC partial
+// dot products of a lane are reduced over the 16 lanes by a transposed butterfly -- each
+// exchange keeps half of the rows and sends the other half (8 rows: 4 + 2 + 1 + 1
+// shuffles instead of 8 x 4; 4 rows: 2 + 1 + 1 + 1) -- and lane (16 / RC) j ends with
+// row j's total. Rows past p.rows read zero q rows and are not stored.
+template <int RC>
+__device__ __forceinline__ void score_rows(const Params& p, const __nv_bfloat16* s_k, const float* s_q, float* s_s,
+                                           int tile, int warp, int half, int sub, int r0) {
+  constexpr int STEPS = TILE / (2 * (THREADS / 32));
+  float qr[RC][8];
+#pragma unroll
+  for (int j = 0; j < RC; ++j) {
+    const float4 qa = *reinterpret_cast<const float4*>(s_q + (r0 + j) * D + sub * 8);
+    const float4 qc = *reinterpret_cast<const float4*>(s_q + (r0 + j) * D + sub * 8 + 4);
+    qr[j][0] = qa.x; qr[j][1] = qa.y; qr[j][2] = qa.z; qr[j][3] = qa.w;
+    qr[j][4] = qc.x; qr[j][5] = qc.y; qr[j][6] = qc.z; qr[j][7] = qc.w;
+  }
+#pragma unroll 2
+  for (int step = 0; step < STEPS; ++step) {
+    const int kk = step * 2 * (THREADS / 32) + warp * 2 + half;
+    const int key = tile * TILE + kk;
+    const uint4 kcur = *reinterpret_cast<const uint4*>(s_k + kk * KS + sub * 8);
+    const uint32_t w[4] = {kcur.x, kcur.y, kcur.z, kcur.w};
+    float kv[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      kv[2 * i] = __uint_as_float(w[i] << 16);
+      kv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+    float v[RC];
+#pragma unroll
+    for (int j = 0; j < RC; ++j) {
+      float acc = __fmul_rn(qr[j][0], kv[0]);
+#pragma unroll
+      for (int c = 1; c < 8; ++c) acc = __fmaf_rn(qr[j][c], kv[c], acc);
+      v[j] = acc;
+    }
+    const bool b3 = sub & 8, b2 = sub & 4, b1 = sub & 2;
+    float tot;
+    int r;
+    if constexpr (RC == 8) {
+      float u4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float send = b3 ? v[i] : v[i + 4];
+        const float keep = b3 ? v[i + 4] : v[i];
+        u4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      float u2[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float send = b2 ? u4[i] : u4[i + 2];
+        const float keep = b2 ? u4[i + 2] : u4[i];
+        u2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      const float send = b1 ? u2[0] : u2[1];
+      const float keep = b1 ? u2[1] : u2[0];
+      tot = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+      tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+      r = r0 + (b3 ? 4 : 0) + (b2 ? 2 : 0) + (b1 ? 1 : 0);
+    } else {
+      float u2[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float send = b3 ? v[i] : v[i + 2];
+        const float keep = b3 ? v[i + 2] : v[i];
+        u2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      const float send = b2 ? u2[0] : u2[1];
+      const float keep = b2 ? u2[1] : u2[0];
+      tot = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+      tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+      r = r0 + (b3 ? 2 : 0) + (b2 ? 1 : 0);
+    }
+    const bool writer = (sub & (16 / RC - 1)) == 0;
+    if (writer && r < p.rows) s_s[r * TILE + kk] = (key <= last_key(p, r)) ? tot : -INFINITY;
+  }
+}
+
+// Dynamic shared memory: the K tile (staged by cp.async, all of it in flight at once),
+// the group's q rows in fp32, the tile's scores.
+constexpr size_t SCORES_SMEM = TILE * KS * 2 + MAX_ROWS * D * 4 + MAX_ROWS * TILE * 4;
+
+__global__ void __launch_bounds__(THREADS, 2) decode_scores_kernel(Params p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* s_k = reinterpret_cast<__nv_bfloat16*>(smem_raw);   // [TILE][D]
+  float* s_q = reinterpret_cast<float*>(s_k + TILE * KS);             // [MAX_ROWS][D]
+  float* s_s = s_q + MAX_ROWS * D;                                    // [MAX_ROWS][TILE]
   const int tile = blockIdx.x, bh = blockIdx.y;
   const int b = bh / p.hkv, hk = bh % p.hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int i = tid; i < p.rows * D; i += THREADS) {
-    const int r = i / D, dd = i % D;
-    const int g = r / p.sq, pos = r % p.sq;  // query head in the group, position in q
-    const int64_t off = b * p.qb + static_cast<int64_t>(hk * p.group + g) * p.qh + static_cast<int64_t>(pos) * p.qs + dd;
-    s_q[i] = __bfloat162float(p.q[off]);
+  {
+    const __nv_bfloat16* kbase = p.k + b * p.kb + hk * p.kh;
+    for (int i = tid; i < TILE * D / 8; i += THREADS) {
+      const int key = tile * TILE + i / (D / 8), c8 = i % (D / 8);
+      __nv_bfloat16* dst = s_k + (i / (D / 8)) * KS + c8 * 8;
+      if (key < p.sk)
+        cp_async16(dst, kbase + static_cast<int64_t>(key) * p.ks + c8 * 8);
+      else
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
   }
+  const int rows8 = (p.rows + 7) / 8 * 8;
+  for (int i = tid; i < rows8 * (D / 8); i += THREADS) {  // 8 channels per thread, 16-byte loads
+    const int r = i / (D / 8), c8 = i % (D / 8);
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (r < p.rows) {
+      const int g = r / p.sq, pos = r % p.sq;  // query head in the group, position in q
+      const uint4 u = *reinterpret_cast<const uint4*>(p.q + b * p.qb + static_cast<int64_t>(hk * p.group + g) * p.qh +
+                                                      static_cast<int64_t>(pos) * p.qs + c8 * 8);
+      lo = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                       __uint_as_float(u.y & 0xFFFF0000u));
+      hi = make_float4(__uint_as_float(u.z << 16), __uint_as_float(u.z & 0xFFFF0000u), __uint_as_float(u.w << 16),
+                       __uint_as_float(u.w & 0xFFFF0000u));
+    }
+    *reinterpret_cast<float4*>(s_q + r * D + c8 * 8) = lo;
+    *reinterpret_cast<float4*>(s_q + r * D + c8 * 8 + 4) = hi;
+  }
+  cp_async_wait_all();
   __syncthreads();
   const int half = lane >> 4, sub = lane & 15;
-  // every lane runs the same TILE / 16 steps (the reductions shuffle the whole warp)
-  for (int step = 0; step < TILE / (2 * (THREADS / 32)); ++step) {
-    const int kk = step * 2 * (THREADS / 32) + warp * 2 + half;
-    const int key = tile * TILE + kk;
-    float kv[8];
-    if (key < p.sk) {
-      const uint4 u = *reinterpret_cast<const uint4*>(p.k + b * p.kb + hk * p.kh + static_cast<int64_t>(key) * p.ks + sub * 8);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kv[2 * i] = __uint_as_float(w[i] << 16);
-        kv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) kv[i] = 0.0f;
-    }
-    for (int r = 0; r < p.rows; ++r) {
-      const float4 qa = *reinterpret_cast<const float4*>(s_q + r * D + sub * 8);
-      const float4 qc = *reinterpret_cast<const float4*>(s_q + r * D + sub * 8 + 4);
-      float acc = qa.x * kv[0];
-      acc = __fmaf_rn(qa.y, kv[1], acc);
-      acc = __fmaf_rn(qa.z, kv[2], acc);
-      acc = __fmaf_rn(qa.w, kv[3], acc);
-      acc = __fmaf_rn(qc.x, kv[4], acc);
-      acc = __fmaf_rn(qc.y, kv[5], acc);
-      acc = __fmaf_rn(qc.z, kv[6], acc);
-      acc = __fmaf_rn(qc.w, kv[7], acc);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (sub == 0) s_s[r * TILE + kk] = (key <= last_key(p, r)) ? acc : -INFINITY;
-    }
-  }
+  if (p.rows <= 4)
+    score_rows<4>(p, s_k, s_q, s_s, tile, warp, half, sub, 0);
+  else
+    for (int r0 = 0; r0 < p.rows; r0 += 8) score_rows<8>(p, s_k, s_q, s_s, tile, warp, half, sub, r0);
   __syncthreads();
   float* dst = p.scores + (static_cast<int64_t>(bh) * p.rows) * (p.ntiles * TILE) + static_cast<int64_t>(tile) * TILE;
   for (int i = tid; i < p.rows * TILE; i += THREADS) {
@@ -135,15 +225,37 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+
+// Dynamic shared memory: two V tiles (the next one arrives by cp.async while this one is
+// multiplied), P of the tile in bf16, the two key halves' partial O, per-row scalars.
+constexpr size_t PV_SMEM = 2 * TILE * D * 2 + MAX_ROWS * TILE * 2 + 2 * MAX_ROWS * D * 4 + 3 * MAX_ROWS * 4;
+
 __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
-  __shared__ __align__(16) __nv_bfloat16 s_p[MAX_ROWS * TILE];  // P of the tile as the bf16 PV operand
-  __shared__ __align__(16) __nv_bfloat16 s_v[TILE * D];     // the V tile
-  __shared__ float s_m[MAX_ROWS], s_alpha[MAX_ROWS], s_sum[MAX_ROWS];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __nv_bfloat16* s_vbuf = reinterpret_cast<__nv_bfloat16*>(smem_raw);                     // [2][TILE][D]
+  __nv_bfloat16* s_p = s_vbuf + 2 * TILE * D;                                              // [MAX_ROWS][TILE]
+  float* s_o = reinterpret_cast<float*>(s_p + MAX_ROWS * TILE);                            // [2][MAX_ROWS][D]
+  float* s_m = s_o + 2 * MAX_ROWS * D;
+  float* s_alpha = s_m + MAX_ROWS;
+  float* s_sum = s_alpha + MAX_ROWS;
   const int split = blockIdx.x, bh = blockIdx.y;
   const int b = bh / p.hkv, hk = bh % p.hkv;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = split * SPLIT_TILES, t1 = min(p.ntiles, t0 + SPLIT_TILES);
   const float* tmax = p.tmax + static_cast<int64_t>(bh) * p.rows * p.ntiles;
+  const __nv_bfloat16* vbase = p.v + b * p.vb + hk * p.vh;
+  auto prefetch_v = [&](int t, int buf) {
+    __nv_bfloat16* dst = s_vbuf + buf * TILE * D;
+    for (int i = tid; i < TILE * D / 8; i += THREADS) {
+      const int key = t * TILE + i / (D / 8), c8 = i % (D / 8);
+      if (key < p.sk)
+        cp_async16(dst + i * 8, vbase + static_cast<int64_t>(key) * p.vs + c8 * 8);
+      else
+        *reinterpret_cast<uint4*>(dst + i * 8) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
+  };
+  prefetch_v(t0, 0);
   // running max before the split (log2 domain): max over the earlier tiles' maxima
   for (int r = warp; r < p.rows; r += THREADS / 32) {
     float m = -INFINITY;
@@ -152,12 +264,14 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane == 0) s_m[r] = m == -INFINITY ? -INFINITY : __fmul_rn(m, p.scale_log2);
   }
-  // O accumulators: thread (row group, 4 channels); rows_per_warp rows per warp
-  const int rows_per_warp = (p.rows + 7) / 8;  // <= 4
-  float acc[4][4];
-  float l_run[4];
+  // P.V work split: warp = (key half kh, row group rg); rows rg*rpw .. rg*rpw + rpw - 1,
+  // keys 64 kh .. 64 kh + 63 of each tile; lane = 4 channels
+  const int kh = warp & 1, rg = warp >> 1;
+  const int rpw = (p.rows + 3) / 4;  // <= 8
+  float acc[8][4];
+  float l_run[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 8; ++j) {
     l_run[j] = 0.0f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[j][c] = 0.0f;
@@ -165,12 +279,11 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
   __syncthreads();
   const float* sc = p.scores + static_cast<int64_t>(bh) * p.rows * (p.ntiles * TILE);
   for (int t = t0; t < t1; ++t) {
-    // V tile into shared memory (rows past the cache end read as zero)
-    for (int i = tid; i < TILE * D / 8; i += THREADS) {
-      const int key = t * TILE + i / (D / 8), c8 = i % (D / 8);
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (key < p.sk) u = *reinterpret_cast<const uint4*>(p.v + b * p.vb + hk * p.vh + static_cast<int64_t>(key) * p.vs + c8 * 8);
-      reinterpret_cast<uint4*>(s_v)[i] = u;
+    const int buf = (t - t0) & 1;
+    if (t + 1 < t1) {
+      prefetch_v(t + 1, buf ^ 1);
+    } else {
+      cp_async_commit();  // an empty group keeps the wait count uniform
     }
     // new running max and alpha per row (the reference's order: max includes this tile)
     if (tid < p.rows) {
@@ -193,11 +306,12 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
       const float m = s_m[r];
       const float m_use = m == -INFINITY ? 0.0f : m;
       float v8[8];
+      const float* srow = sc + static_cast<int64_t>(r) * (p.ntiles * TILE) + t * TILE + kk0;
+      const float4 sa = live ? *reinterpret_cast<const float4*>(srow) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const float4 sb = live ? *reinterpret_cast<const float4*>(srow + 4) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float s = live ? sc[static_cast<int64_t>(r) * (p.ntiles * TILE) + t * TILE + kk0 + i] : -INFINITY;
-        v8[i] = s == -INFINITY ? 0.0f : ex2(__fmaf_rn(s, p.scale_log2, -m_use));
-      }
+      for (int i = 0; i < 8; ++i) v8[i] = sv[i] == -INFINITY ? 0.0f : ex2(__fmaf_rn(sv[i], p.scale_log2, -m_use));
       float raw = 0.0f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) raw = __fadd_rn(raw, v8[i]);
@@ -221,18 +335,22 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
         if ((lane & 7) == 0) atomicAdd(&s_sum[r], contrib);
       }
     }
+    cp_async_wait_all_but_one();  // this tile's V landed (the next one may still be in flight)
     __syncthreads();
-    // O = alpha O + P V; l = alpha l + sum
+    // O = alpha O + P V over this warp's key half; l = alpha l + sum (key half 0 keeps l)
+    const __nv_bfloat16* vt = s_vbuf + buf * TILE * D;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int r = warp * rows_per_warp + j;
-      if (j < rows_per_warp && r < p.rows) {
+    for (int j = 0; j < 8; ++j) {
+      const int r = rg * rpw + j;
+      if (j < rpw && r < p.rows) {
         const float a = s_alpha[r];
         float o0 = acc[j][0] * a, o1 = acc[j][1] * a, o2 = acc[j][2] * a, o3 = acc[j][3] * a;
-        const __nv_bfloat16* pr = s_p + r * TILE;
-        for (int kk = 0; kk < TILE; ++kk) {
+        const __nv_bfloat16* pr = s_p + r * TILE + kh * 64;
+        const __nv_bfloat16* vr = vt + (kh * 64) * D + lane * 4;
+#pragma unroll 4
+        for (int kk = 0; kk < 64; ++kk) {
           const float pv = __bfloat162float(pr[kk]);
-          const uint2 u = *reinterpret_cast<const uint2*>(s_v + kk * D + lane * 4);
+          const uint2 u = *reinterpret_cast<const uint2*>(vr + kk * D);
           o0 = __fmaf_rn(pv, __uint_as_float(u.x << 16), o0);
           o1 = __fmaf_rn(pv, __uint_as_float(u.x & 0xFFFF0000u), o1);
           o2 = __fmaf_rn(pv, __uint_as_float(u.y << 16), o2);
@@ -245,16 +363,29 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
         l_run[j] = __fadd_rn(__fmul_rn(a, l_run[j]), s_sum[r]);
       }
     }
-    __syncthreads();
+    __syncthreads();  // P, the scalars and this V buffer are rewritten next tile
   }
-  // the split's partial state
-  const int64_t base = (static_cast<int64_t>(bh) * p.nsplits + split) * p.rows;
+  cp_async_wait_all_but_one();
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  // join the two key halves, write the split's partial state
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int r = warp * rows_per_warp + j;
-    if (j < rows_per_warp && r < p.rows) {
-      *reinterpret_cast<float4*>(p.part_o + (base + r) * D + lane * 4) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
-      if (lane == 0) {
+  for (int j = 0; j < 8; ++j) {
+    const int r = rg * rpw + j;
+    if (j < rpw && r < p.rows)
+      *reinterpret_cast<float4*>(s_o + (kh * MAX_ROWS + r) * D + lane * 4) =
+          make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+  }
+  __syncthreads();
+  const int64_t base = (static_cast<int64_t>(bh) * p.nsplits + split) * p.rows;
+  for (int i = tid; i < p.rows * D; i += THREADS) {
+    const int r = i / D, dd = i % D;
+    p.part_o[(base + r) * D + dd] = __fadd_rn(s_o[r * D + dd], s_o[(MAX_ROWS + r) * D + dd]);
+  }
+  if (kh == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = rg * rpw + j;
+      if (j < rpw && r < p.rows && lane == 0) {
         p.part_l[base + r] = l_run[j];
         p.part_m[base + r] = s_m[r];
       }
@@ -263,16 +394,16 @@ __global__ void __launch_bounds__(THREADS) decode_pv_kernel(Params p) {
 }
 
 // ---------------------------------------------------------------- pass 3
-__global__ void __launch_bounds__(THREADS) decode_combine_kernel(Params p) {
-  const int bh = blockIdx.x;
+__global__ void __launch_bounds__(D) decode_combine_kernel(Params p) {
+  const int bh = blockIdx.x, r = blockIdx.y, dd = threadIdx.x;  // one CTA per (batch, kv head, row)
   const int b = bh / p.hkv, hk = bh % p.hkv;
-  for (int i = threadIdx.x; i < p.rows * D; i += THREADS) {
-    const int r = i / D, dd = i % D;
+  {
     const int64_t base = static_cast<int64_t>(bh) * p.nsplits * p.rows;
     const float m_end = p.part_m[base + static_cast<int64_t>(p.nsplits - 1) * p.rows + r];
     const float m_use = m_end == -INFINITY ? 0.0f : m_end;
     float o = 0.0f, l = 0.0f;
-    for (int s = 0; s < p.nsplits; ++s) {
+#pragma unroll 8
+    for (int s = 0; s < p.nsplits; ++s) {  // unrolled: the splits' loads are independent
       const float ms = p.part_m[base + static_cast<int64_t>(s) * p.rows + r];
       const float f = ms == -INFINITY ? 0.0f : ex2(__fsub_rn(ms, m_use));
       o = __fmaf_rn(p.part_o[(base + static_cast<int64_t>(s) * p.rows + r) * D + dd], f, o);
@@ -300,9 +431,9 @@ static int decode_setup(dec::Params& p, const void* q, const void* k, const void
   FAQ_CHECK_ARG((hq / hkv) * sq <= dec::MAX_ROWS, "decode handles at most 32 rows per kv head ((hq / hkv) * sq)");
   FAQ_CHECK_ARG(sk < (int64_t(1) << 30), "cache too long");
   FAQ_CHECK_ARG(p_levels == 0 || p_levels == 123 || p_levels == 12 || p_levels == 13, "p_levels must be 0/123/12/13");
-  FAQ_CHECK_ARG(aligned16(k) && aligned16(v) && kb % 8 == 0 && kh % 8 == 0 && ks % 8 == 0 && vb % 8 == 0 &&
-                    vh % 8 == 0 && vs % 8 == 0,
-                "K/V must be 16-byte aligned with strides multiple of 8");
+  FAQ_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && qb % 8 == 0 && qh % 8 == 0 && qs % 8 == 0 &&
+                    kb % 8 == 0 && kh % 8 == 0 && ks % 8 == 0 && vb % 8 == 0 && vh % 8 == 0 && vs % 8 == 0,
+                "Q/K/V must be 16-byte aligned with strides multiple of 8");
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
   p.v = static_cast<const __nv_bfloat16*>(v);
@@ -333,9 +464,13 @@ static int decode_launch(dec::Params& p, float* ws, void* stream) {
   p.part_m = p.part_l + dec::round16(bh * p.nsplits * p.rows);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   FAQ_CHECK_ARG(bh <= 65535, "batch * kv heads must be <= 65535");
-  dec::decode_scores_kernel<<<dim3(p.ntiles, static_cast<unsigned>(bh)), dec::THREADS, 0, st>>>(p);
-  dec::decode_pv_kernel<<<dim3(p.nsplits, static_cast<unsigned>(bh)), dec::THREADS, 0, st>>>(p);
-  dec::decode_combine_kernel<<<static_cast<unsigned>(bh), dec::THREADS, 0, st>>>(p);
+  FAQ_CUDA(cudaFuncSetAttribute(dec::decode_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(dec::SCORES_SMEM)));
+  dec::decode_scores_kernel<<<dim3(p.ntiles, static_cast<unsigned>(bh)), dec::THREADS, dec::SCORES_SMEM, st>>>(p);
+  FAQ_CUDA(cudaFuncSetAttribute(dec::decode_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(dec::PV_SMEM)));
+  dec::decode_pv_kernel<<<dim3(p.nsplits, static_cast<unsigned>(bh)), dec::THREADS, dec::PV_SMEM, st>>>(p);
+  dec::decode_combine_kernel<<<dim3(static_cast<unsigned>(bh), static_cast<unsigned>(p.rows)), dec::D, 0, st>>>(p);
   return launch_status("hif4 decode kernels");
 }
 }  // namespace faq

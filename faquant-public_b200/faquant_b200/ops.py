@@ -376,14 +376,11 @@ def hif4_decode_attention(
     _, hkv, sk, _ = k.shape
     if v.shape != k.shape:
         raise ValueError("K and V shapes differ")
-    if q.stride(-1) != 1:
-        q = q.contiguous()
-
     def fix(t: torch.Tensor) -> torch.Tensor:
         ok = t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1]) and t.data_ptr() % 16 == 0
         return t if ok else t.contiguous()
 
-    k, v = fix(k), fix(v)
+    q, k, v = fix(q), fix(k), fix(v)
     need = int(_lib.load().faq_hif4_decode_workspace_bytes(b, hq, hkv, sq, sk, d))
     if need == 0:
         raise ValueError("unsupported decode shape")
