@@ -417,6 +417,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       l_run = __fadd_rn(__fmul_rn(alpha, l_run), half_sum);
       m_run = m_new;
+      // P as packed bf16 (exact for quantized values) over the half's first 32 S columns,
+      // stored before the O rescale so the two TMEM transfers overlap
+      {
+        float w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+          w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
+        }
+        tmem_st32f(s_addr, w);
+      }
       // s_full(j) completes after PV_t(j-1) (tcgen05 operations complete in issue order),
       // so O may be rescaled here
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
@@ -435,16 +446,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tmem_st32f(o_addr + c * 32, o);
         }
-      }
-      // P as packed bf16 (exact for quantized values) over the half's first 32 S columns
-      {
-        float w[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-          w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
-        }
-        tmem_st32f(s_addr, w);
       }
       tc_wait_st();
       tc_fence_before();
