@@ -4,9 +4,16 @@
 //                  eps), rounded to bf16, times the bf16 weight, rounded.
 //   faq_silu_mul   the SwiGLU gate of Qwen3MLP on one [rows, 2f] gate|up tensor:
 //                  bf16(bf16(silu(g)) * u), silu(g) = g / (1 + exp(-g)) in fp32.
+//   faq_layer_norm WanLayerNorm without affine (the DiT block's norm1/norm2: LayerNorm of
+//                  fp32(x), cast back): mean, biased variance, (x - mean) * rsqrt(var + eps).
+//   faq_gelu_tanh  the tanh GELU of the DiT FFN in fp32, rounded once:
+//                  0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+//   faq_row_sumsq  per-row fp32 sums of squares of column segments, row-major (one per
+//                  head for Wan's q/k RMSNorm over all heads: a head-sharded layer
+//                  all-gathers them and K4 adds them up in a fixed order).
 // torch runs each as 4-8 elementwise kernels with fp32 temporaries; here one read and
 // one write of the tensor. Rounding points are torch's; the fp32 sums are not in
-// torch's order (tolerance, not bit-exactness, for these two).
+// torch's order (tolerance, not bit-exactness, for these).
 #include "common.cuh"
 
 namespace faq {
@@ -87,6 +94,120 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
   }
 }
 
+// One CTA (256 threads) per row, the row in registers: the mean, then the sum of squared
+// deviations from it (two passes over registers, one over HBM).
+template <int CHUNKS>
+__global__ void __launch_bounds__(256) layer_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
+                                                        int64_t ldx, float eps, __nv_bfloat16* __restrict__ out,
+                                                        int64_t ldo) {
+  __shared__ float partial[2][8];
+  const int tid = threadIdx.x, chunks = k / 8;
+  const float inv_k = 1.0f / static_cast<float>(k);
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    float v[CHUNKS][8];
+    float sum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int ch = tid + c * 256;
+      if (ch < chunks) {
+        unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + ch * 8), v[c]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum = __fadd_rn(sum, v[c][i]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    if ((tid & 31) == 0) partial[0][tid >> 5] = sum;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) total = __fadd_rn(total, partial[0][i]);
+    const float mean = __fmul_rn(total, inv_k);
+    float dev = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      if (tid + c * 256 < chunks) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float e = __fsub_rn(v[c][i], mean);
+          dev = __fadd_rn(dev, __fmul_rn(e, e));
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dev = __fadd_rn(dev, __shfl_xor_sync(0xffffffffu, dev, o));
+    if ((tid & 31) == 0) partial[1][tid >> 5] = dev;
+    __syncthreads();
+    float var = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) var = __fadd_rn(var, partial[1][i]);
+    __syncthreads();  // partial[] is rewritten by the next row
+    const float r = rsqrtf(__fadd_rn(__fmul_rn(var, inv_k), eps));
+#pragma unroll
+    for (int c = 0; c < CHUNKS; ++c) {
+      const int ch = tid + c * 256;
+      if (ch < chunks) {
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(__fsub_rn(v[c][i], mean), r));
+        *reinterpret_cast<uint4*>(out + row * ldo + ch * 8) = pack8(y);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) gelu_tanh_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                        int64_t cols, int64_t ld, __nv_bfloat16* __restrict__ out,
+                                                        int64_t ldo) {
+  const int64_t per_row = cols / 8, total = rows * per_row;
+  const float beta = 0.7978845608028654f;  // sqrt(2 / pi)
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / per_row, col = (i % per_row) * 8;
+    float v[8], y[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + row * ld + col), v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float cube = __fmul_rn(__fmul_rn(v[j], v[j]), v[j]);
+      const float inner = __fmul_rn(beta, __fadd_rn(v[j], __fmul_rn(0.044715f, cube)));
+      y[j] = bf16_round(__fmul_rn(__fmul_rn(0.5f, v[j]), __fadd_rn(1.0f, tanhf(inner))));
+    }
+    *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
+  }
+}
+
+// GROUP lanes (16 or 32) per (row, segment) item, consecutive items on consecutive
+// groups; the lanes stride the segment's 8-value chunks, then a butterfly. The order of
+// the additions depends only on seg_cols.
+template <int GROUP>
+__global__ void __launch_bounds__(256) row_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                        int64_t segments, int64_t seg_cols, int64_t ld,
+                                                        float* __restrict__ out) {
+  const int lane = threadIdx.x & 31, sub = lane % GROUP;
+  const int64_t items = rows * segments, chunks = seg_cols / 8;
+  const int64_t groups = static_cast<int64_t>(gridDim.x) * (blockDim.x / GROUP);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * (blockDim.x / GROUP) + threadIdx.x / GROUP;
+  // every lane of a warp runs the same number of iterations (the butterfly is warp-wide)
+  const int64_t warp_first = first - lane / GROUP;
+  for (int64_t base = warp_first; base < items; base += groups) {
+    const int64_t it = base + lane / GROUP;
+    float ss = 0.0f;
+    if (it < items) {
+      const int64_t row = it / segments, seg = it % segments;
+      const __nv_bfloat16* src = x + row * ld + seg * seg_cols;
+      for (int64_t ch = sub; ch < chunks; ch += GROUP) {
+        float v[8];
+        unpack8(*reinterpret_cast<const uint4*>(src + ch * 8), v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < GROUP; o <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    if (sub == 0 && it < items) out[it] = ss;
+  }
+}
+
 }  // namespace faq
 
 extern "C" int faq_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
@@ -129,4 +250,68 @@ extern "C" int faq_silu_mul(const void* gate_up, int64_t rows, int64_t f, int64_
                                                                         rows, f, ld, static_cast<__nv_bfloat16*>(out),
                                                                         ldo);
   return launch_status("silu_mul_kernel");
+}
+
+extern "C" int faq_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps, void* out, int64_t ldo,
+                              void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(rows >= 0 && k > 0 && k % 8 == 0 && k <= 32768, "k must be a positive multiple of 8, at most 32768");
+  if (rows == 0) return FAQ_OK;  // an empty tensor may have no storage
+  FAQ_CHECK_ARG(x && out, "null pointer");
+  FAQ_CHECK_ARG(ldx >= k && ldo >= k && ldx % 8 == 0 && ldo % 8 == 0, "row strides must be >= k and multiples of 8");
+  FAQ_CHECK_ARG(aligned16(x) && aligned16(out), "tensors must be 16-byte aligned");
+  FAQ_CHECK_ARG(eps >= 0.0f, "eps must be non-negative");
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  auto* op = static_cast<__nv_bfloat16*>(out);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int chunks = static_cast<int>(k / 8), per_thread = (chunks + 255) / 256;
+  const int kk = static_cast<int>(k);
+  if (per_thread <= 1)
+    layer_norm_kernel<1><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  else if (per_thread <= 3)
+    layer_norm_kernel<3><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  else if (per_thread <= 8)
+    layer_norm_kernel<8><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  else
+    layer_norm_kernel<16><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  return launch_status("layer_norm_kernel");
+}
+
+extern "C" int faq_gelu_tanh(const void* x, int64_t rows, int64_t cols, int64_t ld, void* out, int64_t ldo,
+                             void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(rows >= 0 && cols > 0 && cols % 8 == 0, "cols must be a positive multiple of 8");
+  if (rows == 0) return FAQ_OK;  // an empty tensor may have no storage
+  FAQ_CHECK_ARG(x && out, "null pointer");
+  FAQ_CHECK_ARG(ld >= cols && ldo >= cols && ld % 8 == 0 && ldo % 8 == 0, "bad row strides");
+  FAQ_CHECK_ARG(aligned16(x) && aligned16(out), "tensors must be 16-byte aligned");
+  const int64_t total = rows * (cols / 8);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(num_sms()) * 16));
+  gelu_tanh_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), rows, cols, ld, static_cast<__nv_bfloat16*>(out), ldo);
+  return launch_status("gelu_tanh_kernel");
+}
+
+extern "C" int faq_row_sumsq(const void* x, int64_t rows, int64_t segments, int64_t seg_cols, int64_t ld, float* out,
+                             void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(rows >= 0 && segments > 0 && seg_cols > 0 && seg_cols % 8 == 0,
+                "segments must be positive and seg_cols a positive multiple of 8");
+  if (rows == 0) return FAQ_OK;  // an empty tensor may have no storage
+  FAQ_CHECK_ARG(x && out, "null pointer");
+  FAQ_CHECK_ARG(ld >= segments * seg_cols && ld % 8 == 0, "ld must be >= segments * seg_cols and a multiple of 8");
+  FAQ_CHECK_ARG(aligned16(x), "x must be 16-byte aligned");
+  const int64_t items = rows * segments;
+  const int group = seg_cols <= 128 ? 16 : 32;
+  const int64_t per_block = 256 / group;
+  const unsigned grid = static_cast<unsigned>(
+      std::min<int64_t>((items + per_block - 1) / per_block, static_cast<int64_t>(num_sms()) * 16));
+  const auto* xp = static_cast<const __nv_bfloat16*>(x);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (group == 16)
+    row_sumsq_kernel<16><<<grid, 256, 0, st>>>(xp, rows, segments, seg_cols, ld, out);
+  else
+    row_sumsq_kernel<32><<<grid, 256, 0, st>>>(xp, rows, segments, seg_cols, ld, out);
+  return launch_status("row_sumsq_kernel");
 }

@@ -8,6 +8,10 @@
 // head_dim (simulated_flash_attention.py:588-619). Wan does the same
 // (wan22_attention.py:186-192, 221, 257-259).
 //
+// faq_wan_qk_prep does the same for Wan's self-attention (wan22_attention.py:250-258
+// with Wan's WanRMSNorm and rope_apply): the RMSNorm over all heads of a token from
+// per-head sums of squares, the 3-D RoPE in fp64 rounded to fp32, then the steps above.
+//
 // The fused entry point faq_qk_norm_rope_prep puts Qwen3's own steps in front
 // (qwen3.py:87-100 with HF Qwen3Attention): the per-head RMSNorm over head_dim
 // (Qwen3RMSNorm: fp32 mean of squares, rsqrt, cast to bf16, times the bf16 weight, cast)
@@ -43,6 +47,18 @@ struct QkPrepParams {
   const __nv_bfloat16* cos;     // [seq, rope_ld] or null: RoPE after the norm
   const __nv_bfloat16* sin;
   int64_t rope_ld;
+  // Wan's self-attention glue: WanRMSNorm over a token's whole row of heads_total * d
+  // channels, bf16(x * rsqrt(mean + eps)) times the weight w[head * d + c] in fp32. The
+  // row's sum of squares is the sum, in a fixed order, of per-head sums: head g of token
+  // t at head_ss[(g / heads_per_block) * ss_block_stride + t * ss_token_stride + g %
+  // heads_per_block] (blocks = ranks of a head-sharded layer), so the sum is the same
+  // for every sharding. Then rope_apply's 3-D RoPE on channel pairs (2i, 2i+1) as
+  // complex numbers: fp64 products with fp64 tables [seq, d/2], rounded to fp32.
+  const float* head_ss;         // or null
+  int64_t heads_total, heads_per_block, ss_token_stride, ss_block_stride;
+  const float* tok_w;           // [heads, d]
+  const double* pair_cos;       // [seq, d/2] or null
+  const double* pair_sin;
 };
 
 template <typename T, int D>
@@ -99,6 +115,31 @@ __global__ void __launch_bounds__(256) qk_prep_kernel(QkPrepParams p) {
       for (int i = 0; i < 8; ++i) {
         const float w = __uint_as_float(i & 1 ? ww[i >> 1] & 0xFFFF0000u : ww[i >> 1] << 16);
         v[i] = bf16_round(__fmul_rn(w, bf16_round(__fmul_rn(v[i], r))));
+      }
+    }
+    if (p.head_ss != nullptr) {
+      // lane `sub` adds heads sub, sub + LANES, ..., then a butterfly over the row's lanes
+      const int64_t t = b * p.seq + s;
+      float ss = 0.0f;
+      for (int64_t g = sub; g < p.heads_total; g += LANES)
+        ss = __fadd_rn(ss, p.head_ss[(g / p.heads_per_block) * p.ss_block_stride + t * p.ss_token_stride +
+                                     g % p.heads_per_block]);
+#pragma unroll
+      for (int ls = 1; ls < LANES; ls <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, ls));
+      const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.heads_total * D)), p.eps));
+      const float* w = p.tok_w + h * D + sub * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(bf16_round(__fmul_rn(v[i], r)), w[i]);
+    }
+    if (p.pair_cos != nullptr) {
+      // four complex pairs per lane; the fp32 result stays unrounded into the Hadamard
+      const double* cr = p.pair_cos + s * (D / 2) + sub * 4;
+      const double* sr = p.pair_sin + s * (D / 2) + sub * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const double re = v[2 * i], im = v[2 * i + 1], c = cr[i], sn = sr[i];
+        v[2 * i] = __double2float_rn(__dsub_rn(__dmul_rn(re, c), __dmul_rn(im, sn)));
+        v[2 * i + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, sn), __dmul_rn(im, c)));
       }
     }
     if (p.cos != nullptr) {
@@ -263,6 +304,12 @@ static int qk_prep_checked(const void* x, int x_dtype, int64_t batch, int64_t he
   p.cos = static_cast<const __nv_bfloat16*>(cos);
   p.sin = static_cast<const __nv_bfloat16*>(sin);
   p.rope_ld = rope_ld;
+  p.head_ss = nullptr;
+  p.heads_total = p.heads_per_block = 1;
+  p.ss_token_stride = p.ss_block_stride = 0;
+  p.tok_w = nullptr;
+  p.pair_cos = nullptr;
+  p.pair_sin = nullptr;
   return qk_prep_launch(p, x_dtype, d, stream);
 }
 }  // namespace faq
@@ -285,4 +332,57 @@ extern "C" int faq_qk_norm_rope_prep(const void* x, int x_dtype, int64_t batch, 
   return faq::qk_prep_checked(x, x_dtype, batch, heads, seq, d, sb, sh, ss, offset, smooth, smooth_head_stride,
                               smooth_mode, rotate, levels, out, ob, oh, os, codes, meta, norm_weight, eps, cos, sin,
                               rope_ld, stream);
+}
+
+extern "C" int faq_wan_qk_prep(const void* x, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb,
+                               int64_t sh, int64_t ss, const float* head_ss, int64_t heads_total,
+                               int64_t heads_per_block, int64_t ss_token_stride, int64_t ss_block_stride,
+                               const float* norm_weight, float eps, const double* pair_cos, const double* pair_sin, const float* smooth,
+                               int64_t smooth_head_stride, int smooth_mode, int rotate, int levels, void* out,
+                               int64_t ob, int64_t oh, int64_t os, void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(batch >= 0 && heads > 0 && seq >= 0, "bad shape");
+  if (d != 64 && d != 128) return fail(FAQ_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  FAQ_CHECK_ARG(levels == 0 || levels == 123 || levels == 12 || levels == 13, "levels must be 0, 123, 12 or 13");
+  FAQ_CHECK_ARG((pair_cos == nullptr) == (pair_sin == nullptr), "pair_cos and pair_sin come together");
+  FAQ_CHECK_ARG(heads_total > 0 && heads_per_block > 0 && eps >= 0.0f,
+                "heads_total and heads_per_block must be positive and eps non-negative");
+  FAQ_CHECK_ARG(smooth_mode >= 0 && smooth_mode <= 2, "smooth_mode must be 0, 1 or 2");
+  FAQ_CHECK_ARG(smooth_mode == 0 || smooth != nullptr, "smooth_mode needs smooth");
+  if (batch == 0 || seq == 0) return FAQ_OK;
+  FAQ_CHECK_ARG(x && out && head_ss && norm_weight, "null pointer");
+  QkPrepParams p;
+  p.x = x;
+  p.batch = batch;
+  p.heads = heads;
+  p.seq = seq;
+  p.sb = sb;
+  p.sh = sh;
+  p.ss = ss;
+  p.offset = nullptr;
+  p.smooth = smooth;
+  p.smooth_head_stride = smooth_head_stride;
+  p.smooth_mode = smooth_mode;
+  p.rotate = rotate;
+  p.levels = levels;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ob = ob;
+  p.oh = oh;
+  p.os = os;
+  p.codes = nullptr;
+  p.meta = nullptr;
+  p.norm_w = nullptr;
+  p.eps = eps;
+  p.cos = nullptr;
+  p.sin = nullptr;
+  p.rope_ld = 0;
+  p.head_ss = head_ss;
+  p.heads_total = heads_total;
+  p.heads_per_block = heads_per_block;
+  p.ss_token_stride = ss_token_stride;
+  p.ss_block_stride = ss_block_stride;
+  p.tok_w = norm_weight;
+  p.pair_cos = pair_cos;
+  p.pair_sin = pair_sin;
+  return qk_prep_launch(p, FAQ_BF16, d, stream);
 }

@@ -41,6 +41,12 @@ SIGNATURES: dict[str, list] = {
                               _int, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
     "faq_rms_norm": [_c_void_p, _i64, _i64, _i64, _c_void_p, ctypes.c_float, _c_void_p, _i64, _c_void_p],
     "faq_silu_mul": [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
+    "faq_layer_norm": [_c_void_p, _i64, _i64, _i64, ctypes.c_float, _c_void_p, _i64, _c_void_p],
+    "faq_gelu_tanh": [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
+    "faq_row_sumsq": [_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p],
+    "faq_wan_qk_prep": [_c_void_p, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p, _i64, _i64, _i64, _i64,
+                        _c_void_p, ctypes.c_float, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _int, _c_void_p, _i64,
+                        _i64, _i64, _c_void_p],
     "faq_hif4_attention": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _int,
                            _int, _c_void_p, _i64, _i64, _i64, _c_void_p],

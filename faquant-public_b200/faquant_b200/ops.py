@@ -283,6 +283,106 @@ def qk_norm_rope_prep(
     return out
 
 
+def wan_qk_prep(
+    x: torch.Tensor,
+    head_sumsq: torch.Tensor,
+    norm_weight: torch.Tensor,
+    *,
+    head_offset: int = 0,
+    eps: float = 1e-6,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    smooth_scale: torch.Tensor | None = None,
+    smooth_mode: str | None = None,
+    levels: str | int | None = "123",
+    rotate: bool = True,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Wan2.2 self-attention operand in one pass: WanRMSNorm over each token's whole row
+    of all heads, the 3-D RoPE (fp64 ``cos``/``sin`` ``[S, D/2]``), optional Smooth-QK,
+    Hadamard over D, bf16, HiF4. ``x [B, H, S, D]`` bf16, any strides with D contiguous.
+
+    ``head_sumsq [ranks, B*S, C]`` fp32 holds per-head sums of squares (``row_sumsq``
+    with one segment per head; ``ranks`` > 1 when gathered from a head-sharded layer):
+    this tensor's heads of rank r are columns ``head_offset .. head_offset + H`` of
+    block r, so the norm runs over ``ranks * H`` heads. ``norm_weight [H, D]`` or
+    ``[H*D]`` is this shard's weight."""
+    device = _require_cuda(x, head_sumsq, norm_weight, cos, sin, smooth_scale)
+    if x.dim() != 4 or x.dtype != torch.bfloat16:
+        raise ValueError("wan_qk_prep expects bf16 [batch, heads, seq, head_dim]")
+    b, h, s, d = x.shape
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty((b, h, s, d), dtype=torch.bfloat16, device=device)
+    if head_sumsq.dtype != torch.float32 or head_sumsq.dim() != 3 or not head_sumsq.is_contiguous():
+        raise TypeError("head_sumsq must be a contiguous fp32 [ranks, batch * seq, columns] tensor")
+    ranks, tokens, cols = head_sumsq.shape
+    if tokens != b * s or head_offset < 0 or head_offset + h > cols:
+        raise ValueError("head_sumsq does not cover these heads and tokens")
+    norm_weight = norm_weight.to(device=device, dtype=torch.float32).reshape(h, d).contiguous()
+    if cos is not None:
+        cos = cos.to(device=device, dtype=torch.float64).contiguous()
+        sin = sin.to(device=device, dtype=torch.float64).contiguous()
+        if cos.shape != (s, d // 2) or sin.shape != (s, d // 2):
+            raise ValueError("cos/sin must be [seq, head_dim / 2]")
+    mode = {None: 0, "mul": 1, "div": 2}[smooth_mode]
+    head_stride = 0
+    if smooth_scale is not None:
+        smooth_scale = smooth_scale.to(device=device, dtype=torch.float32).contiguous()
+        head_stride = d if smooth_scale.dim() == 2 else 0
+    lv = 0 if levels is None else levels_code(levels)
+    _lib.call("faq_wan_qk_prep", x.data_ptr(), b, h, s, d, x.stride(0), x.stride(1), x.stride(2),
+              head_sumsq.data_ptr() + 4 * head_offset, ranks * h, h, cols, tokens * cols, norm_weight.data_ptr(),
+              float(eps), _ptr(cos), _ptr(sin),
+              _ptr(smooth_scale), head_stride, mode, int(rotate), lv, out.data_ptr(), out.stride(0), out.stride(1),
+              out.stride(2), _stream(device))
+    return out
+
+
+def row_sumsq(x: torch.Tensor, segments: int = 1, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 ``[rows, segments]`` sums of squares of the ``segments`` equal column blocks
+    of bf16 ``x [rows, cols]`` (a column slice of a wider tensor is fine)."""
+    device = _require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise TypeError("row_sumsq takes a bf16 [rows, cols] tensor with contiguous rows")
+    rows, cols = x.shape
+    if cols % segments:
+        raise ValueError("cols must divide into the segments")
+    if out is None:
+        out = torch.empty((rows, segments), dtype=torch.float32, device=device)
+    _lib.call("faq_row_sumsq", x.data_ptr(), rows, segments, cols // segments, x.stride(0) if rows > 1 else cols,
+              out.data_ptr(), _stream(device))
+    return out
+
+
+def layer_norm(x: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """LayerNorm without affine of bf16 ``x [..., k]`` (fp32 statistics), one pass."""
+    device = _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("layer_norm takes bfloat16")
+    rows, ldx = _rows_view(x)
+    k = x.shape[-1]
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=device)
+    _lib.call("faq_layer_norm", rows.data_ptr(), rows.shape[0], k, ldx, float(eps), out.data_ptr(), k,
+              _stream(device))
+    return out
+
+
+def gelu_tanh(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """GELU (tanh approximation) of a bf16 ``[rows, cols]`` tensor, one pass."""
+    device = _require_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise TypeError("gelu_tanh takes a bf16 [rows, cols] tensor with contiguous rows")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.bfloat16, device=device)
+    _lib.call("faq_gelu_tanh", x.data_ptr(), rows, cols, x.stride(0) if rows > 1 else cols, out.data_ptr(),
+              out.stride(0) if rows > 1 else cols, _stream(device))
+    return out
+
+
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
     """Qwen3RMSNorm of bf16 ``x [..., k]`` in one pass."""
     device = _require_cuda(x, weight)

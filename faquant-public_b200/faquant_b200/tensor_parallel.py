@@ -55,6 +55,16 @@ class TPGroup:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
+    def all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        """``[world, *t.shape]``: every rank's ``t`` in rank order."""
+        if self.world == 1:
+            return t.unsqueeze(0)
+        import torch.distributed as dist
+
+        out = torch.empty((self.world, *t.shape), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
+
     def comm_stream(self, device: torch.device) -> torch.cuda.Stream:
         """The side stream the chunked all-reduces run on (one per rank and device)."""
         key = ("stream", device.index)
@@ -377,10 +387,11 @@ class WanBlockConfig:
 
 
 def rope3d_tables(grid: tuple[int, int, int], head_dim: int, theta: float, device: torch.device):
-    """cos/sin ``[F*H*W, head_dim/2]`` of the 3-axis rotary embedding of Wan's DiT: the
-    ``head_dim/2`` complex pairs are split ``[c - 2(c//3), c//3, c//3]`` over (frame,
-    height, width), each band with its own ``theta^(-2i/d_band)`` frequencies, and a token
-    at grid position (f, h, w) rotates band pairs by (f, h, w) times those frequencies."""
+    """fp64 cos/sin ``[F*H*W, head_dim/2]`` of the 3-axis rotary embedding of Wan's DiT
+    (Wan's rope_params/rope_apply, which multiply in complex128): the ``head_dim/2``
+    complex pairs are split ``[c - 2(c//3), c//3, c//3]`` over (frame, height, width),
+    each band with its own ``theta^(-2i/d_band)`` frequencies, and a token at grid
+    position (f, h, w) rotates band pairs by (f, h, w) times those frequencies."""
     c = head_dim // 2
     bands = [c - 2 * (c // 3), c // 3, c // 3]
     angles = []
@@ -393,17 +404,26 @@ def rope3d_tables(grid: tuple[int, int, int], head_dim: int, theta: float, devic
         a = torch.outer(pos, inv).reshape(shape).expand(grid[0], grid[1], grid[2], pairs)
         angles.append(a)
     ang = torch.cat(angles, dim=-1).reshape(-1, c)
-    return ang.cos().float(), ang.sin().float()
+    return ang.cos(), ang.sin()
 
 
 def apply_rope3d(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """``x [L, H, D]`` with channel pairs (2i, 2i+1) as complex numbers, rotated in fp64-built
-    fp32 tables; returns ``x.dtype``."""
-    xf = x.float().reshape(*x.shape[:-1], -1, 2)
+    """torch statement of Wan's rope_apply (the check for ``ops.wan_qk_prep``): ``x [L, H,
+    D]`` with channel pairs (2i, 2i+1) as complex numbers, multiplied in fp64 by the fp64
+    tables, returned as fp32."""
+    xf = x.double().reshape(*x.shape[:-1], -1, 2)
     re, im = xf[..., 0], xf[..., 1]
-    c, s = cos[:, None, :], sin[:, None, :]
+    c, s = cos.double()[:, None, :], sin.double()[:, None, :]
     out = torch.stack([re * c - im * s, re * s + im * c], dim=-1)
-    return out.reshape(x.shape).to(x.dtype)
+    return out.reshape(x.shape).float()
+
+
+def wan_qk_norm(t: torch.Tensor, weight: torch.Tensor, heads_total_dim: int, eps: float) -> torch.Tensor:
+    """torch statement of WanRMSNorm on the whole q (or k) row ``t [L, dim]`` (the check
+    for ``ops.wan_qk_prep``): ``bf16(x * rsqrt(mean(x^2) + eps)) * w``, fp32 out."""
+    tf = t.float()
+    r = torch.rsqrt(tf.pow(2).sum(-1, keepdim=True) / heads_total_dim + eps)
+    return (tf * r).to(torch.bfloat16).float() * weight.float()
 
 
 class WanBlockTP(nn.Module):
@@ -414,8 +434,11 @@ class WanBlockTP(nn.Module):
     Column-parallel q/k/v and ffn.0 read the LayerNorm outputs with the ``rbhn_r64``
     reader rotation (one HiSQ rotation per norm, 64-channel blocks; shared, so one K1 per
     norm); row-parallel o and ffn.2 use shard-local ``"signs"`` rotations. Wan normalizes
-    q and k over all heads (RMSNorm over ``dim``), so the head-sharded form all-reduces the
-    per-token sum of squares (``[L]`` fp32) -- attention itself needs no collective.
+    q and k over all heads (RMSNorm over ``dim``), so the head-sharded form all-gathers
+    per-head sums of squares (``[L, 2 heads/world]`` fp32) and K4 adds all heads' sums in
+    one fixed order -- the norm, and so the attention operands, are the same bits at
+    every TP size; attention itself needs no collective. The glue is one kernel each:
+    LayerNorm, the per-head sums, K4 with the norm and the 3-D RoPE in front, GELU.
     """
 
     def __init__(self, cfg: WanBlockConfig, tp: TPGroup, device: torch.device, index: int = 0) -> None:
@@ -453,16 +476,9 @@ class WanBlockTP(nn.Module):
                                  bias=b("ffn.2", cfg.dim) if tp.rank == 0 else None, quantize=True,
                                  levels=cfg.levels, reduce=tp,
                                  rotation=row_rotation(f"{name}.ffn.2", cfg.ffn, tp, seed=cfg.hisq_seed))
-        self.norm_q = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows]
-        self.norm_k = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows]
+        self.norm_q = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows].contiguous()
+        self.norm_k = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows].contiguous()
         self.cos, self.sin = rope3d_tables(cfg.grid, d, cfg.rope_theta, device)
-
-    def _qk_norm(self, t: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-        """Wan's RMSNorm over all ``dim`` channels of q or k, from this rank's head slice."""
-        tf = t.float()
-        ss = tf.pow(2).sum(-1, keepdim=True)
-        self.tp.all_reduce_(ss)
-        return (tf * torch.rsqrt(ss / self.cfg.dim + self.cfg.eps) * weight).to(t.dtype)
 
     @torch.no_grad()
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -470,19 +486,21 @@ class WanBlockTP(nn.Module):
         cfg, d, hl = self.cfg, self.cfg.head_dim, self.h_local
         seq = x.shape[0]
         tr = (lambda stage, t: (self.trace(stage, 0, t), t)[1]) if self.trace is not None else (lambda stage, t: t)
-        h = tr("norm1", torch.nn.functional.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps).to(x.dtype))
+        h = tr("norm1", ops.layer_norm(x, cfg.eps))
         qkv = tr("qkv", self.qkv(h))
         n = hl * d
-        q = tr("q_rope", apply_rope3d(self._qk_norm(qkv[:, :n], self.norm_q).view(seq, hl, d), self.cos, self.sin))
-        k = tr("k_rope", apply_rope3d(self._qk_norm(qkv[:, n:2 * n], self.norm_k).view(seq, hl, d), self.cos, self.sin))
-        v = qkv[:, 2 * n:].view(seq, hl, d)
-        qd = ops.qk_prep(q.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=True)[0]
-        kd = ops.qk_prep(k.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=True)[0]
-        vd = ops.qk_prep(v.unsqueeze(0).transpose(1, 2), levels=cfg.levels, rotate=False)[0]
+        # per-head sums of squares of q and k: [world, L, 2 hl] after the gather
+        head_ss = self.tp.all_gather(ops.row_sumsq(qkv[:, :2 * n], segments=2 * hl))
+        heads = lambda lo: qkv[:, lo:lo + n].view(1, seq, hl, d).transpose(1, 2)  # noqa: E731
+        qd = tr("qd", ops.wan_qk_prep(heads(0), head_ss, self.norm_q, head_offset=0, eps=cfg.eps, cos=self.cos,
+                                      sin=self.sin, levels=cfg.levels))
+        kd = tr("kd", ops.wan_qk_prep(heads(n), head_ss, self.norm_k, head_offset=hl, eps=cfg.eps, cos=self.cos,
+                                      sin=self.sin, levels=cfg.levels))
+        vd = tr("vd", ops.qk_prep(heads(2 * n), levels=cfg.levels, rotate=False)[0])
         att = tr("attention", ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=False, p_levels=cfg.levels,
                                                  quantized_normalizer=True))  # [1, L, hl, d]
-        x = x + tr("o", self.o(att.view(seq, n)))
-        h = tr("norm2", torch.nn.functional.layer_norm(x.float(), (cfg.dim,), eps=cfg.eps).to(x.dtype))
+        x = tr("x_mid", x + tr("o", self.o(att.view(seq, n))))
+        h = tr("norm2", ops.layer_norm(x, cfg.eps))
         f0 = tr("ffn0", self.ffn0(h))
-        a = tr("act", torch.nn.functional.gelu(f0.float(), approximate="tanh").to(x.dtype))
+        a = tr("act", ops.gelu_tanh(f0))
         return x + tr("ffn2", self.ffn2(a))

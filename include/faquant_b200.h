@@ -155,17 +155,48 @@ int faq_qk_norm_rope_prep(const void* x, int x_dtype, int64_t batch, int64_t hea
                           uint32_t* meta, void* stream);
 
 /*
+ * K4 for Wan2.2's self-attention q/k (wan22_attention.py:250-258: norm_q/norm_k, Wan's
+ * rope_apply, the optional faquant_qk_smooth_scale, then make_flash_attention's
+ * rotate_heads and input_qdq): x bf16 [batch, heads, seq, d] with element strides.
+ * head_ss holds the per-head sums of squares of all heads_total heads of the layer
+ * (faq_row_sumsq with seg_cols = d; on a head shard all-gathered over the ranks): head
+ * g of token t at head_ss[(g / heads_per_block) * ss_block_stride + t * ss_token_stride
+ * + g % heads_per_block]. They are added in a fixed order, so the norm does not depend
+ * on the sharding. norm_weight fp32 [heads, d] this shard's weight; pair_cos/pair_sin
+ * fp64 [seq, d/2] (or null) the 3-axis RoPE table. v = bf16(x * rsqrt(sum / (heads_total
+ * d) + eps)) * w, the RoPE in fp64 rounded to fp32, smooth (as faq_qk_prep), Hadamard,
+ * one bf16 rounding, HiF4.
+ */
+int faq_wan_qk_prep(const void* x, int64_t batch, int64_t heads, int64_t seq, int d, int64_t sb, int64_t sh,
+                    int64_t ss, const float* head_ss, int64_t heads_total, int64_t heads_per_block,
+                    int64_t ss_token_stride, int64_t ss_block_stride, const float* norm_weight, float eps,
+                    const double* pair_cos, const double* pair_sin, const float* smooth,
+                    int64_t smooth_head_stride, int smooth_mode, int rotate, int levels, void* out, int64_t ob,
+                    int64_t oh, int64_t os, void* stream);
+
+/*
  * Decoder glue, one HBM pass each (bf16, 16-byte aligned rows, strides in elements):
  * faq_rms_norm: out = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) per row of k, as HF
  *   Qwen3RMSNorm (the input_layernorm/post_attention_layernorm the reference's Qwen3
  *   decoder layers apply before the projections K1 quantizes);
  * faq_silu_mul: out[:, j] = bf16(bf16(silu(gu[:, j])) * gu[:, f + j]) for a gate|up
- *   tensor of 2f columns, as Qwen3MLP's act_fn(gate) * up.
+ *   tensor of 2f columns, as Qwen3MLP's act_fn(gate) * up;
+ * faq_layer_norm: out = bf16((x - mean) * rsqrt(var + eps)) per row of k (biased
+ *   variance, no affine), as the Wan DiT block's WanLayerNorm norm1/norm2 in fp32;
+ * faq_gelu_tanh: out = bf16(0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))), the
+ *   Wan FFN's GELU(approximate="tanh");
+ * faq_row_sumsq: out[r * segments + s] = sum of x[r, s * seg_cols + c]^2 over c, fp32,
+ *   for `segments` adjacent column segments (the q and k heads of a fused qkv projection).
  */
 int faq_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* weight, float eps,
                  void* out, int64_t ldo, void* stream);
 int faq_silu_mul(const void* gate_up, int64_t rows, int64_t f, int64_t ld, void* out, int64_t ldo,
                  void* stream);
+int faq_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps, void* out, int64_t ldo,
+                   void* stream);
+int faq_gelu_tanh(const void* x, int64_t rows, int64_t cols, int64_t ld, void* out, int64_t ldo, void* stream);
+int faq_row_sumsq(const void* x, int64_t rows, int64_t segments, int64_t seg_cols, int64_t ld, float* out,
+                  void* stream);
 
 /*
  * K5 -- HiF4 QK/PV flash attention on pre-quantized bf16 operands (output of K4).

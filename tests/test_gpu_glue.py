@@ -1,8 +1,10 @@
-"""GPU tests of the fused decoder glue: faq_rms_norm, faq_silu_mul and the Qwen3 K4
-variant faq_qk_norm_rope_prep, against torch's own ops on the CPU (the reference's
-glue) and the oracle. Where the ops are pure bf16-rounded elementwise math (RoPE, the
-HiF4 steps) the results are bit-exact; the row reductions (RMSNorm) and exp (SiLU) sum or
-round differently from torch's CPU kernels, so those are held to one bf16 ulp."""
+"""GPU tests of the fused decoder glue: faq_rms_norm, faq_silu_mul, the Qwen3 K4 variant
+faq_qk_norm_rope_prep, and Wan's faq_layer_norm, faq_gelu_tanh, faq_row_sumsq and K4
+variant faq_wan_qk_prep, against torch's own ops on the CPU (the reference's glue) and
+the oracle. Where the ops are pure bf16-rounded elementwise math (RoPE, the HiF4 steps)
+the results are bit-exact; the row reductions (RMSNorm, LayerNorm) and exp/tanh (SiLU,
+GELU) sum or round differently from torch's CPU kernels, so those are held to one bf16
+ulp."""
 
 from __future__ import annotations
 
@@ -68,3 +70,108 @@ def test_qk_norm_rope_prep_stages() -> None:
     got = full.float().cpu().numpy()
     assert np.mean(got == expect) >= 0.995
     assert np.linalg.norm(got - expect) <= 2e-2 * np.linalg.norm(expect)
+
+
+def test_layer_norm_matches_wan_layernorm() -> None:
+    from faquant_b200 import ops
+
+    g = torch.Generator().manual_seed(4)
+    for k in (64, 512, 2048, 5120, 13824):
+        x = (torch.randn(29, k, generator=g) * 3 + 0.7).to(torch.bfloat16)
+        ref = torch.nn.functional.layer_norm(x.float(), (k,), eps=1e-6).to(torch.bfloat16)
+        _within_ulp(ops.layer_norm(x.to(DEV), 1e-6), ref)
+    assert ops.layer_norm(torch.zeros(0, 64, dtype=torch.bfloat16, device=DEV), 1e-6).shape == (0, 64)
+
+
+def test_gelu_tanh_matches_torch() -> None:
+    from faquant_b200 import ops
+
+    x = (torch.randn(41, 1376, generator=torch.Generator().manual_seed(5)) * 4).to(torch.bfloat16)
+    ref = torch.nn.functional.gelu(x.float(), approximate="tanh").to(torch.bfloat16).float()
+    got = ops.gelu_tanh(x.to(DEV)).float().cpu()
+    # one bf16 ulp; the far negative tail, where 1 + tanh cancels, to an absolute 1e-5
+    assert torch.all((got - ref).abs() <= 2.0**-7 * ref.abs() + 1e-5)
+
+
+def test_row_sumsq_segments() -> None:
+    from faquant_b200 import ops
+
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(300, 3 * 640, generator=g).to(torch.bfloat16)
+    for cols, segments in ((2 * 640, 10), (2 * 640, 2), (640, 1)):  # 128-wide heads, 640-wide halves, whole
+        got = ops.row_sumsq(x.to(DEV)[:, :cols], segments=segments).cpu().double()
+        ref = x[:, :cols].double().pow(2).reshape(300, segments, -1).sum(-1)
+        assert got.shape == (300, segments)
+        assert torch.allclose(got, ref, rtol=1e-5, atol=0)
+
+
+def _wan_operands(seq, heads, d=128, seed=7):
+    g = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(seq, 3 * heads * d, generator=g) * 2).to(torch.bfloat16)
+    w = 1 + 0.2 * torch.randn(heads * d, generator=g)
+    return qkv, w
+
+
+def test_wan_qk_prep_matches_the_reference_glue() -> None:
+    """WanRMSNorm over all heads + rope_apply (fp64) + Hadamard + HiF4 against torch's
+    statement of Wan's glue and the oracle; with Smooth-QK (per head, multiply)."""
+    from faquant_b200 import ops
+    from faquant_b200.tensor_parallel import apply_rope3d, rope3d_tables, wan_qk_norm
+
+    grid, heads, d = (2, 4, 6), 5, 128
+    seq = grid[0] * grid[1] * grid[2]
+    qkv, w = _wan_operands(seq, heads)
+    n = heads * d
+    cos, sin = rope3d_tables(grid, d, 10000.0, torch.device("cpu"))
+    smooth = 0.5 + torch.rand(heads, d, generator=torch.Generator().manual_seed(8))
+    dq = qkv.to(DEV)
+    head_ss = ops.row_sumsq(dq[:, :2 * n], segments=2 * heads)[None]
+    for lo, off, sm in ((0, 0, None), (n, heads, None), (0, 0, smooth)):
+        x = dq[:, lo:lo + n].view(1, seq, heads, d).transpose(1, 2)
+        got = ops.wan_qk_prep(x, head_ss, w.to(DEV), head_offset=off, eps=1e-6, cos=cos.to(DEV), sin=sin.to(DEV),
+                              smooth_scale=None if sm is None else sm.to(DEV), smooth_mode=None if sm is None else "mul",
+                              levels="123").float().cpu().numpy()
+        r = apply_rope3d(wan_qk_norm(qkv[:, lo:lo + n], w, n, 1e-6).view(seq, heads, d), cos, sin)
+        r = r.transpose(0, 1)[None].numpy()
+        expect = oh.fake_quantize(oatt.qk_pretransform(r, r, smooth_scale=None if sm is None else sm.numpy())[0], "123")
+        assert np.mean(got == expect) >= 0.995
+        assert np.linalg.norm(got - expect) <= 2e-2 * np.linalg.norm(expect)
+
+
+def test_wan_qk_prep_is_the_same_for_every_head_sharding() -> None:
+    """The per-head sums laid out as a TP-4 all-gather ([4, L, 2 heads/4]) give each
+    rank's heads the same bits as the unsharded call."""
+    from faquant_b200 import ops
+    from faquant_b200.tensor_parallel import rope3d_tables
+
+    grid, heads, d, world = (3, 4, 5), 8, 128, 4
+    seq, hl = grid[0] * grid[1] * grid[2], heads // world
+    qkv, w = _wan_operands(seq, heads, seed=9)
+    n = heads * d
+    cos, sin = rope3d_tables(grid, d, 10000.0, DEV)
+    dq, dw = qkv.to(DEV), w.to(DEV)
+    full_ss = ops.row_sumsq(dq[:, :2 * n], segments=2 * heads)  # [L, 2 heads]: q heads, then k heads
+    for lo, q_or_k in ((0, 0), (n, 1)):
+        x = dq[:, lo:lo + n].view(1, seq, heads, d).transpose(1, 2)
+        whole = ops.wan_qk_prep(x, full_ss[None], dw, head_offset=q_or_k * heads, cos=cos, sin=sin)
+        gathered = torch.stack([torch.cat([full_ss[:, r * hl:(r + 1) * hl], full_ss[:, heads + r * hl:heads + (r + 1) * hl]],
+                                          dim=1) for r in range(world)]).contiguous()
+        for r in range(world):
+            part = ops.wan_qk_prep(x[:, r * hl:(r + 1) * hl], gathered, dw[r * hl * d:(r + 1) * hl * d],
+                                   head_offset=q_or_k * hl, cos=cos, sin=sin)
+            assert torch.equal(part, whole[:, r * hl:(r + 1) * hl])
+
+
+def test_wan_glue_rejects_bad_calls() -> None:
+    from faquant_b200 import ops
+
+    qkv, w = _wan_operands(16, 2)
+    dq = qkv.to(DEV)
+    x = dq[:, :256].view(1, 16, 2, 128).transpose(1, 2)
+    ss = ops.row_sumsq(dq[:, :512], segments=4)
+    with pytest.raises(TypeError):  # the sums must be [ranks, tokens, columns]
+        ops.wan_qk_prep(x, ss, w.to(DEV))
+    with pytest.raises(ValueError):  # heads 3..4 of a 4-column block do not exist
+        ops.wan_qk_prep(x, ss[None], w.to(DEV), head_offset=3)
+    with pytest.raises(ValueError):  # 100 columns do not split into 3 segments
+        ops.row_sumsq(dq[:, :100], segments=3)

@@ -174,7 +174,10 @@ def test_qwen3_prefill_stages_match_the_oracle() -> None:
 
 
 def test_wan_block_stages_match_the_oracle() -> None:
-    from faquant_b200.tensor_parallel import TPGroup, WanBlockTP, apply_rope3d
+    """Every stage of a Wan2.2 block at TP 1 against the reference's torch glue and the
+    oracle: the LayerNorms, the W4A4 projections, the fused q/k RMSNorm over all heads +
+    3-D RoPE (fp64) + Hadamard + HiF4 (K4), V's HiF4, the attention and the GELU."""
+    from faquant_b200.tensor_parallel import TPGroup, WanBlockTP, apply_rope3d, wan_qk_norm
 
     block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
     cfg, d, hl = block.cfg, block.cfg.head_dim, block.h_local
@@ -184,25 +187,30 @@ def test_wan_block_stages_match_the_oracle() -> None:
     assert np.isfinite(y).all()
     seq, n = cfg.seq, hl * d
     bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+
+    def layer_norm(t):
+        return torch.nn.functional.layer_norm(bf(t).float(), (cfg.dim,), eps=cfg.eps).to(torch.bfloat16).float()
+
+    _within_ulp(tr[("norm1", 0)].numpy(), layer_norm(x).numpy())
     qkv = tr[("qkv", 0)]
     _close_linear(qkv.numpy(), _oracle_linear(tr[("norm1", 0)].numpy(), block.qkv, True))
-
-    def qk_norm(z, w):
-        zf = bf(z).float()
-        return (zf * torch.rsqrt(zf.pow(2).sum(-1, keepdim=True) / cfg.dim + cfg.eps) * w.cpu()).to(torch.bfloat16)
-
     cos, sin = block.cos.cpu(), block.sin.cpu()
-    q = apply_rope3d(qk_norm(qkv[:, :n], block.norm_q).view(seq, hl, d), cos, sin)
-    assert _rel(tr[("q_rope", 0)].numpy(), q.float().numpy()) <= 1e-3
-    qr, kr = oatt.qk_pretransform(tr[("q_rope", 0)].transpose(0, 1)[None].numpy(),
-                                  tr[("k_rope", 0)].transpose(0, 1)[None].numpy())
+    for name, lo, w in (("qd", 0, block.norm_q), ("kd", n, block.norm_k)):
+        r = apply_rope3d(wan_qk_norm(qkv[:, lo:lo + n], w.cpu(), cfg.dim, cfg.eps).view(seq, hl, d), cos, sin)
+        r = r.transpose(0, 1)[None].numpy()
+        _mostly_equal(tr[(name, 0)].numpy(), oh.fake_quantize(oatt.qk_pretransform(r, r)[0], cfg.levels))
     v = qkv[:, 2 * n:].view(seq, hl, d).transpose(0, 1)[None].numpy()
-    att = oatt.attention(qr, kr, v, causal=False, scale=d**-0.5, normalizer="quantized_same")
+    assert np.array_equal(tr[("vd", 0)].numpy(), oh.fake_quantize(v, cfg.levels))
+    att = oatt.attention(tr[("qd", 0)].numpy(), tr[("kd", 0)].numpy(), tr[("vd", 0)].numpy(), causal=False,
+                         scale=d**-0.5, normalizer="quantized_same", operands_quantized=True)
     _close_attention(tr[("attention", 0)].numpy(), att)
     _close_linear(tr[("o", 0)].numpy(), _oracle_linear(tr[("attention", 0)].reshape(seq, n).numpy(), block.o, True))
+    _within_ulp(tr[("norm2", 0)].numpy(), layer_norm(tr[("x_mid", 0)]).numpy())
     _close_linear(tr[("ffn0", 0)].numpy(), _oracle_linear(tr[("norm2", 0)].numpy(), block.ffn0, True))
-    act = torch.nn.functional.gelu(tr[("ffn0", 0)], approximate="tanh")
-    assert _rel(tr[("act", 0)].numpy(), act.numpy()) <= 1e-2
+    act = bf(torch.nn.functional.gelu(tr[("ffn0", 0)], approximate="tanh")).float().numpy()
+    got = tr[("act", 0)].numpy()
+    # one bf16 ulp; the far negative tail, where 1 + tanh cancels, to an absolute 1e-5
+    assert np.all(np.abs(got - act) <= 2.0**-7 * np.abs(act) + 1e-5)
     _close_linear(tr[("ffn2", 0)].numpy(), _oracle_linear(tr[("act", 0)].numpy(), block.ffn2, True))
 
 
@@ -231,7 +239,7 @@ def _tp_rank(rank: int, world: int, port: int, results) -> None:
         x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
         block(x.to(dev))
         mine = {("qwen",) + k: v.numpy() for k, v in tq.items() if k[1] == 0 and k[0] in ("qkv", "attention", "o")}
-        mine.update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "attention", "o")})
+        mine.update({("wan",) + k: v.numpy() for k, v in tw.items() if k[0] in ("qkv", "qd", "kd", "attention", "o")})
         # a row-parallel projection large enough for the chunked, overlapped all-reduce:
         # with two ranks each element sums two values, so it equals one whole all-reduce
         from faquant_b200.tensor_parallel import TPHiF4Linear, random_weight, row_rotation
@@ -281,6 +289,9 @@ def test_tp2_over_nccl_matches_tp1() -> None:
             k1 = qkv1[:, hq * d + r * nk:hq * d + (r + 1) * nk]
             v1 = qkv1[:, hq * d + hkv * d + r * nk:hq * d + hkv * d + (r + 1) * nk]
             assert np.array_equal(got[(tag, "qkv", 0)], np.concatenate([q1, k1, v1], axis=1)), (tag, r)
+            if tag == "wan":  # the norm over all heads adds the gathered per-head sums in one fixed order
+                for op in ("qd", "kd"):
+                    assert np.array_equal(got[(tag, op, 0)], tr[(op, 0)].numpy()[:, r * hq // 2:(r + 1) * hq // 2])
             assert np.array_equal(got[(tag, "attention", 0)], att1[..., r * hq // 2:(r + 1) * hq // 2, :]), (tag, r)
             o1 = tr[("o", 0)].numpy()
             assert np.all(np.abs(got[(tag, "o", 0)] - o1) <= 2.0**-6 * np.abs(o1) + 2e-3 * np.abs(o1).max()), (tag, r)
