@@ -119,6 +119,79 @@ __device__ __forceinline__ uint32_t hif4_quant8(const float (&v)[8], int levels,
   return nibbles;
 }
 
+// hif4_quant8 on bf16 input held as four pair words (value 2i in the low half of w[i]),
+// with the arithmetic moved off the conversion units: |x| and the sign come from the bit
+// pattern (the sign is dropped on a zero half, sign(-0.0) = +0), 4 qm and ds / 4 are exponent
+// field moves of rec and s (both normal, and they stay normal), and per pair
+//   t   = min(fl(fl(|x| 4qm) + 0.5), 7.5)   (== clamping the code to 7 after the floor)
+//   r   = t + 2^23 rounded toward zero       (== 2^23 + floor(t); the code is r's low bits)
+//   mag = r * ds/4 - 2^23 * ds/4             (one FMA, exact: code * ds/4 has <= 6 bits)
+// so the dequantized value is the top half of mag's pattern with the sign put back.
+// Returns the four dequantized pair words; nib and meta_word as hif4_quant8 when
+// want_codes (which must be the same in all lanes of the warp), else left 0.
+__device__ __forceinline__ uint4 hif4_quant8_bits(const uint32_t (&w)[4], int levels, bool want_codes,
+                                                  uint32_t& nib, uint32_t& meta_word) {
+  uint32_t sgn[4];
+  float2 a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t m = w[i] & 0x7FFF7FFFu;
+    // bit 15 of each half of m + 0x7FFF is set iff that half's magnitude is nonzero
+    sgn[i] = w[i] & (m + 0x7FFF7FFFu) & 0x80008000u;
+    a[i] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+  }
+  const float m3_0 = fmaxf(fmaxf(a[0].x, a[0].y), fmaxf(a[1].x, a[1].y));
+  const float m3_1 = fmaxf(fmaxf(a[2].x, a[2].y), fmaxf(a[3].x, a[3].y));
+  const float m2 = fmaxf(m3_0, m3_1);
+  float m1 = m2;
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 4));
+  const Hif4Scale sc = hif4_scale(m1, levels);
+  uint32_t lv2 = 0, lv3_0 = 0, lv3_1 = 0;
+  if (levels == 123) {
+    lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;
+    const float thr = lv2 ? 4.0f : 2.0f;
+    lv3_0 = __fmul_rn(m3_0, sc.rec) >= thr;
+    lv3_1 = __fmul_rn(m3_1, sc.rec) >= thr;
+  } else if (levels == 12) {
+    lv2 = __fmul_rn(m2, sc.rec) >= 2.0f;
+  } else {
+    lv3_0 = __fmul_rn(m3_0, sc.rec) >= 2.0f;
+    lv3_1 = __fmul_rn(m3_1, sc.rec) >= 2.0f;
+  }
+  const uint32_t rec_q = __float_as_uint(sc.rec) + (2u << 23), s_d = __float_as_uint(sc.s) - (2u << 23);
+  const uint32_t e0 = (lv2 + lv3_0) << 23, e1 = (lv2 + lv3_1) << 23;
+  const float qm[2] = {__uint_as_float(rec_q - e0), __uint_as_float(rec_q - e1)};
+  const float ds[2] = {__uint_as_float(s_d + e0), __uint_as_float(s_d + e1)};
+  const float off[2] = {__uint_as_float(s_d + e0 + 0x8B800000u), __uint_as_float(s_d + e1 + 0x8B800000u)};
+  uint32_t out[4];
+  nib = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qq = i >> 1;  // pairs 0, 1: first quarter; 2, 3: second
+    float2 t = __fadd2_rn(__fmul2_rn(a[i], make_float2(qm[qq], qm[qq])), make_float2(0.5f, 0.5f));
+    t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
+    const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
+    const float2 mag = __ffma2_rn(r, make_float2(ds[qq], ds[qq]), make_float2(off[qq], off[qq]));
+    out[i] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[i];
+    if (want_codes) {
+      const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[i] >> 12) & 8u);
+      const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[i] >> 28) & 8u);
+      nib |= (na | (nb << 4)) << (8 * i);
+    }
+  }
+  meta_word = 0;
+  if (!want_codes) return make_uint4(out[0], out[1], out[2], out[3]);
+  const int pos = threadIdx.x & 7;
+  uint32_t bits = (lv2 << (8 + pos)) | (lv3_0 << (16 + 2 * pos)) | (lv3_1 << (17 + 2 * pos));
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 1);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 2);
+  bits |= __shfl_xor_sync(0xffffffffu, bits, 4);
+  meta_word = bits | sc.code;
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 // Decode one packed nibble with its block's meta word (inverse of the packing).
 __device__ __forceinline__ float hif4_decode(uint32_t nibble, uint32_t meta, int index_in_block) {
   const uint32_t code = meta & 0xFFu;

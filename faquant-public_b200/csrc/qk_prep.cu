@@ -59,172 +59,221 @@ struct QkPrepParams {
   const float* tok_w;           // [heads, d]
   const double* pair_cos;       // [seq, d/2] or null
   const double* pair_sin;
+  int hpw, groups;              // heads per work item, items per token (set by the launch)
+  bool passthrough;             // bf16 input that no stage changes (set by the launch)
 };
 
-template <typename T, int D>
-__global__ void __launch_bounds__(256) qk_prep_kernel(QkPrepParams p) {
+// bf16(fp32(x / c)) for c = fp32(sqrt(128)), the last step of the head_dim Hadamard:
+// returns a value whose bf16 rounding is that of the correctly rounded quotient.
+// q = fl(x * fl(1/c)) is within |x/c| * 2^-23 (1 + 2^-25) of x/c, i.e. within 5 units of
+// the quotient's bit pattern even next to a power of two; when the low 16 bits of q's
+// pattern are 8 or more away from 0 and 0x8000 (the bf16 boundaries) the two round to the
+// same bf16. Otherwise -- and for zero, tiny, infinite or NaN q -- the division is done.
+__device__ __forceinline__ float div_sqrt128_for_bf16(float x) {
+  const float q = __fmul_rn(x, __uint_as_float(0x3DB504F3u));  // fl(1 / fp32(sqrt(128)))
+  const uint32_t bits = __float_as_uint(q);
+  const bool safe = ((bits & 0x7FFFu) - 8u) <= 0x7FF0u && (bits & 0x7F800000u) >= (27u << 23);
+  return safe ? q : __fdiv_rn(x, 11.313708498984761f);
+}
+
+// Work item = (token, group of hpw heads): the index arithmetic and the token's data
+// (Wan's row norm, the RoPE table rows) are set up once per item, and the heads of the
+// group -- neighbours in a [.., S, H, D] projection output -- go RPW per warp iteration.
+// codes/meta rows are in [b, h, s] order. MODE 0: offset/smooth only; MODE 1: Qwen3's
+// per-head RMSNorm and RoPE in front; MODE 2: Wan's row RMSNorm and 3-D RoPE in front.
+template <typename T, int D, int MODE>
+__global__ void __launch_bounds__(256, 4) qk_prep_kernel(QkPrepParams p) {
   constexpr int LANES = D / 8;           // lanes per row
-  constexpr int ROWS_PER_WARP = 32 / LANES;
+  constexpr int RPW = 32 / LANES;        // rows per warp iteration
   const int lane = threadIdx.x & 31;
   const int sub = lane % LANES;          // position of the lane inside its row
-  const int64_t rows = p.batch * p.heads * p.seq;
+  const int slot = lane / LANES;
+  const int64_t items = p.batch * p.seq * p.groups;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  for (int64_t base = warp_id * ROWS_PER_WARP; base < rows; base += warps_total * ROWS_PER_WARP) {
-    const int64_t r = base + lane / LANES;
-    const bool live = r < rows;
-    const int64_t rr = live ? r : 0;
-    const int64_t s = rr % p.seq, h = (rr / p.seq) % p.heads, b = rr / (p.seq * p.heads);
-    const T* src = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + s * p.ss + sub * 8;
-    float v[8];
-    if (p.x_vec) {
-      if constexpr (sizeof(T) == 2) {
-        const uint4 u = *reinterpret_cast<const uint4*>(src);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[2 * i] = __uint_as_float(w[i] << 16);
-          v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-        }
-      } else {
-        const float4 a = reinterpret_cast<const float4*>(src)[0];
-        const float4 c = reinterpret_cast<const float4*>(src)[1];
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if constexpr (sizeof(T) == 2)
-          v[i] = __bfloat162float(src[i]);
-        else
-          v[i] = src[i];
-      }
-    }
-    if (p.norm_w != nullptr) {
-      // Qwen3RMSNorm over the row: sum of squares across the row's lanes
+  uint32_t nw[4] = {0, 0, 0, 0};
+  if (MODE == 1 && p.norm_w != nullptr) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p.norm_w + sub * 8);
+    nw[0] = u.x; nw[1] = u.y; nw[2] = u.z; nw[3] = u.w;
+  }
+  for (int64_t item = warp_id; item < items; item += warps_total) {
+    const int64_t t = item / p.groups;
+    const int h_begin = static_cast<int>(item - t * p.groups) * p.hpw;
+    const int h_end = min(h_begin + p.hpw, static_cast<int>(p.heads));
+    const int64_t b = t / p.seq, s = t - b * p.seq;
+    float tok_r = 0.0f;
+    if (MODE == 2) {
+      // lane l adds heads l, l + 32, ..., then a butterfly: an order fixed by heads_total
       float ss = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));  // h.pow(2), summed
-#pragma unroll
-      for (int ls = 1; ls < LANES; ls <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, ls));
-      const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), p.eps));
-      const uint4 wu = *reinterpret_cast<const uint4*>(p.norm_w + sub * 8);
-      const uint32_t ww[4] = {wu.x, wu.y, wu.z, wu.w};
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float w = __uint_as_float(i & 1 ? ww[i >> 1] & 0xFFFF0000u : ww[i >> 1] << 16);
-        v[i] = bf16_round(__fmul_rn(w, bf16_round(__fmul_rn(v[i], r))));
-      }
-    }
-    if (p.head_ss != nullptr) {
-      // lane `sub` adds heads sub, sub + LANES, ..., then a butterfly over the row's lanes
-      const int64_t t = b * p.seq + s;
-      float ss = 0.0f;
-      for (int64_t g = sub; g < p.heads_total; g += LANES)
+      for (int64_t g = lane; g < p.heads_total; g += 32)
         ss = __fadd_rn(ss, p.head_ss[(g / p.heads_per_block) * p.ss_block_stride + t * p.ss_token_stride +
                                      g % p.heads_per_block]);
 #pragma unroll
-      for (int ls = 1; ls < LANES; ls <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, ls));
-      const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.heads_total * D)), p.eps));
-      const float* w = p.tok_w + h * D + sub * 8;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(bf16_round(__fmul_rn(v[i], r)), w[i]);
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      tok_r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.heads_total * D)), p.eps));
     }
-    if (p.pair_cos != nullptr) {
-      // four complex pairs per lane; the fp32 result stays unrounded into the Hadamard
-      const double* cr = p.pair_cos + s * (D / 2) + sub * 4;
-      const double* sr = p.pair_sin + s * (D / 2) + sub * 4;
+    double pc[4] = {0, 0, 0, 0}, ps[4] = {0, 0, 0, 0};
+    if (MODE == 2 && p.pair_cos != nullptr) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const double re = v[2 * i], im = v[2 * i + 1], c = cr[i], sn = sr[i];
-        v[2 * i] = __double2float_rn(__dsub_rn(__dmul_rn(re, c), __dmul_rn(im, sn)));
-        v[2 * i + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, sn), __dmul_rn(im, c)));
+        pc[i] = p.pair_cos[s * (D / 2) + sub * 4 + i];
+        ps[i] = p.pair_sin[s * (D / 2) + sub * 4 + i];
       }
     }
-    if (p.cos != nullptr) {
-      // HF rotate_half: channel j pairs with j + d/2 (negated) below d/2, with j - d/2 above
-      constexpr int HALF_LANES = LANES / 2;
-      const __nv_bfloat16* cr = p.cos + s * p.rope_ld + sub * 8;
-      const __nv_bfloat16* sr = p.sin + s * p.rope_ld + sub * 8;
-      const uint4 cu = *reinterpret_cast<const uint4*>(cr);
-      const uint4 su = *reinterpret_cast<const uint4*>(sr);
-      const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
-      const bool low = sub < HALF_LANES;
+    for (int h0 = h_begin; h0 < h_end; h0 += RPW) {
+      const bool live = h0 + slot < h_end;
+      const int64_t h = live ? h0 + slot : h_begin;  // idle slots redo a live row, unstored
+      const T* src = static_cast<const T*>(p.x) + b * p.sb + h * p.sh + s * p.ss + sub * 8;
+      float v[8];
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (p.x_vec) {
+        if constexpr (sizeof(T) == 2) {
+          const uint4 u = __ldcs(reinterpret_cast<const uint4*>(src));
+          raw = u;
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[i], HALF_LANES);
-        const float rot = low ? -partner : partner;
-        const float c = __uint_as_float(i & 1 ? cw[i >> 1] & 0xFFFF0000u : cw[i >> 1] << 16);
-        const float sn = __uint_as_float(i & 1 ? sw[i >> 1] & 0xFFFF0000u : sw[i >> 1] << 16);
-        v[i] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(v[i], c)), bf16_round(__fmul_rn(rot, sn))));
-      }
-    }
-    if (p.offset != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fsub_rn(v[i], p.offset[h * D + sub * 8 + i]);
-    }
-    if (p.smooth_mode != 0) {
-      const float* sm = p.smooth + h * p.smooth_head_stride + sub * 8;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = p.smooth_mode == 1 ? __fmul_rn(v[i], sm[i]) : __fdiv_rn(v[i], sm[i]);
-    }
-    if (p.rotate) {
-      // strides 1, 2, 4 inside the lane
-#pragma unroll
-      for (int st = 1; st < 8; st <<= 1) {
+          for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+          }
+        } else {
+          const float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+          const float4 c = __ldcs(reinterpret_cast<const float4*>(src) + 1);
+          v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+          v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+        }
+      } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          if ((i & st) == 0) {
-            const float l = v[i], rgt = v[i + st];
-            v[i] = __fadd_rn(l, rgt);
-            v[i + st] = __fsub_rn(l, rgt);
+          if constexpr (sizeof(T) == 2)
+            v[i] = __bfloat162float(src[i]);
+          else
+            v[i] = src[i];
+        }
+      }
+      if (MODE == 1 && p.norm_w != nullptr) {
+        // Qwen3RMSNorm over the row: sum of squares across the row's lanes
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));  // h.pow(2), summed
+#pragma unroll
+        for (int ls = 1; ls < LANES; ls <<= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, ls));
+        const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), p.eps));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float w = __uint_as_float(i & 1 ? nw[i >> 1] & 0xFFFF0000u : nw[i >> 1] << 16);
+          v[i] = bf16_round(__fmul_rn(w, bf16_round(__fmul_rn(v[i], r))));
+        }
+      }
+      if (MODE == 2) {
+        const float4* w4 = reinterpret_cast<const float4*>(p.tok_w + h * D + sub * 8);
+        const float4 wa = w4[0], wb = w4[1];
+        const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(bf16_round(__fmul_rn(v[i], tok_r)), w[i]);
+      }
+      if (MODE == 2 && p.pair_cos != nullptr) {
+        // four complex pairs per lane; the fp32 result stays unrounded into the Hadamard
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const double re = v[2 * i], im = v[2 * i + 1];
+          v[2 * i] = __double2float_rn(__dsub_rn(__dmul_rn(re, pc[i]), __dmul_rn(im, ps[i])));
+          v[2 * i + 1] = __double2float_rn(__dadd_rn(__dmul_rn(re, ps[i]), __dmul_rn(im, pc[i])));
+        }
+      }
+      if (MODE == 1 && p.cos != nullptr) {
+        // HF rotate_half: channel j pairs with j + d/2 (negated) below d/2, with j - d/2 above
+        constexpr int HALF_LANES = LANES / 2;
+        const bool low = sub < HALF_LANES;
+        // the token's table row, re-read per head from L1 (holding it would spill)
+        const uint4 cu = *reinterpret_cast<const uint4*>(p.cos + s * p.rope_ld + sub * 8);
+        const uint4 su = *reinterpret_cast<const uint4*>(p.sin + s * p.rope_ld + sub * 8);
+        const uint32_t cw[4] = {cu.x, cu.y, cu.z, cu.w}, sw[4] = {su.x, su.y, su.z, su.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float partner = __shfl_xor_sync(0xffffffffu, v[i], HALF_LANES);
+          const float rot = low ? -partner : partner;
+          const float c = __uint_as_float(i & 1 ? cw[i >> 1] & 0xFFFF0000u : cw[i >> 1] << 16);
+          const float sn = __uint_as_float(i & 1 ? sw[i >> 1] & 0xFFFF0000u : sw[i >> 1] << 16);
+          v[i] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(v[i], c)), bf16_round(__fmul_rn(rot, sn))));
+        }
+      }
+      if (p.offset != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __fsub_rn(v[i], p.offset[h * D + sub * 8 + i]);
+      }
+      if (p.smooth_mode != 0) {
+        const float* sm = p.smooth + h * p.smooth_head_stride + sub * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = p.smooth_mode == 1 ? __fmul_rn(v[i], sm[i]) : __fdiv_rn(v[i], sm[i]);
+      }
+      float2 f[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) f[i] = make_float2(v[2 * i], v[2 * i + 1]);
+      if (p.rotate) {
+        // stride 1 inside each pair, 2 and 4 between the lane's pairs
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = make_float2(__fadd_rn(f[i].x, f[i].y), __fsub_rn(f[i].x, f[i].y));
+#pragma unroll
+        for (int d = 1; d < 4; d <<= 1) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if ((i & d) == 0) {
+              const float2 l = f[i], r = f[i + d];
+              f[i] = __fadd2_rn(l, r);
+              f[i + d] = __ffma2_rn(r, make_float2(-1.0f, -1.0f), l);  // l - r, one rounding
+            }
           }
         }
-      }
-      // strides 8 .. D/2 across the lanes of the row
+        // strides 8 .. D/2 across the lanes of the row: the upper lane of a pair takes
+        // other - own, the lower own + other, both as one FMA with a +-1 factor
 #pragma unroll
-      for (int ls = 1; ls < LANES; ls <<= 1) {
+        for (int ls = 1; ls < LANES; ls <<= 1) {
+          const float sg = (sub & ls) ? -1.0f : 1.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float other = __shfl_xor_sync(0xffffffffu, v[i], ls);
-          v[i] = (sub & ls) ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+          for (int i = 0; i < 4; ++i) {
+            const float2 other = make_float2(__shfl_xor_sync(0xffffffffu, f[i].x, ls),
+                                             __shfl_xor_sync(0xffffffffu, f[i].y, ls));
+            f[i] = __ffma2_rn(f[i], make_float2(sg, sg), other);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if constexpr (D == 128)
+            f[i] = make_float2(div_sqrt128_for_bf16(f[i].x), div_sqrt128_for_bf16(f[i].y));
+          else
+            f[i] = __fmul2_rn(f[i], make_float2(0.125f, 0.125f));  // 1/sqrt(64), exact
         }
       }
+      uint32_t w[4];
+      if (sizeof(T) == 2 && p.x_vec && p.passthrough) {
+        w[0] = raw.x; w[1] = raw.y; w[2] = raw.z; w[3] = raw.w;  // no stage changed the bf16 values
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if constexpr (D == 128)
-          v[i] = __fdiv_rn(v[i], 11.313708498984761f);  // fp32(sqrt(128)), correctly rounded divide
-        else
-          v[i] = __fmul_rn(v[i], 0.125f);  // 1/sqrt(64), exact
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 b2 = __float22bfloat162_rn(f[i]);
+          w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(b2.x)) |
+                 (static_cast<uint32_t>(__bfloat16_as_ushort(b2.y)) << 16);
+        }
       }
-    }
+      uint32_t nib = 0, meta_word = 0;
+      const uint4 o = p.levels != 0 ? hif4_quant8_bits(w, p.levels, p.codes != nullptr || p.meta != nullptr, nib, meta_word)
+                                    : make_uint4(w[0], w[1], w[2], w[3]);
+      if (!live) continue;
+      __nv_bfloat16* dst = p.out + b * p.ob + h * p.oh + s * p.os + sub * 8;
+      if (p.out_vec) {
+        __stcs(reinterpret_cast<uint4*>(dst), o);
+      } else {
+        const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = bf16_round(v[i]);
-    float q[8];
-    uint32_t nib = 0, meta_word = 0;
-    if (p.levels != 0) {
-      nib = hif4_quant8(v, p.levels, q, meta_word);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = v[i];
-    }
-    if (!live) continue;
-    __nv_bfloat16* dst = p.out + b * p.ob + h * p.oh + s * p.os + sub * 8;
-    if (p.out_vec) {
-      uint4 u;
-      u.x = exact_bf16_bits(q[0]) | (exact_bf16_bits(q[1]) << 16);
-      u.y = exact_bf16_bits(q[2]) | (exact_bf16_bits(q[3]) << 16);
-      u.z = exact_bf16_bits(q[4]) | (exact_bf16_bits(q[5]) << 16);
-      u.w = exact_bf16_bits(q[6]) | (exact_bf16_bits(q[7]) << 16);
-      *reinterpret_cast<uint4*>(dst) = u;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) dst[i] = __ushort_as_bfloat16(static_cast<unsigned short>(exact_bf16_bits(q[i])));
-    }
-    if (p.levels != 0) {
-      if (p.codes) reinterpret_cast<uint32_t*>(p.codes + r * (D / 2))[sub] = nib;
-      if (p.meta && (lane & 7) == 0) p.meta[r * (D / 64) + sub / 8] = meta_word;
+        for (int i = 0; i < 8; ++i)
+          dst[i] = __ushort_as_bfloat16(static_cast<unsigned short>(i & 1 ? ow[i >> 1] >> 16 : ow[i >> 1] & 0xFFFFu));
+      }
+      if (p.levels != 0) {
+        const int64_t canon = (b * p.heads + h) * p.seq + s;
+        if (p.codes) reinterpret_cast<uint32_t*>(p.codes + canon * (D / 2))[sub] = nib;
+        if (p.meta && (lane & 7) == 0) p.meta[canon * (D / 64) + sub / 8] = meta_word;
+      }
     }
   }
 }
@@ -237,22 +286,51 @@ static int qk_prep_launch(QkPrepParams& p, int x_dtype, int d, void* stream) {
   const uint64_t xa = reinterpret_cast<uintptr_t>(p.x), oa = reinterpret_cast<uintptr_t>(p.out);
   p.x_vec = (xa & 15) == 0 && p.sb % vec_elems == 0 && p.sh % vec_elems == 0 && p.ss % vec_elems == 0;
   p.out_vec = (oa & 15) == 0 && p.ob % 8 == 0 && p.oh % 8 == 0 && p.os % 8 == 0;
-  const int64_t rows = p.batch * p.heads * p.seq;
-  const int rows_per_block = 8 * (32 / (d / 8));
-  const int64_t blocks = std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block,
-                                           static_cast<int64_t>(num_sms()) * 16);
+  // heads per work item: whole tokens when there are enough of them to fill the resident
+  // warps (4 blocks of 8 per SM), fewer heads per item (down to one warp iteration) else
+  const int rpw = 32 / (d / 8);
+  const int64_t tokens = p.batch * p.seq, resident = static_cast<int64_t>(num_sms()) * 32;
+  const int64_t iters_all = (p.heads + rpw - 1) / rpw;
+  const int64_t iters = std::max<int64_t>(1, std::min<int64_t>(iters_all, tokens * iters_all / resident));
+  p.hpw = static_cast<int>(iters * rpw);
+  p.groups = static_cast<int>((p.heads + p.hpw - 1) / p.hpw);
+  const int64_t items = tokens * p.groups;
+  p.passthrough = x_dtype == FAQ_BF16 && p.head_ss == nullptr && p.norm_w == nullptr && p.cos == nullptr &&
+                  p.offset == nullptr && p.smooth_mode == 0 && !p.rotate;
+  // one resident wave: every warp loops over items with the grid's stride
+  const int64_t blocks = std::min<int64_t>((items + 7) / 8, static_cast<int64_t>(num_sms()) * 4);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const unsigned g = static_cast<unsigned>(blocks);
+  const int mode = p.head_ss != nullptr ? 2 : (p.norm_w != nullptr || p.cos != nullptr) ? 1 : 0;
   if (x_dtype == FAQ_BF16) {
-    if (d == 128)
-      qk_prep_kernel<__nv_bfloat16, 128><<<g, 256, 0, st>>>(p);
-    else
-      qk_prep_kernel<__nv_bfloat16, 64><<<g, 256, 0, st>>>(p);
+    if (mode == 2) {
+      if (d == 128)
+        qk_prep_kernel<__nv_bfloat16, 128, 2><<<g, 256, 0, st>>>(p);
+      else
+        qk_prep_kernel<__nv_bfloat16, 64, 2><<<g, 256, 0, st>>>(p);
+    } else if (mode == 1) {
+      if (d == 128)
+        qk_prep_kernel<__nv_bfloat16, 128, 1><<<g, 256, 0, st>>>(p);
+      else
+        qk_prep_kernel<__nv_bfloat16, 64, 1><<<g, 256, 0, st>>>(p);
+    } else {
+      if (d == 128)
+        qk_prep_kernel<__nv_bfloat16, 128, 0><<<g, 256, 0, st>>>(p);
+      else
+        qk_prep_kernel<__nv_bfloat16, 64, 0><<<g, 256, 0, st>>>(p);
+    }
   } else {
-    if (d == 128)
-      qk_prep_kernel<float, 128><<<g, 256, 0, st>>>(p);
-    else
-      qk_prep_kernel<float, 64><<<g, 256, 0, st>>>(p);
+    if (mode == 1) {  // fp32 input with Qwen's norm/RoPE
+      if (d == 128)
+        qk_prep_kernel<float, 128, 1><<<g, 256, 0, st>>>(p);
+      else
+        qk_prep_kernel<float, 64, 1><<<g, 256, 0, st>>>(p);
+    } else {
+      if (d == 128)
+        qk_prep_kernel<float, 128, 0><<<g, 256, 0, st>>>(p);
+      else
+        qk_prep_kernel<float, 64, 0><<<g, 256, 0, st>>>(p);
+    }
   }
   return launch_status("qk_prep_kernel");
 }

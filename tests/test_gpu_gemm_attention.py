@@ -103,6 +103,30 @@ def test_qk_prep_strided_fp32_input_and_per_head_scale() -> None:
     assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), oh.f32_to_bf16_bits(expect))
 
 
+@pytest.mark.parametrize("d", [128, 64])
+def test_qk_prep_hadamard_rounding_over_many_magnitudes(d) -> None:
+    """bf16(Hadamard(x) / sqrt(d)) bit for bit over ~2M fp32 values whose magnitudes span
+    ~70 binades, with zeros, -0.0, values near the bottom of the normal range and a row
+    that overflows to infinity: the head_dim scaling takes a reciprocal product except
+    next to a bf16 rounding boundary, where it divides."""
+    ops = _ops()
+    rng = np.random.default_rng(21)
+    n = (1 << 21) // d
+    x = (rng.standard_normal((n, d)) * np.exp2(rng.integers(-40, 30, (n, 1)))).astype(np.float32)
+    x[0] = 0.0
+    x[1] = -0.0
+    x[2, ::2] = -0.0
+    x[3] = (rng.standard_normal(d) * 2.0**-120).astype(np.float32)
+    x[4] = 0.0
+    x[4, :2] = 3.0e38  # one pair overflows: +-inf and zeros downstream, no inf - inf
+    got = ops.qk_prep(torch.from_numpy(x).to(DEV).view(1, 1, n, d), levels=None, rotate=True)[0]
+    from oracle.rotation import hadamard
+
+    with np.errstate(over="ignore"):
+        expect = oh.f32_to_bf16_bits(oh.bf16_round(hadamard(x)))
+    assert np.array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16).reshape(n, d), expect)
+
+
 def _attention_gpu(q, k, v, *, causal, normalizer, qk_quant, pv_quant, levels="123"):
     ops = _ops()
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
