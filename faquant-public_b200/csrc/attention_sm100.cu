@@ -14,23 +14,25 @@
 //                first four warps take keys 0..63 of every key tile and the other four
 //                keys 64..127 -- one HiF4 group each -- for the same query rows (a
 //                warp reaches the tensor-memory lanes 32 (warp % 4) .. + 31);
-//   warp 16      TMA producer: Q_A and Q_B once, K and V tiles [128 x 128] (two
-//                64-column 128-byte-swizzled chunks each) into 2-stage rings;
+//   warp 16      TMA producer of Q_A and Q_B (once) and of the K tiles [128 x 128] (two
+//                64-column 128-byte-swizzled chunks) into a 2-stage ring;
 //   warp 17      TMEM allocation (512 columns: S_A, S_B, O_A, O_B) and the single
-//                MMA-issuing lane: S_t = Q_t.K_j^T (SS form), O_t += P_t.V_j (TS form:
-//                P is read from tensor memory, V is an MN-major shared-memory operand);
-//                warps 18, 19 have no role.
+//                MMA-issuing lane: S_t = Q_t.K_j^T and O_t += P_t.V_j, both SS form (P is
+//                written by the softmax warps to shared memory in the layout TMA gives
+//                Q; V is an MN-major operand);
+//   warp 18      TMA producer of the V tiles (one stage);
+//   warp 19      no role.
 // Softmax, per key tile and query row, split over the two key halves: tcgen05.ld of the
-// half row of S, mask, partial max; the halves swap partial maxima through shared
-// memory behind a named barrier (which also ANDs their wait results, so a timed-out
-// wait ends both halves at the same iteration); exp2, HiF4 quantization of the half's
-// 64-key group on FP32x2 pairs, a running sum per half (same maxima, so the two sums
-// add up at the end), this half's 64 columns of O rescaled when the max moved (alpha ==
-// 1 is exact and skipped), P stored as packed bf16 over the half's first 32 S columns
-// (keys 64h + 2c, 64h + 2c + 1 in column 64h + c), and at the end O / (sum_0 + sum_1).
-// The two tiles ping-pong: while the softmax warps of one tile work, the tensor core
-// runs the other tile's QK^T and PV. With causal masking both tiles walk the key tiles
-// of tile B; the extra tile of tile A is fully masked (P = 0, alpha = 1: no effect).
+// half row of S and, for the row maximum only, of the other half (no exchange between
+// the warps); as soon as S is in registers the tile's eight warps release it and the
+// tensor core computes the next S_t = Q_t.K_{j+1}^T while they work. Then mask, max,
+// exp2 and HiF4 quantization of the half's 64-key group on FP32x2 pairs, interleaved by
+// 8-key sub-block (the group's scale comes from the largest score), a running sum per
+// half (same maxima, so the two sums add up at the end); once PV_t(j-1) has completed,
+// P goes to shared memory and this half's 64 columns of O are rescaled when the max moved
+// (alpha == 1 is exact and skipped); at the end O / (sum_0 + sum_1). The two tiles
+// share the tensor core; with causal masking both walk the key tiles of tile B, the
+// extra tile of tile A being fully masked (P = 0, alpha = 1: no effect).
 // Every wait is bounded (common.cuh) and warp-uniform for whole-warp roles.
 #include <algorithm>
 
@@ -46,10 +48,10 @@ constexpr int BN = 128;   // keys per tile
 constexpr int D = 128;    // head dim
 constexpr int THREADS = 640;
 constexpr int SOFTMAX_WARPS = 16;
-constexpr int PRODUCER_WARP = 16, MMA_WARP = 17;
+constexpr int PRODUCER_WARP = 16, MMA_WARP = 17, V_WARP = 18;
 constexpr int TILE_BYTES = BM * D * 2;      // 32 KB (two 16 KB chunks)
 constexpr int CHUNK_BYTES = 128 * 128;      // 128 rows x 128 B
-constexpr int KV_STAGES = 2;
+constexpr int K_STAGES = 2;
 constexpr uint32_t IDESC_QK = idesc_bf16_f32(BM, BN, false, false);
 constexpr uint32_t IDESC_PV = idesc_bf16_f32(BM, D, false, true);
 constexpr int TMEM_COLS = 512;
@@ -58,10 +60,9 @@ __device__ __forceinline__ uint32_t o_col(int t) { return t ? 384u : 256u; }
 // smem: Q_A | Q_B | K[2] | V[2] | row exchange [2 parities][2 tiles][2 halves][128] f32 | barriers
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
-constexpr int OFF_V = OFF_K + KV_STAGES * TILE_BYTES;
-constexpr int OFF_RED = OFF_V + KV_STAGES * TILE_BYTES;
-constexpr int RED_PARITY = 2 * 2 * BM;  // floats per parity
-constexpr int OFF_BAR = OFF_RED + 2 * RED_PARITY * 4;
+constexpr int OFF_V = OFF_K + K_STAGES * TILE_BYTES;
+constexpr int OFF_P = OFF_V + TILE_BYTES;  // P_A, P_B; after the last PV, the row sums' exchange
+constexpr int OFF_BAR = OFF_P + 2 * TILE_BYTES;
 constexpr size_t SMEM_BYTES = 1024 + OFF_BAR + 256;
 
 // Named barrier over the `count` threads of one tile's softmax warps that also ANDs a
@@ -164,6 +165,70 @@ __device__ __forceinline__ float quantize_p64(float* f) {
   return __fadd_rn(s.x, s.y);
 }
 
+// exp2 and HiF4 quantization of one 64-key group (this thread's half row, f[0..63] the
+// masked scores), sub-block by sub-block so that the exp2 of one sub-block overlaps the
+// quantization of the previous one. p = ex2(fma(s, c, -m)) as in the unfused form; the
+// group maximum is taken from the scores: p_max = ex2(fma(s_max, c, -m)) is the largest
+// p, since fma with c > 0 and ex2.approx.ftz are both non-decreasing (the second checked
+// over every float in [-inf, 1] on the device, faq_selftest_ex2_monotone). Returns the
+// sum of the quantized values; *raw gets the sum of the unquantized p.
+template <int LEVELS, bool RAW>
+__device__ __forceinline__ float exp_quantize_p64(float* f, float2 c2, float2 mneg, float s_max, float* raw) {
+  const float m1 = ex2(__fmaf_rn(s_max, c2.x, mneg.x));
+  const Hif4Scale sc = hif4_scale(m1, LEVELS);
+  // 4 qm = rec * 2^(2 - sh), ds / 4 = s * 2^(sh - 2) and -2^23 ds / 4 by exponent moves
+  const uint32_t rec_q = __float_as_uint(sc.rec) + (2u << 23), s_d = __float_as_uint(sc.s) - (2u << 23);
+  float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float2 rp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float* v = f + 8 * i;
+    float2 e[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 d = __ffma2_rn(make_float2(v[2 * t], v[2 * t + 1]), c2, mneg);  // s * c - m, one rounding
+      e[t] = make_float2(ex2(d.x), ex2(d.y));
+      if constexpr (RAW) rp[t] = __fadd2_rn(rp[t], e[t]);
+    }
+    const float m3a = fmaxf(fmax3(e[0].x, e[0].y, e[1].x), e[1].y);
+    const float m3b = fmaxf(fmax3(e[2].x, e[2].y, e[3].x), e[3].y);
+    const float m2 = fmaxf(m3a, m3b);
+    uint32_t lv2 = 0, lv3a = 0, lv3b = 0;
+    if constexpr (LEVELS == 123) {
+      lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;
+      const float thr = lv2 ? 4.0f : 2.0f;
+      lv3a = __fmul_rn(m3a, sc.rec) >= thr;
+      lv3b = __fmul_rn(m3b, sc.rec) >= thr;
+    } else if constexpr (LEVELS == 12) {
+      lv2 = __fmul_rn(m2, sc.rec) >= 2.0f;
+    } else {
+      lv3a = __fmul_rn(m3a, sc.rec) >= 2.0f;
+      lv3b = __fmul_rn(m3b, sc.rec) >= 2.0f;
+    }
+    const uint32_t ea = (lv2 + lv3a) << 23, eb = (lv2 + lv3b) << 23;
+    const float qa = __uint_as_float(rec_q - ea), qb = __uint_as_float(rec_q - eb);
+    const float da = __uint_as_float(s_d + ea), db = __uint_as_float(s_d + eb);
+    const float oa = __uint_as_float(s_d + ea + 0x8B800000u), ob = __uint_as_float(s_d + eb + 0x8B800000u);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float qm = t < 2 ? qa : qb, ds = t < 2 ? da : db, off = t < 2 ? oa : ob;
+      float2 y = __fadd2_rn(__fmul2_rn(e[t], make_float2(qm, qm)), make_float2(0.5f, 0.5f));
+      y = make_float2(fminf(y.x, 7.5f), fminf(y.y, 7.5f));
+      const float2 r = __fadd2_rz(y, make_float2(8388608.0f, 8388608.0f));
+      const float2 q = __ffma2_rn(r, make_float2(ds, ds), make_float2(off, off));
+      v[2 * t] = q.x;
+      v[2 * t + 1] = q.y;
+      part[t] = __fadd2_rn(part[t], q);
+    }
+  }
+  if constexpr (RAW) {
+    const float2 r = __fadd2_rn(__fadd2_rn(rp[0], rp[1]), __fadd2_rn(rp[2], rp[3]));
+    *raw = __fadd_rn(r.x, r.y);
+  }
+  const float2 s = __fadd2_rn(__fadd2_rn(part[0], part[1]), __fadd2_rn(part[2], part[3]));
+  return __fadd_rn(s.x, s.y);
+}
+
 // PLEV: HiF4 levels of P (0 = P not quantized); RAW: the denominator sums the raw P
 template <int PLEV, bool RAW>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -175,13 +240,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2 tiles]
-  uint64_t* p_full = bars + 11;  // [2 tiles]
-  uint64_t* o_done = bars + 13;  // [2 tiles]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;   // [2 tiles] S_t(j) computed
+  uint64_t* s_free = bars + 9;   // [2 tiles] S_t(j) read by the tile's eight warps
+  uint64_t* p_full = bars + 11;  // [2 tiles] P_t(j) written, O_t rescaled
+  uint64_t* p_free = bars + 13;  // [2 tiles] PV_t(j) completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  float* red = reinterpret_cast<float*>(base + OFF_RED);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // longest causal rows first: the last query tiles have the most key tiles
@@ -196,14 +261,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_addr(q_full), 1);
+    mbar_init(smem_addr(v_full), 1);
+    mbar_init(smem_addr(v_empty), 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_addr(&k_full[i]), 1);
       mbar_init(smem_addr(&k_empty[i]), 1);
-      mbar_init(smem_addr(&v_full[i]), 1);
-      mbar_init(smem_addr(&v_empty[i]), 1);
       mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&p_full[i]), 8);  // the eight softmax warps of the tile
-      mbar_init(smem_addr(&o_done[i]), 1);
+      mbar_init(smem_addr(&s_free[i]), 8);  // the eight softmax warps of the tile
+      mbar_init(smem_addr(&p_full[i]), 8);
+      mbar_init(smem_addr(&p_free[i]), 1);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tmap_q);
@@ -223,7 +289,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp >= SOFTMAX_WARPS) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 32;\n" ::: "memory");
     if (warp == PRODUCER_WARP) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ Q and K producer
     if (lane == 0 && n_tiles > 0) {
       bool ok = true;
       mbar_arrive_expect_tx(smem_addr(q_full), 2 * TILE_BYTES);
@@ -233,27 +299,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                       static_cast<int>(q0 + t * BM), h, b);
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        const uint32_t ph = ((j >> 1) & 1) ^ 1;
-        if (!mbar_wait_site(smem_addr(&k_empty[st]), ph, 1, j)) { ok = false; break; }
+        if (!mbar_wait_site(smem_addr(&k_empty[st]), ((j >> 1) & 1) ^ 1, 1, j)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_addr(&k_full[st]), TILE_BYTES);
         for (int c = 0; c < 2; ++c)
           tma_load_4d(smem_addr(base + OFF_K + st * TILE_BYTES + c * CHUNK_BYTES), &tmap_k, smem_addr(&k_full[st]),
                       c * 64, j * BN, hk, b);
-        if (!mbar_wait_site(smem_addr(&v_empty[st]), ph, 2, j)) { ok = false; break; }
-        mbar_arrive_expect_tx(smem_addr(&v_full[st]), TILE_BYTES);
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(smem_addr(base + OFF_V + st * TILE_BYTES + c * CHUNK_BYTES), &tmap_v, smem_addr(&v_full[st]),
-                      c * 64, j * BN, hk, b);
       }
       // drain (bounded): every load landed and was consumed before the CTA exits
       if (ok) {
-        for (int j = std::max(0, n_tiles - 2); j < n_tiles; ++j) {
-          const int st = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!mbar_wait_site(smem_addr(&k_empty[st]), ph, 3, j)) break;
-          if (!mbar_wait_site(smem_addr(&v_empty[st]), ph, 3, j)) break;
-        }
+        for (int j = std::max(0, n_tiles - 2); j < n_tiles; ++j)
+          if (!mbar_wait_site(smem_addr(&k_empty[j & 1]), (j >> 1) & 1, 3, j)) break;
       }
+    }
+    __syncwarp();
+    } else if (warp == V_WARP) {
+    // ------------------------------------------------------------ V producer
+    if (lane == 0 && n_tiles > 0) {
+      bool ok = true;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (!mbar_wait_site(smem_addr(v_empty), (j & 1) ^ 1, 2, j)) { ok = false; break; }
+        mbar_arrive_expect_tx(smem_addr(v_full), TILE_BYTES);
+        for (int c = 0; c < 2; ++c)
+          tma_load_4d(smem_addr(base + OFF_V + c * CHUNK_BYTES), &tmap_v, smem_addr(v_full), c * 64, j * BN, hk, b);
+      }
+      if (ok) mbar_wait_site(smem_addr(v_empty), (n_tiles - 1) & 1, 3, n_tiles);
     }
     __syncwarp();
     } else if (warp == MMA_WARP) {
@@ -266,6 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // of waiting on a descriptor chain -- one N = 128 MMA runs only 64 cycles.
       const uint32_t q_desc = sw128_desc_lo(smem_addr(base + OFF_Q), 16);  // LBO unused (K-major SW128)
       const uint32_t k_desc = sw128_desc_lo(smem_addr(base + OFF_K), 16);
+      const uint32_t p_desc = sw128_desc_lo(smem_addr(base + OFF_P), 16);
       const uint32_t v_desc = sw128_desc_lo(smem_addr(base + OFF_V), CHUNK_BYTES);
       constexpr uint32_t TILE_D = TILE_BYTES >> 4;
       // an opaque copy keeps the compiler from hoisting every per-MMA descriptor of the
@@ -276,24 +346,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       // S_t = Q_t . K_j^T
       auto issue_qk = [&](int t, int j) {
-        const uint32_t a = pin(q_desc + t * TILE_D), b = pin(k_desc + (j & 1) * TILE_D);
+        const uint32_t a = pin(q_desc + t * TILE_D), bq = pin(k_desc + (j & 1) * TILE_D);
         const uint32_t d = tmem + s_col(t);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = static_cast<uint32_t>((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;
-          tc_mma_f16_lo(d, a + off, b + off, IDESC_QK, kk != 0);
+          tc_mma_f16_lo(d, a + off, bq + off, IDESC_QK, kk != 0);
         }
         tc_commit(smem_addr(&s_full[t]));
       };
-      // O_t += P_t . V_j; keys 16 kk .. 16 kk + 15 of P_t sit in the 8 packed columns
-      // 64 (kk / 4) + 8 (kk % 4) of S_t (each key half wrote its own first 32 columns)
+      // O_t += P_t . V_j: P_t [128 queries x 128 keys] K-major like Q, V_j MN-major
       auto issue_pv = [&](int t, int j) {
-        const uint32_t b = pin(v_desc + (j & 1) * TILE_D);
-        const uint32_t d = tmem + o_col(t), a = pin(tmem + s_col(t));
+        const uint32_t a = pin(p_desc + t * TILE_D), bv = pin(v_desc);
+        const uint32_t d = tmem + o_col(t);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          tc_mma_f16_ts_lo(d, a + (kk >> 2) * 64 + (kk & 3) * 8, b + ((kk * 2048) >> 4), IDESC_PV, (j | kk) != 0);
-        tc_commit(smem_addr(&o_done[t]));
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t off = static_cast<uint32_t>((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;
+          tc_mma_f16_lo(d, a + off, bv + ((kk * 2048) >> 4), IDESC_PV, (j | kk) != 0);
+        }
+        tc_commit(smem_addr(&p_free[t]));
       };
       if (ok) ok = mbar_wait_site(smem_addr(&k_full[0]), 0, 5, 0);
       if (ok) {
@@ -303,31 +374,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_commit(smem_addr(&k_empty[0]));
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        const bool next = j + 1 < n_tiles;
-        // tile A
-        if (!mbar_wait_site(smem_addr(&p_full[0]), j & 1, 7, j)) break;
-        if (!mbar_wait_site(smem_addr(&v_full[st]), (j >> 1) & 1, 8, j)) break;
-        tc_fence_after();
-        issue_pv(0, j);
-        if (next) {
+        if (j + 1 < n_tiles) {
+          // S_t(j + 1) as soon as the tile's warps hold S_t(j) in registers
           if (!mbar_wait_site(smem_addr(&k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, 5, j + 1)) break;
+          if (!mbar_wait_site(smem_addr(&s_free[0]), j & 1, 6, j)) break;
           tc_fence_after();
-          issue_qk(0, j + 1);  // overwrites S_A after PV_A(j) read P_A from it (tcgen05.mma run in order)
-        }
-        // tile B
-        if (!mbar_wait_site(smem_addr(&p_full[1]), j & 1, 9, j)) break;
-        tc_fence_after();
-        issue_pv(1, j);
-        tc_commit(smem_addr(&v_empty[st]));
-        if (next) {
+          issue_qk(0, j + 1);
+          if (!mbar_wait_site(smem_addr(&s_free[1]), j & 1, 7, j)) break;
+          tc_fence_after();
           issue_qk(1, j + 1);
           tc_commit(smem_addr(&k_empty[(j + 1) & 1]));
         }
+        if (!mbar_wait_site(smem_addr(v_full), j & 1, 8, j)) break;
+        if (!mbar_wait_site(smem_addr(&p_full[0]), j & 1, 9, j)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (!mbar_wait_site(smem_addr(&p_full[1]), j & 1, 10, j)) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        tc_commit(smem_addr(v_empty));
       }
     }
     __syncwarp();
-    }  // warps 18 and 19 have no role
+    }  // warp 19 has no role
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 112;\n" ::: "memory");
     // ------------------------------------------------------------ softmax warps 0..15
@@ -336,42 +405,88 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;          // TMEM lane == query row in the tile
     // Masking in 32 bits (sequence lengths are below 2^31, as the TMA coordinates are):
-    // key tile j needs a mask from j_mask on, and the last visible key of this half of
-    // tile j is lk - 128 j (relative to the half's first key).
-    int j_mask, lk;
+    // key tile j needs a mask in half x from j_mask[x] on, and the last visible key of
+    // half x of tile j is lk[x] - 128 j (relative to the half's first key).
+    int j_mask[2], lk[2];
     {
       const int64_t qpos = q0 + t * BM + row;
       const int64_t last_key = p.causal ? std::min<int64_t>(qpos + offset, p.sk - 1) : p.sk - 1;
       auto first_j = [](int64_t num) -> int64_t { return num < 0 ? 0 : num / BN + 1; };  // least j: BN j > num
-      int64_t jm = first_j(p.sk - 64 - 64 * hh);  // keys past the end
-      if (p.causal) jm = std::min<int64_t>(jm, first_j(q0 + t * BM + offset - 63 - 64 * hh));  // future keys
-      j_mask = static_cast<int>(std::min<int64_t>(jm, n_tiles));
-      lk = static_cast<int>(std::max<int64_t>(-1, last_key - 64 * hh));
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        int64_t jm = first_j(p.sk - 64 - 64 * x);  // keys past the end
+        if (p.causal) jm = std::min<int64_t>(jm, first_j(q0 + t * BM + offset - 63 - 64 * x));  // future keys
+        j_mask[x] = static_cast<int>(std::min<int64_t>(jm, n_tiles));
+        lk[x] = static_cast<int>(std::max<int64_t>(-1, last_key - 64 * x));
+      }
     }
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_addr + s_col(t) + 64 * hh;  // this half's S columns
-    const uint32_t o_addr = tmem + lane_addr + o_col(t) + 64 * hh;  // this half's head dims of O
-    const uint32_t my_red = smem_addr(red + (t * 2 + hh) * BM + row);
-    const uint32_t peer_red = smem_addr(red + (t * 2 + (hh ^ 1)) * BM + row);
-    const int bar_id = 1 + t;  // 0 is __syncthreads
+    const uint32_t s_addr = tmem + lane_addr + s_col(t) + 64 * hh;           // this half's S columns
+    const uint32_t s_other = tmem + lane_addr + s_col(t) + 64 * (hh ^ 1);    // the other half's
+    const uint32_t o_addr = tmem + lane_addr + o_col(t) + 64 * hh;           // this half's head dims of O
+    // P_t in the 128-byte-swizzled K-major layout of a TMA tile: key chunk hh, row `row`,
+    // 16-byte unit u of the row at u ^ (row % 8)
+    const uint32_t p_row = smem_addr(base + OFF_P + t * TILE_BYTES + hh * CHUNK_BYTES + row * 128);
+    const int p_sw = row & 7;
     const float2 c2 = make_float2(p.scale_log2, p.scale_log2);
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const bool w_ok = mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j);
+      if (!mbar_wait_warp(smem_addr(&s_full[t]), j & 1, 12 + t, j)) { ok = false; break; }
       float f[64];  // the half row of S, then P, in place
-      if (w_ok) {
-        tc_fence_after();
+      float omax;
+      tc_fence_after();
+      {
+        float g[32];
         tmem_ld32f(s_addr, f);
         tmem_ld32f(s_addr + 32, f + 32);
+        tmem_ld32f(s_other, g);
         tc_wait_ld();
         reg_fence32f(f);
         reg_fence32f(f + 32);
+        reg_fence32f(g);
+        const int ho = hh ^ 1;
+        if (j >= j_mask[ho]) {
+          const int lim = std::max(-1, std::min(63, lk[ho] - BN * j));
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i > lim) g[i] = -INFINITY;
+        }
+        float m4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) m4[q] = fmax3(g[8 * q], g[8 * q + 1], g[8 * q + 2]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          m4[q] = fmax3(m4[q], g[8 * q + 3], g[8 * q + 4]);
+          m4[q] = fmax3(m4[q], g[8 * q + 5], g[8 * q + 6]);
+          m4[q] = fmaxf(m4[q], g[8 * q + 7]);
+        }
+        tmem_ld32f(s_other + 32, g);
+        tc_wait_ld();
+        reg_fence32f(g);
+        // S_t(j) is in registers: the tensor core may overwrite it with S_t(j + 1)
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&s_free[t]));
+        if (j >= j_mask[ho]) {
+          const int lim = std::max(-1, std::min(63, lk[ho] - BN * j));
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i + 32 > lim) g[i] = -INFINITY;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          m4[q] = fmax3(m4[q], g[8 * q], g[8 * q + 1]);
+          m4[q] = fmax3(m4[q], g[8 * q + 2], g[8 * q + 3]);
+          m4[q] = fmax3(m4[q], g[8 * q + 4], g[8 * q + 5]);
+          m4[q] = fmax3(m4[q], g[8 * q + 6], g[8 * q + 7]);
+        }
+        omax = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
       // mask future / out-of-range keys; the max is taken on the raw scores (the scale is
       // positive, so max(fl(s * c)) == fl(max(s) * c))
-      if (j >= j_mask) {
-        const int lim = std::max(-1, std::min(63, lk - BN * j));
+      if (j >= j_mask[hh]) {
+        const int lim = std::max(-1, std::min(63, lk[hh] - BN * j));
 #pragma unroll
         for (int i = 0; i < 64; ++i)
           if (i > lim) f[i] = -INFINITY;
@@ -385,51 +500,49 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 3; i < 15; i += 2) mx[g] = fmax3(mx[g], f[16 * g + i], f[16 * g + i + 1]);
         mx[g] = fmaxf(mx[g], f[16 * g + 15]);
       }
-      const float pmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      st_shared_f32(my_red + (j & 1) * RED_PARITY * 4, pmax);
-      if (!bar_and(bar_id, 256, w_ok)) { ok = false; break; }
-      const float tmax = fmaxf(pmax, ld_shared_f32(peer_red + (j & 1) * RED_PARITY * 4));
+      const float own_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float tmax = fmaxf(own_max, omax);
       const float m_new = fmaxf(m_run, __fmul_rn(tmax, p.scale_log2));  // log2 domain
       const float m_use = m_new == -INFINITY ? 0.0f : m_new;
       const float alpha = m_run == -INFINITY ? 0.0f : ex2(__fsub_rn(m_run, m_use));
       const float2 mneg = make_float2(-m_use, -m_use);
-      float2 raw[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float2 d = __ffma2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2, mneg);  // s * c - m, one rounding
-        const float2 e = make_float2(ex2(d.x), ex2(d.y));
-        f[2 * i] = e.x;
-        f[2 * i + 1] = e.y;
-        if constexpr (RAW) raw[i & 3] = __fadd2_rn(raw[i & 3], e);
-      }
       float half_sum;
       if constexpr (PLEV != 0) {
-        const float qs = quantize_p64<PLEV>(f);
-        if constexpr (RAW) {
-          const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
-          half_sum = __fadd_rn(r.x, r.y);
-        } else {
-          half_sum = qs;
-        }
+        float raw_sum = 0.0f;
+        const float qs = exp_quantize_p64<PLEV, RAW>(f, c2, mneg, own_max, &raw_sum);
+        half_sum = RAW ? raw_sum : qs;
       } else {
+        float2 raw[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float2 d = __ffma2_rn(make_float2(f[2 * i], f[2 * i + 1]), c2, mneg);  // s * c - m, one rounding
+          const float2 e = make_float2(ex2(d.x), ex2(d.y));
+          f[2 * i] = e.x;
+          f[2 * i + 1] = e.y;
+          raw[i & 3] = __fadd2_rn(raw[i & 3], e);
+        }
         const float2 r = __fadd2_rn(__fadd2_rn(raw[0], raw[1]), __fadd2_rn(raw[2], raw[3]));
         half_sum = __fadd_rn(r.x, r.y);
       }
       l_run = __fadd_rn(__fmul_rn(alpha, l_run), half_sum);
       m_run = m_new;
-      // P as packed bf16 (exact for quantized values) over the half's first 32 S columns,
-      // stored before the O rescale so the two TMEM transfers overlap
-      {
-        float w[32];
+      // PV_t(j - 1) has completed: P_t may be overwritten and O_t is final for step j - 1
+      if (j > 0 && !mbar_wait_warp(smem_addr(&p_free[t]), (j - 1) & 1, 14 + t, j)) { ok = false; break; }
+      tc_fence_after();
+      // P as bf16 (exact for quantized values), 16-byte units of 8 keys
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-          w[i] = __uint_as_float(*reinterpret_cast<const uint32_t*>(&pr));
+      for (int u = 0; u < 8; ++u) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(f[8 * u + 2 * i], f[8 * u + 2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&pr);
         }
-        tmem_st32f(s_addr, w);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(p_row + ((u ^ p_sw) << 4)), "r"(w[0]),
+                     "r"(w[1]), "r"(w[2]), "r"(w[3])
+                     : "memory");
       }
-      // s_full(j) completes after PV_t(j-1) (tcgen05 operations complete in issue order),
-      // so O may be rescaled here
+      fence_proxy_async_smem();  // the tensor core reads P through the async proxy
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
         const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll 1
@@ -446,19 +559,21 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tmem_st32f(o_addr + c * 32, o);
         }
+        tc_wait_st();
       }
-      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&p_full[t]));
     }
     if (n_tiles > 0) {
-      // every warp of the tile takes this barrier once more, whatever happened above
-      const bool e_ok = ok && mbar_wait_warp(smem_addr(&o_done[t]), (n_tiles - 1) & 1, 16 + t, n_tiles);
-      st_shared_f32(my_red + (n_tiles & 1) * RED_PARITY * 4, l_run);
-      if (bar_and(bar_id, 256, e_ok)) {
+      // every warp of the tile takes the barrier below once, whatever happened above
+      const bool e_ok = ok && mbar_wait_warp(smem_addr(&p_free[t]), (n_tiles - 1) & 1, 16 + t, n_tiles);
+      // the row sums of the two halves meet in P_t's buffer, free after the last PV_t
+      const uint32_t red = smem_addr(base + OFF_P + t * TILE_BYTES);
+      st_shared_f32(red + (hh * BM + row) * 4, l_run);
+      if (bar_and(1 + t, 256, e_ok)) {
         tc_fence_after();
-        const float l_sum = __fadd_rn(l_run, ld_shared_f32(peer_red + (n_tiles & 1) * RED_PARITY * 4));
+        const float l_sum = __fadd_rn(l_run, ld_shared_f32(red + ((hh ^ 1) * BM + row) * 4));
         const int64_t qpos = q0 + t * BM + row;
         // tcgen05.ld is .sync.aligned: every lane loads, even the lanes of query rows
         // past the end (a tile can end mid-warp); only the stores are predicated.
@@ -570,4 +685,39 @@ extern "C" int faq_hif4_attention(const void* q, const void* k, const void* v, i
   dim3 grid(p.m_tiles, static_cast<unsigned>(hq), static_cast<unsigned>(batch));
   kern<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return launch_status("hif4_attention_kernel");
+}
+
+namespace faq {
+namespace attn {
+// ex2.approx.ftz over every float in [-inf, 1], in increasing order: counts the
+// consecutive pairs whose results decrease (the group maximum of P above relies on none).
+__device__ unsigned long long g_ex2_violations;
+__device__ __forceinline__ uint32_t ordered_float_bits(uint64_t k) {
+  constexpr uint64_t kNeg = 0xFF800000ull - 0x80000000ull + 1;  // -inf .. -0
+  return k < kNeg ? static_cast<uint32_t>(0xFF800000ull - k) : static_cast<uint32_t>(k - kNeg);
+}
+__global__ void __launch_bounds__(256) ex2_monotone_kernel(uint64_t n) {
+  unsigned long long bad = 0;
+  for (uint64_t k = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; k + 1 < n;
+       k += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+    bad += !(ex2(__uint_as_float(ordered_float_bits(k))) <= ex2(__uint_as_float(ordered_float_bits(k + 1))));
+  if (bad) atomicAdd(&g_ex2_violations, bad);
+}
+}  // namespace attn
+}  // namespace faq
+
+extern "C" int faq_selftest_ex2_monotone(uint64_t* violations, void* stream) {
+  using namespace faq;
+  FAQ_CHECK_ARG(violations, "null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned long long zero = 0;
+  FAQ_CUDA(cudaMemcpyToSymbolAsync(attn::g_ex2_violations, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st));
+  const uint64_t n = (0xFF800000ull - 0x80000000ull + 1) + 0x3F800000ull + 1;  // -inf .. +1.0
+  attn::ex2_monotone_kernel<<<num_sms() * 8, 256, 0, st>>>(n);
+  FAQ_CUDA(cudaGetLastError());
+  unsigned long long bad = 0;
+  FAQ_CUDA(cudaMemcpyFromSymbolAsync(&bad, attn::g_ex2_violations, sizeof(bad), 0, cudaMemcpyDeviceToHost, st));
+  FAQ_CUDA(cudaStreamSynchronize(st));
+  *violations = bad;
+  return FAQ_OK;
 }

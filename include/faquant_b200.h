@@ -267,6 +267,12 @@ int faq_device_trace(unsigned int* records, int max_records, int reset);
  * Exercises the bounded-wait path of the kernels without faulting the GPU. */
 int faq_selftest_wait_timeout(int64_t limit_ns, void* stream);
 
+/* Diagnostics (no counterpart in the reference): evaluates ex2.approx.ftz on every
+ * float in [-inf, 1] in increasing order and stores in *violations the number of
+ * consecutive pairs whose results decrease. K5 takes the HiF4 scale of each 64-key group
+ * of P from the group's largest score, which equals the largest P only when this is 0. */
+int faq_selftest_ex2_monotone(uint64_t* violations, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

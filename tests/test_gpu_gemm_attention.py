@@ -127,6 +127,19 @@ def test_qk_prep_hadamard_rounding_over_many_magnitudes(d) -> None:
     assert np.array_equal(got.cpu().view(torch.int16).numpy().view(np.uint16).reshape(n, d), expect)
 
 
+def test_ex2_is_monotone_on_this_device() -> None:
+    """K5 takes each HiF4 group's scale from ex2 of the group's largest score, which is
+    the largest P only if ex2.approx.ftz never decreases: checked over every float in
+    [-inf, 1] (about 3.2e9 values)."""
+    import ctypes
+
+    from faquant_b200 import _lib
+
+    bad = ctypes.c_uint64(1)
+    _lib.call("faq_selftest_ex2_monotone", ctypes.byref(bad), torch.cuda.current_stream().cuda_stream)
+    assert bad.value == 0
+
+
 def _attention_gpu(q, k, v, *, causal, normalizer, qk_quant, pv_quant, levels="123"):
     ops = _ops()
     qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
