@@ -605,6 +605,55 @@ def kernel_case(name: str, reps: int) -> None:
     print(json.dumps({"kernel_case": name, "reps": reps, "ok": True}))
 
 
+def gpu_reference_attention(reps: int) -> None:
+    """The reference's own Triton attention (`wan22_attention.hif4_attention`, installed
+    under baseline/_ref by pip from the reference checkout) against K5 on BASELINE config 4
+    (Wan2.2: 75 600 tokens, 40 heads, non-causal, HiF4 P, P-Reordering), the same
+    HiF4-prepared operands for both, on this GPU. Prints one JSON line."""
+    import importlib
+
+    import torch
+
+    ref_dir = Path(__file__).resolve().with_name("baseline") / "_ref"
+    try:
+        sys.path.insert(0, str(ref_dir))
+        ref = importlib.import_module("faquant.wan22_attention")
+    except Exception as e:  # noqa: BLE001 - the install is optional
+        print(json.dumps({"gpu_reference": "unavailable", "why": f"{type(e).__name__}: {e}"[:200]}))
+        return
+    from faquant_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    seq, heads, d = 75600, 40, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    prep = [ops.qk_prep(torch.randn(1, heads, seq, d, device=dev, generator=g).to(torch.bfloat16), levels="123",
+                        rotate=rot)[0] for rot in (True, True, False)]
+    views = [t[0].transpose(0, 1) for t in prep]  # the reference's [L, H, D]
+
+    def timed(fn):
+        out = fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            out = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, out
+
+    ms_ref, o_ref = timed(lambda: ref.hif4_attention(*views, softmax_scale=d**-0.5, quantize_p=True,
+                                                     quantized_normalizer=True))
+    ms_our, o_our = timed(lambda: ops.hif4_attention(*prep, scale=d**-0.5, causal=False, p_levels="123",
+                                                     quantized_normalizer=True))
+    flops = 4.0 * d * heads * seq * seq
+    a, b = o_our[0].float(), o_ref.float()
+    print(json.dumps({"gpu_reference": "triton hif4_attention (wan22_attention.py:165-183)",
+                      "workload": "BASELINE config 4 attention: 75600 tokens, 40 heads, d 128, non-causal",
+                      "reference_ms": ms_ref, "reference_tflops": flops / ms_ref / 1e9, "ours_ms": ms_our,
+                      "ours_tflops": flops / ms_our / 1e9, "speedup": ms_ref / ms_our,
+                      "rel_fro_diff": float((a - b).norm() / b.norm()), "reps": reps}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -621,7 +670,12 @@ def main() -> None:
     ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention"],
                     help="run one kernel on a profiling-sized case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--gpu-reference", action="store_true",
+                    help="time the reference's Triton attention (baseline/_ref) beside K5 on config 4 and exit")
     args = ap.parse_args()
+    if args.gpu_reference:
+        gpu_reference_attention(args.reps)
+        return
     if args.kernel_case:
         kernel_case(args.kernel_case, args.reps)
         return
