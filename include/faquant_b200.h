@@ -224,9 +224,9 @@ int faq_hif4_attention(const void* q, const void* k, const void* v, int64_t batc
  * Same semantics and operand contract as faq_hif4_attention (pre-quantized bf16 Q/K/V;
  * out [batch, sq, hq, 128]), the decode call of simulated_flash_attention_forward
  * (simulated_flash_attention.py:457-909 with a growing cache). The keys are split over
- * the GPU in three passes (scores and per-tile row maxima; P and P.V per split of 8 key
- * tiles starting from the exact running max before the split, so every tile's HiF4 P is
- * the sequential one; the join of the splits). `workspace` is a caller-owned device
+ * the GPU in three kernels (scores and per-tile row maxima; P and P.V per split of 2-16
+ * key tiles starting from the exact running max before the split, so every tile's HiF4 P
+ * is the sequential one; the join of the splits). `workspace` is a caller-owned device
  * buffer of at least faq_hif4_decode_workspace_bytes(...) bytes (scores, tile maxima and
  * per-split partial results); it needs no initialization.
  */
