@@ -79,7 +79,12 @@ def init_dist(world: int, backend: str):
 
     if world > 1 and not dist.is_initialized():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {}
+        if backend == "nccl":  # one GPU per rank, named, so NCCL does not guess the mapping
+            import torch
+
+            kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return dist if world > 1 else None
 
 
