@@ -628,6 +628,27 @@ def kernel_case(name: str, reps: int) -> None:
         vd, _, _ = ops.qk_prep(v, levels="123", rotate=False)
         for _ in range(reps):
             ops.hif4_attention(qd, kd, vd, causal=True, p_levels="123", quantized_normalizer=True)
+    elif name == "decode":  # one token, 32 q / 8 kv heads, 32768-key HiF4 cache (config-3 shapes)
+        q = torch.randn(1, 32, 1, 128, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(1, 8, 32768, 128, device=dev, generator=g).to(torch.bfloat16)
+        v = torch.randn(1, 8, 32768, 128, device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(reps):
+            ops.hif4_decode_attention(q, k, v)
+    elif name == "wan_operands":  # K4 on a Wan qkv output: 16800 tokens x 40 heads (config-4 heads)
+        from faquant_b200.tensor_parallel import rope3d_tables
+
+        seq, heads, d = 16800, 40, 128
+        n = heads * d
+        qkv = torch.randn(seq, 3 * n, device=dev, generator=g).to(torch.bfloat16)
+        cos, sin = rope3d_tables((21, 10, 80), d, 10000.0, dev)
+        w = torch.ones(n, device=dev)
+        view = lambda lo: qkv[:, lo:lo + n].view(1, seq, heads, d).transpose(1, 2)  # noqa: E731
+        out = torch.empty(1, heads, seq, d, dtype=torch.bfloat16, device=dev)
+        for _ in range(reps):
+            head_ss = ops.row_sumsq(qkv[:, :2 * n], segments=2 * heads)[None]
+            ops.wan_qk_prep(view(0), head_ss, w, cos=cos, sin=sin, out=out)
+            ops.qk_prep(view(2 * n), rotate=False, out=out)
+            ops.qk_prep(view(2 * n), rotate=True, out=out)
     else:
         raise SystemExit(f"unknown kernel case {name!r}")
     torch.cuda.synchronize()
@@ -696,7 +717,7 @@ def main() -> None:
     ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
     ap.add_argument("--tp-steps", type=int, default=2)
     ap.add_argument("--qwen-layers", type=int, default=64)
-    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention"],
+    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention", "decode", "wan_operands"],
                     help="run one kernel on a profiling-sized case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--gpu-reference", action="store_true",
