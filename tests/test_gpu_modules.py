@@ -208,3 +208,24 @@ def test_wan_hif4_linear_with_fused_reader_rotation() -> None:
                                  levels="123", dtype="f32", signs=rot.signs.numpy(),
                                  permutation=rot.permutation.numpy(), block=64)
     assert np.all(np.abs(y - ref) <= 2.0**-8 * np.abs(ref) + 1e-3 * np.abs(ref).max())
+
+
+def test_chunked_prefill_equals_one_pass() -> None:
+    """The long-context workflow prefills in chunks of whole query tiles against the growing
+    cache (eval_longbench.py:505-540) and relies on every row being computed exactly as in
+    one pass: the key tiles are anchored at key 0 whatever the query chunk, and the K/V HiF4
+    operands are token-local, so the chunked rows are bit-identical to the single pass."""
+    from faquant_b200.attention import simulated_flash_attention_forward
+
+    g = torch.Generator().manual_seed(12)
+    b, h, kv, s = 1, 8, 2, 768
+    q = torch.randn(b, h, s, 128, generator=g).to(torch.bfloat16).to(DEV)
+    k = torch.randn(b, kv, s, 128, generator=g).to(torch.bfloat16).to(DEV)
+    v = torch.randn(b, kv, s, 128, generator=g).to(torch.bfloat16).to(DEV)
+    whole, _ = simulated_flash_attention_forward(_module(True, "quantized_same", True, True), q, k, v, None)
+    module = _module(True, "quantized_same", True, True)
+    first, _ = simulated_flash_attention_forward(module, q[:, :, :512], k[:, :, :512], v[:, :, :512], None)
+    second, _ = simulated_flash_attention_forward(module, q[:, :, 512:], k, v, None)
+    assert torch.equal(first, whole[:, :512]) and torch.equal(second, whole[:, 512:])
+    # the workflow then frees the QDQ copies (decode runs on the BF16 model)
+    assert module.faquant_k_matmul_qdq_cache.shape == (b, kv, s, 128)
