@@ -414,45 +414,49 @@ def main_arm(args) -> None:
             host_x.append(L["x"].cpu().pin_memory())
             host_y.append(torch.empty(T_TOKENS, L["n"], dtype=torch.bfloat16).pin_memory())
 
-        # The projections' host copies are pipelined with their compute: inputs go up on one
-        # side stream, outputs come down on another (PCIe is full duplex, the copy engines are
-        # separate), the compute stream waits for each input and the step ends when the last
-        # output is on the host. Every byte still crosses PCIe inside the timed region.
+        # The projections' host copies are pipelined with their compute, as a serving loop
+        # streams batches: inputs go up on one side stream, outputs come down on another
+        # (PCIe is full duplex, the copy engines are separate), the compute stream waits for
+        # each input, and the next step's inputs go up while this step's outputs still come
+        # down. Projections with the largest outputs go first, so the download starts early.
+        # The timed region ends when the last output of the last step is on the host: every
+        # byte of every step crosses PCIe inside it.
         main = torch.cuda.current_stream()
         s_in, s_out = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+        order = sorted(range(len(mods)), key=lambda i: -host_y[i].numel())
 
         def e2e_step():
-            s_in.wait_stream(main)
-            s_out.wait_stream(main)
             xs, ev_in = [], []
             with torch.cuda.stream(s_in):
-                for hx in host_x:
-                    xs.append(hx.to(device, non_blocking=True))
+                for i in order:
+                    xs.append(host_x[i].to(device, non_blocking=True))
                     ev = torch.cuda.Event()
                     ev.record(s_in)
                     ev_in.append(ev)
-            for m, x, ev, hy in zip(mods, xs, ev_in, host_y):
+            for i, x, ev in zip(order, xs, ev_in):
                 main.wait_event(ev)
                 x.record_stream(main)
-                y = m(x)
+                y = mods[i](x)
                 done = torch.cuda.Event()
                 done.record(main)
                 s_out.wait_event(done)
                 with torch.cuda.stream(s_out):
-                    hy.copy_(y, non_blocking=True)
+                    host_y[i].copy_(y, non_blocking=True)
                 y.record_stream(s_out)
-            main.wait_stream(s_out)
 
         for _ in range(2):
             e2e_step()
-        e_steps = max(3, args.steps // 10)
+        e_steps = max(6, args.steps // 10)
         barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
+        s_in.wait_stream(main)  # no copy starts before e0
+        s_out.wait_stream(main)
         for _ in range(e_steps):
             e2e_step()
+        main.wait_stream(s_out)  # e1 follows the last output's arrival on the host
         e1.record()
         torch.cuda.synchronize()
         barrier()

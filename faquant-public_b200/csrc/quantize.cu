@@ -520,14 +520,15 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
   }
 }
 
-// ---------------------------------------------------------------- K1 v3, rotation, bf16 rows
-// Throughput path for bf16 rows with k % 1024 == 0 and 32 <= block <= 1024 (all HiSQ and
-// r64 shapes of the BASELINE configurations). It is issue-bound (a 1024-point Hadamard is
-// 10 adds per value before any quantization), so the work is counted per element:
-//   - one warp per 1024-channel chunk (4..16 warps); lane l gathers output channels
-//     32l .. 32l+31 of its chunk through a 32-bit map entry (byte offset | sign << 31),
-//     stored lane-transposed so that one 16-byte load brings 4 entries without bank
-//     conflicts; the sign is one XOR of the sign bit (x * -1 is exact);
+// ---------------------------------------------------------------- K1 v4, rotation, bf16 rows
+// Throughput path for bf16 rows with k % 1024 == 0, k <= 16384 and 32 <= block <= 1024
+// (all HiSQ and r64 shapes of the BASELINE configurations). It is issue-bound (a
+// 1024-point Hadamard is 10 adds per value before any quantization), so the work is
+// counted per element:
+//   - one warp per 1024-channel chunk; lane l gathers output channels 32l .. 32l+31 of its
+//     chunk through a 16-bit map entry (byte offset | sign << 15), stored lane-transposed
+//     so that one 16-byte load brings 8 entries without bank conflicts; the sign is one
+//     XOR of the sign bit (x * -1 is exact);
 //   - butterflies (the reference's stage order, rotation.py:22-28): stride 1 inside a
 //     float2, strides 2..16 on float2 pairs (packed FP32x2 adds), a 32x34 shared-memory
 //     transpose, then strides 32..block/2 the same way;
@@ -538,140 +539,168 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 //     magnitude is zero: a -0.0 (an input zero, an underflow of the scaling, or a tiny
 //     negative value rounded to zero in bf16) quantizes to +0 as the reference's
 //     sign(-0.0) == 0 does;
-//   - quantization: one thread per 32 values (half a 64-block), one shuffle for the
-//     block maximum, per-4/per-8 maxima in registers, the element code on FP32x2.
+//   - quantization: one lane per 32 values (half a 64-block), one shuffle for the block
+//     maximum, per-4/per-8 maxima in registers, the element code on FP32x2.
+// A CTA owns one row at a time (the permutation gathers from anywhere in the row), but
+// its warps meet only at the two row buffers:
+//   - full[b] completes when the row in buffer b has landed (cp.async.bulk, complete_tx);
+//   - empty[b] completes when every warp has gathered its chunk out of buffer b;
+//   - lane 0 of warp 0 refills buffer b with the row after next once empty[b] has
+//     completed, at the end of its own row.
+// Each warp stages its rotated chunk in its own transpose scratch and quantizes it from
+// there (the 64-blocks of a chunk never cross chunks), so no CTA-wide barrier is left in
+// the row loop and the warps of a CTA drift freely over a row. The launch bounds hold
+// every width class to the registers of 20 resident warps per SM (the shared memory of a
+// 4-warp CTA allows 5).
 __device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
 // a - b as one packed FMA: b * -1 + a, a single rounding of the exact difference
 __device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
 
-template <int LOG2B, bool CODES>
-__global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
-                                                             int64_t ldx, const __nv_bfloat16* __restrict__ input_scale,
-                                                             const int8_t* __restrict__ signs,
-                                                             const int64_t* __restrict__ perm, int levels, QuantOut o) {
+// map entry w = ((chunk * 4 + t8) * 32 + lane) * 8 + e8 describes output channel
+// chunk * 1024 + 32 lane + 8 t8 + e8
+__device__ __forceinline__ int v4_map_channel(int w) {
+  return (w & ~1023) + 32 * ((w >> 3) & 31) + 8 * ((w >> 8) & 3) + (w & 7);
+}
+
+__device__ __forceinline__ float v4_gathered(const unsigned char* in, uint32_t off, uint32_t sign,
+                                             const __nv_bfloat16* __restrict__ input_scale) {
+  uint32_t bits = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(in + off)) << 16;
+  if (input_scale != nullptr)
+    bits = __float_as_uint(bf16_round(__fmul_rn(__uint_as_float(bits), __bfloat162float(input_scale[off >> 1]))));
+  return __uint_as_float(bits ^ sign);
+}
+
+constexpr int kK1Warps = 20;  // resident warps per SM the launch bounds size registers for
+
+template <int LOG2B, bool CODES, int MAXW>
+__global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MAXW : 1) hif4_rotate_v4_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t rows, int k, int64_t ldx,
+    const __nv_bfloat16* __restrict__ input_scale, const int8_t* __restrict__ signs,
+    const int64_t* __restrict__ perm, int levels, QuantOut o) {
   constexpr int B = 1 << LOG2B;
-  static_assert(B >= 32 && B <= 1024, "v3 handles blocks 32..1024");
+  static_assert(B >= 32 && B <= 1024, "v4 handles blocks 32..1024");
   constexpr int TS = 34;  // transpose row stride (floats): 64-bit stores and column loads conflict-free
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int NW = blockDim.x >> 5;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
-  uint32_t* s_map = reinterpret_cast<uint32_t*>(smem_raw + 16);                                   // [k]
-  unsigned char* s_in = smem_raw + 16 + static_cast<size_t>(k) * 4;                                // [2][k] bf16
-  float* s_tr = reinterpret_cast<float*>(smem_raw + 16 + static_cast<size_t>(k) * 8);             // [NW][32*TS]
-  // the rotated row [k] bf16 reuses the transpose scratch once every warp is past its
-  // transpose (NW * 32 * TS * 4 >= 2 k bytes); each warp owns exactly one 1024-chunk
-  uint16_t* s_out = reinterpret_cast<uint16_t*>(s_tr);
+  const int W = blockDim.x >> 5;  // == k / 1024
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + 2;
+  unsigned char* s_map = smem_raw + 32;
+  unsigned char* s_in = s_map + static_cast<size_t>(k) * 2;                    // [2][k] bf16
+  float* s_tr = reinterpret_cast<float*>(s_in + static_cast<size_t>(k) * 4);  // [W][32 * TS]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
-  const int nchunks = k >> 10;
+  const int64_t G = gridDim.x;
+  const int64_t first = blockIdx.x;
+  const bool loader = tid == 0;
+  uint32_t pending = 0;  // loader: bit b set while a load into buffer b is in flight unconsumed
 
-  if (tid == 0) {
-    mbar_init(smem_addr(&bars[0]), 1);
-    mbar_init(smem_addr(&bars[1]), 1);
+  if (loader) {
+    mbar_init(smem_addr(&full[0]), 1);
+    mbar_init(smem_addr(&full[1]), 1);
+    mbar_init(smem_addr(&empty[0]), W);
+    mbar_init(smem_addr(&empty[1]), W);
     fence_barrier_init();
+    for (int b = 0; b < 2; ++b) {
+      const int64_t r = first + b * G;
+      if (r < rows) {
+        mbar_arrive_expect_tx(smem_addr(&full[b]), row_bytes);
+        bulk_load(smem_addr(s_in + b * row_bytes), x + r * ldx, row_bytes, smem_addr(&full[b]));
+        pending |= 1u << b;
+      }
+    }
   }
-  // entry (chunk, t4, lane, e) at word ((chunk*8 + t4)*32 + lane)*4 + e describes output
-  // channel chunk*1024 + 32*lane + 4*t4 + e
-  for (int w = tid; w < k; w += blockDim.x) {
-    const int e = w & 3, l = (w >> 2) & 31, t4 = (w >> 7) & 7, ch = w >> 10;
-    const int j = (ch << 10) + 32 * l + 4 * t4 + e;
-    const int src = perm ? static_cast<int>(perm[j]) : j;
-    s_map[w] = static_cast<uint32_t>(src * 2) | ((signs[src] < 0) ? 0x80000000u : 0u);
+  // the map, built while the first rows load: all permutation reads of a batch are in
+  // flight together, then all sign reads
+  {
+    constexpr int U = 16;
+    for (int w0 = tid; w0 < k; w0 += U * static_cast<int>(blockDim.x)) {
+      int src[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int w = w0 + u * static_cast<int>(blockDim.x);
+        const int j = v4_map_channel(w);
+        src[u] = w < k ? (perm ? static_cast<int>(perm[j]) : j) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int w = w0 + u * static_cast<int>(blockDim.x);
+        if (w < k) {
+          const bool neg = signs[src[u]] < 0;
+          reinterpret_cast<uint16_t*>(s_map)[w] = static_cast<uint16_t>((src[u] * 2) | (neg ? 0x8000 : 0));
+        }
+      }
+    }
   }
   __syncthreads();
-  const int64_t first = blockIdx.x;
-  if (tid == 0) {
-    for (int b = 0; b < 2; ++b) {
-      const int64_t r = first + static_cast<int64_t>(b) * gridDim.x;
-      if (r < rows) {
-        mbar_arrive_expect_tx(smem_addr(&bars[b]), row_bytes);
-        bulk_load(smem_addr(s_in + b * row_bytes), x + r * ldx, row_bytes, smem_addr(&bars[b]));
-      }
-    }
-  }
+
+  const int ch = warp;
   float* tr = s_tr + warp * (32 * TS);
-  const int tasks = k >> 5;  // 32-value halves of 64-blocks
+  uint16_t* s_outw = reinterpret_cast<uint16_t*>(tr);  // this warp's rotated chunk, 1024 bf16
+  const uint4* mrow = reinterpret_cast<const uint4*>(s_map) + (ch << 7) + lane;
+  const int rot = (lane >> 1) & 3;  // rotation of this lane's staged row, see below
   int it = 0;
-  for (int64_t row = first; row < rows; row += gridDim.x, ++it) {
+  for (int64_t row = first; row < rows; row += G, ++it) {
     const int buf = it & 1;
-    if (!__syncthreads_and(mbar_wait(smem_addr(&bars[buf]), (it >> 1) & 1))) {
-      if (tid == 0) {
-        trace_timeout(31, it);
-        for (int b = 0; b < 2; ++b) {
-          const int64_t r = row + static_cast<int64_t>(b) * gridDim.x;
-          if (r < rows) mbar_wait(smem_addr(&bars[(it + b) & 1]), ((it + b) >> 1) & 1);
-        }
-      }
-      break;
-    }
+    if (!mbar_wait_warp(smem_addr(&full[buf]), (it >> 1) & 1, 31, it)) break;
+    if (loader) pending &= ~(1u << buf);
     const unsigned char* in = s_in + buf * row_bytes;
-    const int ch = warp;  // nchunks <= NW: one chunk per warp (or none)
     float2 p[16];
-    if (ch < nchunks) {
-      const uint4* mrow = reinterpret_cast<const uint4*>(s_map) + (ch << 8) + lane;
 #pragma unroll
-      for (int t4 = 0; t4 < 8; ++t4) {
-        const uint4 m4 = mrow[t4 * 32];
-        const uint32_t m[4] = {m4.x, m4.y, m4.z, m4.w};
-        float g[4];
+    for (int t8 = 0; t8 < 4; ++t8) {
+      const uint4 m4 = mrow[t8 * 32];
+      const uint32_t m[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t off = m[e] & 0x7FFFFFFFu;
-          uint32_t bits = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(in + off)) << 16;
-          if (input_scale != nullptr)
-            bits = __float_as_uint(bf16_round(__fmul_rn(__uint_as_float(bits), __bfloat162float(input_scale[off >> 1]))));
-          g[e] = __uint_as_float(bits ^ (m[e] & 0x80000000u));
+      for (int h = 0; h < 4; ++h)
+        p[4 * t8 + h] = make_float2(v4_gathered(in, m[h] & 0x7FFFu, (m[h] << 16) & 0x80000000u, input_scale),
+                                    v4_gathered(in, (m[h] >> 16) & 0x7FFFu, m[h] & 0x80000000u, input_scale));
+    }
+    // stride 1: inside each float2 (the gathered values are consumed here)
+#pragma unroll
+    for (int q = 0; q < 16; ++q) p[q] = make_float2(__fadd_rn(p[q].x, p[q].y), __fsub_rn(p[q].x, p[q].y));
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(&empty[buf]));  // this warp is done with the buffer
+    // strides 2 .. 16 (and < B): float2 index distance d = stride / 2
+#pragma unroll
+    for (int d = 1; d < 16 && 2 * d < B; d <<= 1) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        if ((q & d) == 0) {
+          const float2 l = p[q], r = p[q + d];
+          p[q] = f2add(l, r);
+          p[q + d] = f2sub(l, r);
         }
-        p[2 * t4] = make_float2(g[0], g[1]);
-        p[2 * t4 + 1] = make_float2(g[2], g[3]);
       }
-      // stride 1: inside each float2
+    }
+    // transpose through the warp's scratch: lane c then holds channels c + 32 i
+#pragma unroll
+    for (int q = 0; q < 16; ++q) *reinterpret_cast<float2*>(tr + lane * TS + 2 * q) = p[q];
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 16; ++q) p[q] = make_float2(tr[(2 * q) * TS + lane], tr[(2 * q + 1) * TS + lane]);
+    __syncwarp();
+    // strides 32 .. B/2: i xor 1 inside the float2, then float2 distance d
+    if constexpr (B >= 64) {
 #pragma unroll
       for (int q = 0; q < 16; ++q) p[q] = make_float2(__fadd_rn(p[q].x, p[q].y), __fsub_rn(p[q].x, p[q].y));
-      // strides 2 .. 16 (and < B): float2 index distance d = stride / 2
+    }
 #pragma unroll
-      for (int d = 1; d < 16 && 2 * d < B; d <<= 1) {
+    for (int d = 1; 64 * d < B; d <<= 1) {
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if ((q & d) == 0) {
-            const float2 l = p[q], r = p[q + d];
-            p[q] = f2add(l, r);
-            p[q + d] = f2sub(l, r);
-          }
-        }
-      }
-      // transpose through shared memory: lane c then holds channels c + 32 i
-#pragma unroll
-      for (int q = 0; q < 16; ++q) *reinterpret_cast<float2*>(tr + lane * TS + 2 * q) = p[q];
-      __syncwarp();
-#pragma unroll
-      for (int q = 0; q < 16; ++q) p[q] = make_float2(tr[(2 * q) * TS + lane], tr[(2 * q + 1) * TS + lane]);
-      __syncwarp();
-      // strides 32 .. B/2: i xor 1 inside the float2, then float2 distance d
-      if constexpr (B >= 64) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) p[q] = make_float2(__fadd_rn(p[q].x, p[q].y), __fsub_rn(p[q].x, p[q].y));
-      }
-#pragma unroll
-      for (int d = 1; 64 * d < B; d <<= 1) {
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if ((q & d) == 0) {
-            const float2 l = p[q], r = p[q + d];
-            p[q] = f2add(l, r);
-            p[q + d] = f2sub(l, r);
-          }
+      for (int q = 0; q < 16; ++q) {
+        if ((q & d) == 0) {
+          const float2 l = p[q], r = p[q + d];
+          p[q] = f2add(l, r);
+          p[q + d] = f2sub(l, r);
         }
       }
     }
-    __syncthreads();  // every warp is past its transpose: the scratch now holds the rotated row
-    if (ch < nchunks) {
-      // s_out is stored with the 16-byte chunk index c rotated in its low 2 bits by
-      // (c >> 3): chunk c of the row lives at (c & ~3) | ((c + (c >> 3)) & 3). Lane writes
-      // stay contiguous, and the quantization pass's 16-byte reads (4 consecutive chunks
-      // per thread) spread over all banks. For element 32 i + lane of a chunk the rotated
-      // low bits are ((lane >> 3) + (i >> 1)) & 3.
-      uint16_t* out = s_out + (ch << 10) + (lane & 7);
+    // Stage the rotated chunk as bf16, 32-value row i = channels 32 i .. 32 i + 31, with
+    // the 16-byte unit u of row i at (u + (i >> 1)) & 3: lane writes stay one 64-byte
+    // span per instruction, and the quantization below (lane i reads row i's units in
+    // the order u = 0..3, each from its rotated place) hits 8 different 16-byte bank
+    // groups in every quarter-warp. For lane c, element i sits in unit c >> 3 of row i.
+    {
+      uint16_t* out = s_outw + (lane & 7);
       int rot8[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) rot8[r] = 8 * (((lane >> 3) + r) & 3);
@@ -692,41 +721,31 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
         out[(2 * q + 1) * 32 + rot8[q & 3]] = __bfloat16_as_ushort(b2.y);
       }
     }
-    __syncthreads();
-    if (tid == 0) {
-      const int64_t r2 = row + 2 * static_cast<int64_t>(gridDim.x);
-      if (r2 < rows) {
-        mbar_arrive_expect_tx(smem_addr(&bars[buf]), row_bytes);
-        bulk_load(smem_addr(s_in + buf * row_bytes), x + r2 * ldx, row_bytes, smem_addr(&bars[buf]));
-      }
-    }
-    // quantization: thread = 32 consecutive values; partner lane (tid ^ 1) holds the other half.
-    // Slot s (16 bytes = one sub-block of 8 values) of the thread holds logical sub-block
-    // qs = (s - (task >> 1)) & 3 because of the rotated layout above.
-    for (int t0 = 0; t0 < tasks; t0 += blockDim.x) {
-      const int task = t0 + tid;
-      const bool live = task < tasks;
-      const int col = (live ? task : 0) * 32;
-      const int rot = (task >> 1) & 3;
+    __syncwarp();
+    // quantization: lane l = channels 32 l .. 32 l + 31 of the chunk (half a 64-block; the
+    // partner lane l ^ 1 holds the other half)
+    {
+      const int col = (ch << 10) + 32 * lane;
       uint32_t sgn[16];  // sign bits of each bf16 pair, clear on a zero half
-      float2 a[16];      // |x| pairs, slot-major
+      float2 a[16];      // |x| pairs, in channel order
       {
-        const uint4* src = reinterpret_cast<const uint4*>(s_out + col);
+        const uint4* src = reinterpret_cast<const uint4*>(s_outw + 32 * lane);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 u = src[q];
-          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+        for (int u = 0; u < 4; ++u) {
+          const uint4 v = src[(u + rot) & 3];
+          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             const uint32_t w = w4[h];
             const uint32_t m = w & 0x7FFF7FFFu;
             // bit 15 of each half of m + 0x7FFF is set iff that half's magnitude is nonzero
             // (no carry crosses the halves: 0x7FFF + 0x7FFF < 2^16)
-            sgn[4 * q + h] = w & (m + 0x7FFF7FFFu) & 0x80008000u;
-            a[4 * q + h] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+            sgn[4 * u + h] = w & (m + 0x7FFF7FFFu) & 0x80008000u;
+            a[4 * u + h] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
           }
         }
       }
+      __syncwarp();  // the scratch is free for the next row's transpose
       float m3[8], m2[4];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[2 * i].x, a[2 * i].y), fmaxf(a[2 * i + 1].x, a[2 * i + 1].y));
@@ -735,81 +754,80 @@ __global__ void __launch_bounds__(512) hif4_rotate_v3_kernel(const __nv_bfloat16
       float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
       m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
       const Hif4Scale sc = hif4_scale(m1, levels);
-      uint32_t lvbits = 0;  // bit qs: lv2 of logical sub-block qs, bit 4+j: lv3 of logical quarter j
-      float2 qm4[8], ds4[8], off4[8];
+      uint32_t lvbits = 0;  // bit s: lv2 of sub-block s, bit 4+j: lv3 of quarter j
       const uint32_t rec_q0 = __float_as_uint(sc.rec) + (2u << 23);  // 4 * rec
       const uint32_t s_d0 = __float_as_uint(sc.s) - (2u << 23);      // s / 4
+      uint32_t nib[4] = {0, 0, 0, 0};
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int qs = (i - rot) & 3;
+      for (int s = 0; s < 4; ++s) {
         uint32_t lv2 = 0, la = 0, lb = 0;
         if (levels == 123) {
-          lv2 = __fmul_rn(m2[i], sc.rec) >= 4.0f;
+          lv2 = __fmul_rn(m2[s], sc.rec) >= 4.0f;
           const float thr = lv2 ? 4.0f : 2.0f;
-          la = __fmul_rn(m3[2 * i], sc.rec) >= thr;
-          lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= thr;
+          la = __fmul_rn(m3[2 * s], sc.rec) >= thr;
+          lb = __fmul_rn(m3[2 * s + 1], sc.rec) >= thr;
         } else if (levels == 12) {
-          lv2 = __fmul_rn(m2[i], sc.rec) >= 2.0f;
+          lv2 = __fmul_rn(m2[s], sc.rec) >= 2.0f;
         } else {
-          la = __fmul_rn(m3[2 * i], sc.rec) >= 2.0f;
-          lb = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
+          la = __fmul_rn(m3[2 * s], sc.rec) >= 2.0f;
+          lb = __fmul_rn(m3[2 * s + 1], sc.rec) >= 2.0f;
         }
-        lvbits |= (lv2 << qs) | (la << (4 + 2 * qs)) | (lb << (5 + 2 * qs));
+        lvbits |= (lv2 << s) | (la << (4 + 2 * s)) | (lb << (5 + 2 * s));
         // 4 qm = rec * 2^(2 - sh) and ds / 4 = s * 2^(sh - 2) by moving the exponent field
         // (rec and s are normal and stay normal); off = -2^23 * ds / 4 likewise
         const uint32_t ea = (lv2 + la) << 23, eb = (lv2 + lb) << 23;
-        const uint32_t qa = rec_q0 - ea, qb = rec_q0 - eb, da = s_d0 + ea, db = s_d0 + eb;
-        qm4[2 * i] = make_float2(__uint_as_float(qa), __uint_as_float(qa));
-        qm4[2 * i + 1] = make_float2(__uint_as_float(qb), __uint_as_float(qb));
-        ds4[2 * i] = make_float2(__uint_as_float(da), __uint_as_float(da));
-        ds4[2 * i + 1] = make_float2(__uint_as_float(db), __uint_as_float(db));
-        off4[2 * i] = make_float2(__uint_as_float(da + 0x8B800000u), __uint_as_float(da + 0x8B800000u));
-        off4[2 * i + 1] = make_float2(__uint_as_float(db + 0x8B800000u), __uint_as_float(db + 0x8B800000u));
-      }
-      uint32_t packed[16];
-      uint32_t nib[4] = {0, 0, 0, 0};
+        const float2 qm_a = make_float2(__uint_as_float(rec_q0 - ea), __uint_as_float(rec_q0 - ea));
+        const float2 qm_b = make_float2(__uint_as_float(rec_q0 - eb), __uint_as_float(rec_q0 - eb));
+        const float2 ds_a = make_float2(__uint_as_float(s_d0 + ea), __uint_as_float(s_d0 + ea));
+        const float2 ds_b = make_float2(__uint_as_float(s_d0 + eb), __uint_as_float(s_d0 + eb));
+        const float2 of_a = make_float2(__uint_as_float(s_d0 + ea + 0x8B800000u), __uint_as_float(s_d0 + ea + 0x8B800000u));
+        const float2 of_b = make_float2(__uint_as_float(s_d0 + eb + 0x8B800000u), __uint_as_float(s_d0 + eb + 0x8B800000u));
+        uint32_t packed[4];
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        // pair q = values 2q, 2q+1 of slot q / 4, both in its half q / 2:
-        //   t = min(fl(fl(|x| 4qm) + 0.5), 7.5)  (== clamping the code to 7 after the floor)
-        //   r = t + 2^23 rounded toward zero    (== 2^23 + floor(t))
-        //   mag = r * ds/4 - 2^23 * ds/4        (one FMA, exact: code * ds/4 has <= 6 bits)
-        float2 t = __fadd2_rn(__fmul2_rn(a[q], qm4[q >> 1]), make_float2(0.5f, 0.5f));
-        t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
-        const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
-        const float2 mag = __ffma2_rn(r, ds4[q >> 1], off4[q >> 1]);
-        packed[q] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[q];
-        if constexpr (CODES) {
-          const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[q] >> 12) & 8u);  // r = 2^23 + code
-          const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[q] >> 28) & 8u);
-          nib[q >> 2] |= (na | (nb << 4)) << (8 * (q & 3));
-        }
-      }
-      const int half = task & 1;
-      uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
-      mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
-      if (live) {
-        if (o.qdq) {
-          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col;
-#pragma unroll
-          for (int sl = 0; sl < 4; ++sl)
-            *reinterpret_cast<uint4*>(dst + 8 * ((sl - rot) & 3)) =
-                make_uint4(packed[4 * sl], packed[4 * sl + 1], packed[4 * sl + 2], packed[4 * sl + 3]);
-        }
-        if constexpr (CODES) {
-          if (o.codes) {
-            uint32_t* cdst = reinterpret_cast<uint32_t*>(o.codes + row * (k / 2) + col / 2);
-#pragma unroll
-            for (int sl = 0; sl < 4; ++sl) cdst[(sl - rot) & 3] = nib[sl];
+        for (int h = 0; h < 4; ++h) {
+          // pair q = values 2q, 2q+1 of sub-block s, in quarter h / 2:
+          //   t = min(fl(fl(|x| 4qm) + 0.5), 7.5)  (== clamping the code to 7 after the floor)
+          //   r = t + 2^23 rounded toward zero    (== 2^23 + floor(t))
+          //   mag = r * ds/4 - 2^23 * ds/4        (one FMA, exact: code * ds/4 has <= 6 bits)
+          const int q = 4 * s + h;
+          float2 t = __fadd2_rn(__fmul2_rn(a[q], h < 2 ? qm_a : qm_b), make_float2(0.5f, 0.5f));
+          t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
+          const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
+          const float2 mag = __ffma2_rn(r, h < 2 ? ds_a : ds_b, h < 2 ? of_a : of_b);
+          packed[h] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[q];
+          if constexpr (CODES) {
+            const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[q] >> 12) & 8u);  // r = 2^23 + code
+            const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[q] >> 28) & 8u);
+            nib[s] |= (na | (nb << 4)) << (8 * h);
           }
         }
-        if (o.meta && half == 0) o.meta[row * (k / 64) + task / 2] = mb | sc.code;
+        if (o.qdq) *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      }
+      const int half = lane & 1;
+      uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
+      mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
+      if constexpr (CODES) {
+        if (o.codes) *reinterpret_cast<uint4*>(o.codes + row * (k / 2) + col / 2) = make_uint4(nib[0], nib[1], nib[2], nib[3]);
+      }
+      if (o.meta && half == 0) o.meta[row * (k / 64) + col / 64] = mb | sc.code;
+    }
+    // refill this buffer with the row after next once every warp has gathered from it
+    if (loader) {
+      const int64_t r2 = row + 2 * G;
+      if (r2 < rows && mbar_wait_site(smem_addr(&empty[buf]), (it >> 1) & 1, 32, it)) {
+        mbar_arrive_expect_tx(smem_addr(&full[buf]), row_bytes);
+        bulk_load(smem_addr(s_in + buf * row_bytes), x + r2 * ldx, row_bytes, smem_addr(&full[buf]));
+        pending |= 1u << buf;
       }
     }
-    // no barrier here: the next iteration opens with a CTA-wide one before the scratch is
-    // written again
   }
-  __syncthreads();
+  // a wait that gave up leaves loads in flight: let them land (bounded) before exiting.
+  // Buffer b has completed (it - b + 1) / 2 phases by iteration `it`.
+  if (loader) {
+    for (int b = 0; b < 2; ++b)
+      if ((pending >> b) & 1u) mbar_wait(smem_addr(&full[b]), static_cast<uint32_t>((it - b + 1) >> 1) & 1u);
+  }
 }
 
 // ---------------------------------------------------------------- dequantize
@@ -949,35 +967,46 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
 #undef FAQ_ROTS_CASE
   }
   if constexpr (sizeof(T) == 2) {
-    const bool v3 = k % 1024 == 0 && k <= 16384 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
+    const bool v4 = k % 1024 == 0 && k <= 16384 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
                     (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
-    if (v3) {
-      const int warps3 = std::min(16, std::max(4, static_cast<int>(k / 1024)));
-      const size_t smem3 = 16 + static_cast<size_t>(k) * 8 + static_cast<size_t>(warps3) * 32 * 34 * 4;
-      if (smem3 <= 200 * 1024) {
-        const int per_sm = std::max(1, std::min(8, static_cast<int>((224 * 1024) / (smem3 + 1024))));
-        const int64_t blocks3 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
+    if (v4) {
+      // one warp per 1024-chunk: barriers, map (2 B per channel), two row buffers, one
+      // 32 x 34 float transpose scratch per warp
+      const int W = static_cast<int>(k / 1024);
+      const size_t smem4 = 32 + static_cast<size_t>(k) * 2 + static_cast<size_t>(k) * 4 +
+                           static_cast<size_t>(W) * 32 * 34 * 4;
+      if (smem4 <= 200 * 1024) {
+        const int per_sm = std::max(1, std::min(16, static_cast<int>((227 * 1024) / (smem4 + 1024))));
+        const int64_t blocks4 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
         const bool codes = o.codes != nullptr;
-#define FAQ_ROT3_CASE(L)                                                                                          \
-  case L: {                                                                                                       \
-    auto kern = codes ? hif4_rotate_v3_kernel<L, true> : hif4_rotate_v3_kernel<L, false>;                          \
-    FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem3)));  \
-    kern<<<static_cast<unsigned>(blocks3), warps3 * 32, smem3, stream>>>(                                                 \
-        static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                      \
-        static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o);                                   \
-    return launch_status("hif4_rotate_v3_kernel");                                                               \
+        const int wclass = W <= 4 ? 4 : W <= 8 ? 8 : W <= 12 ? 12 : 16;
+#define FAQ_ROT4_LAUNCH(L, MW)                                                                                     \
+  {                                                                                                                \
+    auto kern = codes ? hif4_rotate_v4_kernel<L, true, MW> : hif4_rotate_v4_kernel<L, false, MW>;                 \
+    FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem4)));   \
+    kern<<<static_cast<unsigned>(blocks4), W * 32, smem4, stream>>>(                                               \
+        static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                       \
+        static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o);                                    \
+    return launch_status("hif4_rotate_v4_kernel");                                                                \
   }
+#define FAQ_ROT4_CASE(L)                 \
+  case L:                                \
+    if (wclass == 4) FAQ_ROT4_LAUNCH(L, 4)   \
+    if (wclass == 8) FAQ_ROT4_LAUNCH(L, 8)   \
+    if (wclass == 12) FAQ_ROT4_LAUNCH(L, 12) \
+    FAQ_ROT4_LAUNCH(L, 16)
         switch (log2b) {
-          FAQ_ROT3_CASE(5)
-          FAQ_ROT3_CASE(6)
-          FAQ_ROT3_CASE(7)
-          FAQ_ROT3_CASE(8)
-          FAQ_ROT3_CASE(9)
-          FAQ_ROT3_CASE(10)
+          FAQ_ROT4_CASE(5)
+          FAQ_ROT4_CASE(6)
+          FAQ_ROT4_CASE(7)
+          FAQ_ROT4_CASE(8)
+          FAQ_ROT4_CASE(9)
+          FAQ_ROT4_CASE(10)
           default:
             break;
         }
-#undef FAQ_ROT3_CASE
+#undef FAQ_ROT4_CASE
+#undef FAQ_ROT4_LAUNCH
       }
     }
     const bool v2 = k % 64 == 0 && k <= 32768 && x_vec && (block >= 32 || k % 32 == 0) && block <= 1024;

@@ -94,6 +94,27 @@ def test_rotation_blocks_bit_exact(block: int, dtype: torch.dtype, kind: str) ->
         assert np.array_equal(_bits(qdq), _oracle_bits(expect, dtype)), (block, levels)
 
 
+@pytest.mark.parametrize("k,block", [(5120, 1024), (8192, 256), (12288, 1024), (16384, 512)])
+def test_rotation_wide_rows_bit_exact(k: int, block: int) -> None:
+    """The bf16 rotation kernel runs one warp per 1024 channels, so K = 5120 ... 16384
+    launch its wider CTA classes; 333 rows give every CTA (one per SM at the widest) two
+    or three rows, so both row buffers are refilled while other warps still work."""
+    ops = _ops()
+    rng = np.random.default_rng(k + block)
+    x = torch.from_numpy(rng.standard_normal((333, k)).astype(np.float32) * 2).to(torch.bfloat16)
+    x[:, rng.integers(0, k, 5)] *= 30
+    x[3, :100] = 0.0
+    signs = torch.from_numpy(rng.choice([-1, 1], k).astype(np.int8))
+    perm = torch.from_numpy(rng.permutation(k).astype(np.int64))
+    qdq, codes, meta = ops.hif4_quantize(x.to(DEV), levels="123", signs=signs.to(DEV), permutation=perm.to(DEV),
+                                         rot_block=block, want_codes=True)
+    rotated = olin.rotate_input(x.float().numpy(), signs.numpy(), perm.numpy(), block, "bf16")
+    assert np.array_equal(_bits(qdq), oh.f32_to_bf16_bits(oh.fake_quantize(rotated, "123")))
+    ocodes, ometa = oh.hif4_encode(rotated, "123")
+    assert np.array_equal(codes.cpu().numpy(), ocodes)
+    assert np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
+
+
 @pytest.mark.parametrize("block", [8, 16, 32, 64, 128, 256])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_signs_only_rotation_streaming_bit_exact(block: int, dtype: torch.dtype) -> None:
