@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_scores_kernel(const __grid_
     tma_prefetch_desc(&tmap_k);
   }
   __syncthreads();
+  allow_dependent_launch();  // pass 2 may start setting up on SMs this pass leaves
   auto load_k = [&](int64_t u, int stage) {  // thread 0: the tile as two 64-channel boxes
     const int tile = static_cast<int>(u % p.ntiles), bh = static_cast<int>(u / p.ntiles);
     const uint32_t bar = smem_addr(&bars[stage]);
@@ -289,6 +290,10 @@ __global__ void __launch_bounds__(THREADS, 2) decode_pv_kernel(const __grid_cons
   // rows p.rows .. prow - 1 of P and of the per-row scalars stay zero
   for (int i = p.rows * PS + tid; i < prow * PS; i += THREADS) s_p[i] = __float2bfloat16_rn(0.0f);
   for (int i = p.rows + tid; i < prow; i += THREADS) s_m[i] = s_alpha[i] = s_sum[i] = 0.0f;
+  // Everything above touches only shared memory and the V cache, which pass 1 does not
+  // write: it overlaps pass 1's last tiles. The scores and tile maxima are read below.
+  grid_dependency_wait();
+  allow_dependent_launch();
   // running max before the split (log2 domain): max over the earlier tiles' maxima
   for (int r = warp; r < p.rows; r += THREADS / 32) {
     float m = -INFINITY;
@@ -466,6 +471,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_pv_kernel(const __grid_cons
 // alphas multiply to, up to fp32 rounding order), out = O / denominator in bf16.
 __global__ void __launch_bounds__(4 * D) decode_combine_kernel(Params p) {
   __shared__ float s_o[4][D], s_l[4];
+  grid_dependency_wait();  // launched early, behind pass 2
   const int bh = blockIdx.x, r = blockIdx.y, dd = threadIdx.x % D, grp = threadIdx.x / D;
   const int b = bh / p.hkv, hk = bh % p.hkv;
   const int64_t base = static_cast<int64_t>(bh) * p.nsplits * p.rows;
@@ -566,9 +572,23 @@ static int decode_launch(dec::Params& p, float* ws, void* stream) {
   dec::decode_scores_kernel<<<grid1, dec::THREADS, s1, st>>>(tk, p);
   FAQ_CUDA(cudaFuncSetAttribute(dec::decode_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(s2)));
-  dec::decode_pv_kernel<<<dim3(p.nsplits, static_cast<unsigned>(bh)), dec::THREADS, s2, st>>>(tv, p);
-  dec::decode_combine_kernel<<<dim3(static_cast<unsigned>(bh), static_cast<unsigned>(p.rows)), 4 * dec::D, 0, st>>>(
-      p);
+  // passes 2 and 3 start while the kernel before them drains (programmatic dependent
+  // launch); each waits on the device before it reads that kernel's results
+  cudaLaunchAttribute early[1];
+  early[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  early[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.nsplits), static_cast<unsigned>(bh));
+  cfg.blockDim = dim3(dec::THREADS);
+  cfg.dynamicSmemBytes = s2;
+  cfg.stream = st;
+  cfg.attrs = early;
+  cfg.numAttrs = 1;
+  FAQ_CUDA(cudaLaunchKernelEx(&cfg, dec::decode_pv_kernel, tv, p));
+  cfg.gridDim = dim3(static_cast<unsigned>(bh), static_cast<unsigned>(p.rows));
+  cfg.blockDim = dim3(4 * dec::D);
+  cfg.dynamicSmemBytes = 0;
+  FAQ_CUDA(cudaLaunchKernelEx(&cfg, dec::decode_combine_kernel, p));
 
   return launch_status("hif4 decode kernels");
 }
