@@ -128,21 +128,11 @@ __device__ __forceinline__ float quantize_p64(float* f) {
   float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    int lv2 = 0, lv3a = 0, lv3b = 0;
-    if constexpr (LEVELS == 123) {
-      lv2 = __fmul_rn(m2[i], sc.rec) >= 4.0f;
-      const float thr = lv2 ? 4.0f : 2.0f;
-      lv3a = __fmul_rn(m3[2 * i], sc.rec) >= thr;
-      lv3b = __fmul_rn(m3[2 * i + 1], sc.rec) >= thr;
-    } else if constexpr (LEVELS == 12) {
-      lv2 = __fmul_rn(m2[i], sc.rec) >= 2.0f;
-    } else {
-      lv3a = __fmul_rn(m3[2 * i], sc.rec) >= 2.0f;
-      lv3b = __fmul_rn(m3[2 * i + 1], sc.rec) >= 2.0f;
-    }
+    uint32_t ea, eb;
+    hif4_level_shifts(__fmul_rn(m3[2 * i], sc.rec), __fmul_rn(m3[2 * i + 1], sc.rec), LEVELS, ea, eb);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int sh = lv2 + (h ? lv3b : lv3a);
+      const int sh = static_cast<int>((h ? eb : ea) >> 23);
       const float qm4 = __fmul_rn(sc.rec, pow2f(2 - sh));  // 4 * qm, exact
       const float ds4 = __fmul_rn(sc.s, pow2f(sh - 2));    // ds / 4, exact
       const float2 qm2 = make_float2(qm4, qm4), ds2 = make_float2(ds4, ds4);
@@ -178,6 +168,7 @@ __device__ __forceinline__ float exp_quantize_p64(float* f, float2 c2, float2 mn
   const Hif4Scale sc = hif4_scale(m1, LEVELS);
   // 4 qm = rec * 2^(2 - sh), ds / 4 = s * 2^(sh - 2) and -2^23 ds / 4 by exponent moves
   const uint32_t rec_q = __float_as_uint(sc.rec) + (2u << 23), s_d = __float_as_uint(sc.s) - (2u << 23);
+  const float2 rec2 = make_float2(sc.rec, sc.rec);
   float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float2 rp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -192,20 +183,9 @@ __device__ __forceinline__ float exp_quantize_p64(float* f, float2 c2, float2 mn
     }
     const float m3a = fmaxf(fmax3(e[0].x, e[0].y, e[1].x), e[1].y);
     const float m3b = fmaxf(fmax3(e[2].x, e[2].y, e[3].x), e[3].y);
-    const float m2 = fmaxf(m3a, m3b);
-    uint32_t lv2 = 0, lv3a = 0, lv3b = 0;
-    if constexpr (LEVELS == 123) {
-      lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;
-      const float thr = lv2 ? 4.0f : 2.0f;
-      lv3a = __fmul_rn(m3a, sc.rec) >= thr;
-      lv3b = __fmul_rn(m3b, sc.rec) >= thr;
-    } else if constexpr (LEVELS == 12) {
-      lv2 = __fmul_rn(m2, sc.rec) >= 2.0f;
-    } else {
-      lv3a = __fmul_rn(m3a, sc.rec) >= 2.0f;
-      lv3b = __fmul_rn(m3b, sc.rec) >= 2.0f;
-    }
-    const uint32_t ea = (lv2 + lv3a) << 23, eb = (lv2 + lv3b) << 23;
+    const float2 rab = __fmul2_rn(make_float2(m3a, m3b), rec2);
+    uint32_t ea, eb;
+    hif4_level_shifts(rab.x, rab.y, LEVELS, ea, eb);
     const float qa = __uint_as_float(rec_q - ea), qb = __uint_as_float(rec_q - eb);
     const float da = __uint_as_float(s_d + ea), db = __uint_as_float(s_d + eb);
     const float oa = __uint_as_float(s_d + ea + 0x8B800000u), ob = __uint_as_float(s_d + eb + 0x8B800000u);

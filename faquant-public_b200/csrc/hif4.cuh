@@ -56,6 +56,35 @@ __device__ __forceinline__ Hif4Scale hif4_scale(float max64, int levels) {
   return r;
 }
 
+// The lv2/lv3 shifts of one 8-value sub-block from the products of its two quarter
+// maxima with the reciprocal, ra = fl(m3a * rec) and rb = fl(m3b * rec). The comparisons
+// fl(m2 * rec) >= 4 (or 2) and fl(m3 * rec) >= thr of the three level variants are tests
+// of exponent fields -- x >= 2^k is one for a non-negative float, and fl(m2 * rec) =
+// max(ra, rb) because rounding is monotone -- and for 123, lv2 + [e(ra) >= 1 + lv2] =
+// max(e(ra), lv2) since e(ra) <= e(max(ra, rb)) <= 2. A NaN product counts as 0 (max(NaN,
+// 0) is 0 on the GPU), as it does in the comparisons, and every shift is clamped to its
+// range, so infinite or large products give the comparisons' answers. The equivalence
+// was checked against the comparisons for every exponent field with edge mantissas, zero,
+// infinities and NaNs, in each variant. Returns lv2 (0 or 1); ea and eb receive
+// (lv2 + lv3) << 23 of the two quarters.
+__device__ __forceinline__ uint32_t hif4_level_shifts(float ra, float rb, int levels, uint32_t& ea, uint32_t& eb) {
+  const int fa = static_cast<int>(__float_as_uint(fmaxf(ra, 0.0f)) & 0x7F800000u);
+  const int fb = static_cast<int>(__float_as_uint(fmaxf(rb, 0.0f)) & 0x7F800000u);
+  if (levels == 123) {
+    const int lv = min(max(max(fa, fb) - (128 << 23), 0), 1 << 23);
+    ea = static_cast<uint32_t>(min(max(fa - (127 << 23), lv), 2 << 23));
+    eb = static_cast<uint32_t>(min(max(fb - (127 << 23), lv), 2 << 23));
+    return static_cast<uint32_t>(lv) >> 23;
+  }
+  if (levels == 12) {
+    ea = eb = static_cast<uint32_t>(min(max(max(fa, fb) - (127 << 23), 0), 1 << 23));
+    return ea >> 23;
+  }
+  ea = static_cast<uint32_t>(min(max(fa - (127 << 23), 0), 1 << 23));
+  eb = static_cast<uint32_t>(min(max(fb - (127 << 23), 0), 1 << 23));
+  return 0;
+}
+
 // Element code from |x| and qm4 = 4 * qm (exact): min(floor(fl(fl(|x| * qm4) + 0.5)), 7).
 // fl(|x| * qm) * 4 == fl(|x| * 4qm) because scaling by 4 is exact, so one multiply
 // reproduces the reference's two. floor(t) of 0 <= t < 2^23 is taken on the FP32
@@ -85,18 +114,9 @@ __device__ __forceinline__ uint32_t hif4_quant8(const float (&v)[8], int levels,
   m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
   m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 4));
   const Hif4Scale sc = hif4_scale(m1, levels);
-  uint32_t lv2 = 0, lv3_0 = 0, lv3_1 = 0;
-  if (levels == 123) {
-    lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;
-    const float thr = lv2 ? 4.0f : 2.0f;  // max4*rec/2^lv2 >= 2, the division being exact
-    lv3_0 = __fmul_rn(m3_0, sc.rec) >= thr;
-    lv3_1 = __fmul_rn(m3_1, sc.rec) >= thr;
-  } else if (levels == 12) {
-    lv2 = __fmul_rn(m2, sc.rec) >= 2.0f;
-  } else {
-    lv3_0 = __fmul_rn(m3_0, sc.rec) >= 2.0f;
-    lv3_1 = __fmul_rn(m3_1, sc.rec) >= 2.0f;
-  }
+  uint32_t e0, e1;
+  const uint32_t lv2 = hif4_level_shifts(__fmul_rn(m3_0, sc.rec), __fmul_rn(m3_1, sc.rec), levels, e0, e1);
+  const uint32_t lv3_0 = (e0 >> 23) - lv2, lv3_1 = (e1 >> 23) - lv2;
   const float qm0 = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lv3_0)));  // 4 * qm
   const float qm1 = __fmul_rn(sc.rec, pow2f(2 - static_cast<int>(lv2 + lv3_1)));
   const float ds0 = __fmul_rn(sc.s, pow2f(static_cast<int>(lv2 + lv3_0)));
@@ -148,6 +168,8 @@ __device__ __forceinline__ uint4 hif4_quant8_bits(const uint32_t (&w)[4], int le
   m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 2));
   m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 4));
   const Hif4Scale sc = hif4_scale(m1, levels);
+  // the float comparisons here (not hif4_level_shifts): K4, the caller, sits at its
+  // 64-register budget, which the integer form's live values would exceed
   uint32_t lv2 = 0, lv3_0 = 0, lv3_1 = 0;
   if (levels == 123) {
     lv2 = __fmul_rn(m2, sc.rec) >= 4.0f;

@@ -761,22 +761,13 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
       __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        uint32_t lv2 = 0, la = 0, lb = 0;
-        if (levels == 123) {
-          lv2 = __fmul_rn(m2[s], sc.rec) >= 4.0f;
-          const float thr = lv2 ? 4.0f : 2.0f;
-          la = __fmul_rn(m3[2 * s], sc.rec) >= thr;
-          lb = __fmul_rn(m3[2 * s + 1], sc.rec) >= thr;
-        } else if (levels == 12) {
-          lv2 = __fmul_rn(m2[s], sc.rec) >= 2.0f;
-        } else {
-          la = __fmul_rn(m3[2 * s], sc.rec) >= 2.0f;
-          lb = __fmul_rn(m3[2 * s + 1], sc.rec) >= 2.0f;
-        }
+        const float2 rab = __fmul2_rn(make_float2(m3[2 * s], m3[2 * s + 1]), make_float2(sc.rec, sc.rec));
+        uint32_t ea, eb;  // (lv2 + lv3) << 23 of the two quarters
+        const uint32_t lv2 = hif4_level_shifts(rab.x, rab.y, levels, ea, eb);
+        const uint32_t la = (ea >> 23) - lv2, lb = (eb >> 23) - lv2;
         lvbits |= (lv2 << s) | (la << (4 + 2 * s)) | (lb << (5 + 2 * s));
         // 4 qm = rec * 2^(2 - sh) and ds / 4 = s * 2^(sh - 2) by moving the exponent field
         // (rec and s are normal and stay normal); off = -2^23 * ds / 4 likewise
-        const uint32_t ea = (lv2 + la) << 23, eb = (lv2 + lb) << 23;
         const float2 qm_a = make_float2(__uint_as_float(rec_q0 - ea), __uint_as_float(rec_q0 - ea));
         const float2 qm_b = make_float2(__uint_as_float(rec_q0 - eb), __uint_as_float(rec_q0 - eb));
         const float2 ds_a = make_float2(__uint_as_float(s_d0 + ea), __uint_as_float(s_d0 + ea));
