@@ -472,7 +472,7 @@ def main_arm(args) -> None:
         traffic = None
         tfile = ROOT / "profiles" / "traffic.json"
         if tfile.exists():
-            traffic = json.loads(tfile.read_text()).get("gemm_bf16_tn_kernel_bytes_per_launch")
+            traffic = json.loads(tfile.read_text()).get("gemm_bytes_per_launch")
         avg_gemm_ms = gemm_ms / n_gemm
         gemm_flops_per_launch = linear_flops() / len(PROJECTIONS)
         line = {
@@ -485,7 +485,7 @@ def main_arm(args) -> None:
                        "l2": "inputs larger than L2 (512 MB activations + 436 MB weights per step)"},
             "tokens_per_s": T_TOKENS * world / (ms_max * 1e-3),
             "roofline": {
-                "kernel": "gemm_bf16_tn_kernel", "bound": "tensor", "achieved": gemm_tflops,
+                "kernel": "gemm_bf16_tn_pair_kernel", "bound": "tensor", "achieved": gemm_tflops,
                 "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": gemm_tflops / pk["bf16_tflops"],
                 "peak_kind": f"{pk_kind} bf16 burst", "traffic": traffic,
                 "avg_launch_ms": avg_gemm_ms, "algorithmic_flops_per_launch_avg": gemm_flops_per_launch,
@@ -493,7 +493,7 @@ def main_arm(args) -> None:
                 "frac_of_fp8_dense_nominal": gemm_tflops / 4500.0,
                 "frac_of_fp4_dense_nominal": gemm_tflops / 9000.0,
             },
-            "quantize_kernel": {"kernel": "hif4_quantize_rotate_kernel", "bound": "hbm", "achieved": quant_gbs,
+            "quantize_kernel": {"kernel": "hif4_rotate_v4_kernel", "bound": "hbm", "achieved": quant_gbs,
                                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": quant_gbs / pk["hbm_gbs"],
                                 "ms_per_step": quant_ms / args.steps},
             "per_projection_ms": per_proj,

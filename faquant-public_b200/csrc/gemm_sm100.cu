@@ -17,6 +17,7 @@
 // The two accumulators (2 x 256 columns) let the epilogue of tile i overlap the
 // main loop of tile i+1. Every wait is bounded (common.cuh, mbar_wait).
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "tma.h"
@@ -207,10 +208,197 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+
+// ---------------------------------------------------------------- CTA-pair GEMM
+// The same GEMM on 256 x 256 output tiles, each computed by a cluster of two CTAs on the
+// two SMs of a TPC with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16). Each CTA
+// holds, per stage, its 128 rows of A and its 128 rows (output columns) of B -- 32 KB, so
+// six stages -- and its 128 output rows of the accumulator in its own tensor memory. One
+// MMA reads both CTAs' tiles, so each SM's shared memory supplies half of B instead of
+// all of it: the operand traffic per SM per K-step drops from 12 KB to 8 KB, which is
+// what bounds the one-CTA kernel.
+//   - producer (warp 0 of each CTA): waits for its stage's release, loads its A and B
+//     tiles by TMA; the bytes of both CTAs are counted on the leader's full barrier, which
+//     the leader's producer arms for 64 KB;
+//   - MMA (warp 1 of the leader): waits on full, issues 4 MMAs per stage, and releases the
+//     stage in both CTAs with one multicast commit; after a tile, a multicast commit marks
+//     the accumulator full in both CTAs;
+//   - epilogue (warps 2..5 of each CTA): its 128 rows from its own tensor memory, then an
+//     arrival on the leader's accumulator-empty barrier (8 arrivals: 4 warps x 2 CTAs).
+// Teardown: each producer waits until every stage it loaded was released (no multicast
+// arrival can reach an exited CTA), the leader's MMA warp waits until both CTAs'
+// epilogues released both accumulators, then the two MMA warps hand a token to each other
+// through mbarriers (bounded waits) before both deallocate the pair's tensor memory.
+constexpr int PB_M = 256, PB_N = 256;  // the pair's tile
+constexpr int PA_BYTES = 128 * BK * 2, PB_BYTES = 128 * BK * 2;
+constexpr int P_STAGE_BYTES = PA_BYTES + PB_BYTES;  // 32 KB per CTA
+constexpr int P_STAGES = 6;
+constexpr uint32_t P_IDESC = idesc_bf16_f32(PB_M, PB_N, false, false);
+constexpr size_t P_SMEM_BYTES = 1024 + P_STAGES * P_STAGE_BYTES + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_bf16_tn_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                             Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = base;
+  uint8_t* sB = base + P_STAGES * PA_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + P_STAGES * P_STAGE_BYTES);
+  uint64_t* full = bars;                          // [P_STAGES] (the leader's is used)
+  uint64_t* empty = bars + P_STAGES;              // [P_STAGES]
+  uint64_t* tfull = bars + 2 * P_STAGES;          // [NUM_ACC]
+  uint64_t* tempty = bars + 2 * P_STAGES + NUM_ACC;  // [NUM_ACC] (the leader's is used)
+  uint64_t* token = bars + 2 * P_STAGES + 2 * NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(token + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < NUM_ACC; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), 8);
+    }
+    mbar_init(smem_addr(token), 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_addr(tmem_slot), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before either CTA arrives on the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const uint32_t full_at_leader = mapa_shared(smem_addr(&full[0]), 0);
+  const uint32_t tempty_at_leader = mapa_shared(smem_addr(&tempty[0]), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+        int tm, tn;
+        tile_coords(p, tile, tm, tn);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait_site(smem_addr(&empty[stage]), phase ^ 1, 26, kb)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(smem_addr(&full[stage]), 2 * P_STAGE_BYTES);
+          const uint32_t bar = full_at_leader + 8 * stage;
+          tma_load_2d_pair(smem_addr(sA + stage * PA_BYTES), &tmap_a, bar, kb * BK, tm * PB_M + 128 * rank);
+          tma_load_2d_pair(smem_addr(sB + stage * PB_BYTES), &tmap_b, bar, kb * BK, tn * PB_N + 128 * rank);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // every stage this CTA loaded has been released by the pair's MMAs
+      for (int s = 0; s < P_STAGES; ++s) {
+        if (!mbar_wait_site(smem_addr(&empty[stage]), phase ^ 1, 27, s)) break;
+        if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    int it = 0;
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs, ++it) {
+        const int acc = it & 1;
+        if (!mbar_wait_site(smem_addr(&tempty[acc]), ((it >> 1) & 1) ^ 1, 28, it)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * PB_N;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait_site(smem_addr(&full[stage]), phase, 29, kb)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sA + stage * PA_BYTES), b0 = smem_addr(sB + stage * PB_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc_mma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), P_IDESC,
+                            (kb | kk) != 0);
+          tc_commit_pair(smem_addr(&empty[stage]), 0x3);
+          if (++stage == P_STAGES) { stage = 0; phase ^= 1; }
+        }
+        tc_commit_pair(smem_addr(&tfull[acc]), 0x3);
+      }
+      // both CTAs' epilogues have released both accumulators (the last uses of each)
+      for (int a = 0; a < NUM_ACC && it > a; ++a) {
+        const int last = it - 1 - ((it - 1 - a) & 1);  // the last tile that used accumulator (it - 1 - a) & 1
+        mbar_wait_site(smem_addr(&tempty[last & 1]), (last >> 1) & 1, 30, last);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += pairs, ++it) {
+      const int acc = it & 1;
+      if (!mbar_wait_warp(smem_addr(&tfull[acc]), (it >> 1) & 1, 31, it)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(p, tile, tm, tn);
+      const int row = tm * PB_M + 128 * static_cast<int>(rank) + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PB_N;
+#pragma unroll 1
+      for (int c = 0; c < PB_N; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c, r);
+        tc_wait_ld();
+        reg_fence32(r);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        store_row32(p, row, tn * PB_N + c, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_at_leader + 8 * acc);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    // the peer tells the leader it is done, the leader answers: after this neither CTA's
+    // tensor memory or shared memory is used by the other
+    if (lane == 0) {
+      if (!leader) {
+        mbar_arrive_cluster(mapa_shared(smem_addr(token), 0));
+        mbar_wait_site(smem_addr(token), 0, 32, 0);
+      } else {
+        mbar_wait_site(smem_addr(token), 0, 32, 0);
+        mbar_arrive_cluster(mapa_shared(smem_addr(token), 1));
+      }
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 }  // namespace gemm
 }  // namespace faq
 
 using namespace faq;
+
+namespace faq {
+namespace gemm {
+// FAQ_GEMM_ONE_SM=1 in the environment keeps every GEMM on the one-CTA kernel
+static bool one_sm_forced() {
+  static const bool forced = [] {
+    const char* e = std::getenv("FAQ_GEMM_ONE_SM");
+    return e != nullptr && e[0] == '1';
+  }();
+  return forced;
+}
+}  // namespace gemm
+}  // namespace faq
 
 extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
                                 int64_t k, const void* bias, void* y, int64_t ldy, void* stream) {
@@ -243,16 +431,34 @@ extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64
   p.m = static_cast<int>(m);
   p.n = static_cast<int>(n);
   p.k = static_cast<int>(k);
-  p.tiles_m = static_cast<int>((m + BM - 1) / BM);
-  p.tiles_n = static_cast<int>((n + BN - 1) / BN);
-  // about sqrt(148 * B panel / A panel) = sqrt(148 * 2) ~ 17 M tiles per group minimizes
-  // the panels a wave reads (G A panels + 148 / G B panels, B panels twice as large)
-  p.group_m = std::max(1, std::min(p.tiles_m, 16));
   p.kblocks = static_cast<int>((k + BK - 1) / BK);
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ldy = ldy;
   p.y_vec = aligned16(y) && ldy % 8 == 0;
+  if (m >= PB_M && n >= PB_N && !one_sm_forced()) {
+    // CTA pairs on 256 x 256 tiles: A as 128-row boxes (each CTA its half), B likewise
+    CUtensorMap tb2;
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {BK, 128};
+    int rc = make_tmap(&tb2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, b, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != FAQ_OK) return rc;
+    p.tiles_m = static_cast<int>((m + PB_M - 1) / PB_M);
+    p.tiles_n = static_cast<int>((n + PB_N - 1) / PB_N);
+    p.group_m = std::max(1, std::min(p.tiles_m, 8));  // 8 pair rows = 2048 rows of A per group
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int grid = 2 * std::max(1, std::min(tiles, num_sms() / 2));
+    FAQ_CUDA(cudaFuncSetAttribute(gemm_bf16_tn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(P_SMEM_BYTES)));
+    gemm_bf16_tn_pair_kernel<<<grid, THREADS, P_SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb2, p);
+    return launch_status("gemm_bf16_tn_pair_kernel");
+  }
+  p.tiles_m = static_cast<int>((m + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((n + BN - 1) / BN);
+  // about sqrt(148 * B panel / A panel) = sqrt(148 * 2) ~ 17 M tiles per group minimizes
+  // the panels a wave reads (G A panels + 148 / G B panels, B panels twice as large)
+  p.group_m = std::max(1, std::min(p.tiles_m, 16));
   const int tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(tiles, num_sms());
   FAQ_CUDA(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -114,7 +114,9 @@ int faq_hif4_pack_weight(const void* w, int w_dtype, int64_t n, int64_t k, int64
  * fp32 accumulation on tcgen05 tensor cores (TMEM accumulators, TMA loads).
  * Replaces F.linear(x_qdq, weight, bias) (quantization.py:277, wan22_hif4.py:88)
  * on exactly-dequantized HiF4 operands. Needs lda, ldb multiples of 8, 16-byte
- * aligned a/b and k a multiple of 8.
+ * aligned a/b and k a multiple of 8. Shapes with m >= 256 and n >= 256 run on clusters
+ * of two CTAs (tcgen05.mma.cta_group::2, 256 x 256 tiles), smaller ones on one CTA per
+ * SM; both give the same bits (FAQ_GEMM_ONE_SM=1 in the environment keeps the latter).
  */
 int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
                      int64_t n, int64_t k, const void* bias, void* y, int64_t ldy, void* stream);

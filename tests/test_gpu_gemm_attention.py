@@ -54,6 +54,47 @@ def test_gemm_matches_fp64(m: int, n: int, k: int, bias: bool) -> None:
     assert bool((err <= bound).all()), float((err - bound).max())
 
 
+_ONE_CTA_CHILD = """
+import sys
+import torch
+sys.path[:0] = sys.argv[2:4]
+from faquant_b200 import ops
+cases = torch.load(sys.argv[1])
+torch.save([ops.gemm_bf16(a.cuda(), b.cuda(), None if c is None else c.cuda()).cpu() for a, b, c in cases],
+           sys.argv[1] + ".out")
+"""
+
+
+def test_gemm_cta_pairs_equal_one_cta(tmp_path) -> None:
+    """Shapes with a full 256 x 256 tile run on CTA pairs (tcgen05.mma.cta_group::2, each
+    CTA holding half of A and half of B); FAQ_GEMM_ONE_SM=1 keeps the one-CTA kernel.
+    Both sum the same products in the same K order: the same bits, ragged tiles, K tails
+    and bias included."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    ops = _ops()
+    shapes = [(300, 520, 200, True), (257, 257, 72, False), (1000, 1000, 1024, True), (2048, 4096, 4096, False),
+              (8192, 1024, 4096, False), (512, 768, 8, True)]
+    cases, ours = [], []
+    for i, (m, n, k, bias) in enumerate(shapes):
+        a = _hif4_operand(m, k, 10 + i)
+        b = _hif4_operand(n, k, 20 + i, 0.02)
+        c = (torch.randn(n, generator=torch.Generator().manual_seed(i)) * 0.1).to(torch.bfloat16) if bias else None
+        cases.append((a, b, c))
+        ours.append(ops.gemm_bf16(a.to(DEV), b.to(DEV), None if c is None else c.to(DEV)).cpu())
+    path = tmp_path / "gemm_cases.pt"
+    torch.save(cases, path)
+    root = Path(__file__).resolve().parents[1]
+    subprocess.run([sys.executable, "-c", _ONE_CTA_CHILD, str(path), str(root / "faquant-public_b200"), str(root)],
+                   check=True, env=dict(os.environ, FAQ_GEMM_ONE_SM="1"), timeout=600)
+    theirs = torch.load(str(path) + ".out")
+    for (m, n, k, _), a, b in zip(shapes, ours, theirs):
+        assert torch.equal(a, b), (m, n, k)
+
+
 def test_gemm_strided_and_tail_k() -> None:
     ops = _ops()
     a_full = _hif4_operand(200, 136, 4).to(DEV)
