@@ -79,10 +79,19 @@ def attention_forward(
     if past_key_values is not None:
         cache_kwargs = {"sin": sin, "cos": cos, "cache_position": cache_position}
         key_states, value_states = past_key_values.update(key_states, value_states, self.layer_idx, cache_kwargs)
-    if getattr(self, "faquant_attention_kernel", "simulated") != "simulated":
-        raise NotImplementedError("faquant_b200 replaces the 'simulated' attention kernel only")
-    kwargs["cache_position"] = cache_position
-    attn_output, attn_weights = simulated_flash_attention_forward(
+    kernel = getattr(self, "faquant_attention_kernel", "simulated")
+    if kernel == "simulated":  # the HiF4 attention of this package
+        kwargs["cache_position"] = cache_position
+        interface = simulated_flash_attention_forward
+    elif kernel == "native":  # the model's own attention on the transformed Q/K (qwen3.py:147-152)
+        from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+        from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+
+        impl = self.config._attn_implementation
+        interface = eager_attention_forward if impl == "eager" else ALL_ATTENTION_FUNCTIONS[impl]
+    else:
+        raise NotImplementedError("the differentiable (training) attention kernel is not part of faquant_b200")
+    attn_output, attn_weights = interface(
         self, query_states, key_states, value_states, attention_mask, dropout=0.0, scaling=self.scaling,
         sliding_window=getattr(self, "sliding_window", None), **kwargs)
     attn_output = attn_output.reshape(*input_shape, -1).contiguous()
