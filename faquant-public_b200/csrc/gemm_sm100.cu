@@ -40,9 +40,12 @@ struct Params {
   int tiles_m, tiles_n, kblocks;
   int group_m;  // M tiles per group of the L2-friendly tile order
   const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;  // [m, ldr] added to the bf16 product, or null
+  int64_t ldr;
   __nv_bfloat16* y;
   int64_t ldy;
   bool y_vec;
+  bool r_vec;
 };
 
 // Tile order: groups of group_m M-tiles; inside a group the M tile varies fastest and
@@ -58,6 +61,10 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& tm, 
   tn = in_group / rows;
 }
 
+// Output values of a 32-column run of one row: fl(acc + bias), and with a residual
+// fl(bf16(fl(acc + bias)) + residual) -- the bf16 product first rounded, then the bf16 add
+// of eager `residual + linear(x)`, so the fused epilogue gives the same bits as the two
+// separate steps.
 __device__ __forceinline__ void store_row32(const Params& p, int row, int col, const float (&v)[32]) {
   if (row >= p.m || col >= p.n) return;
   float r[32];
@@ -66,6 +73,24 @@ __device__ __forceinline__ void store_row32(const Params& p, int row, int col, c
     float b = 0.0f;
     if (p.bias != nullptr && col + i < p.n) b = __bfloat162float(p.bias[col + i]);
     r[i] = v[i] + b;
+  }
+  if (p.residual != nullptr) {
+    const __nv_bfloat16* res = p.residual + static_cast<int64_t>(row) * p.ldr + col;
+    if (p.r_vec && col + 32 <= p.n) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = reinterpret_cast<const uint4*>(res)[j];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int i = 8 * j + 2 * h;
+          r[i] = bf16_round(r[i]) + __uint_as_float(ws[h] << 16);
+          r[i + 1] = bf16_round(r[i + 1]) + __uint_as_float(ws[h] & 0xFFFF0000u);
+        }
+      }
+    } else {
+      for (int i = 0; i < 32 && col + i < p.n; ++i) r[i] = bf16_round(r[i]) + __bfloat162float(res[i]);
+    }
   }
   __nv_bfloat16* dst = p.y + static_cast<int64_t>(row) * p.ldy + col;
   if (p.y_vec && col + 32 <= p.n) {
@@ -400,9 +425,11 @@ static bool one_sm_forced() {
 }  // namespace gemm
 }  // namespace faq
 
-extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
-                                int64_t k, const void* bias, void* y, int64_t ldy, void* stream) {
+extern "C" int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
+                                         int64_t n, int64_t k, const void* bias, const void* residual, int64_t ldr,
+                                         void* y, int64_t ldy, void* stream) {
   FAQ_CHECK_ARG(a && b && y, "null pointer");
+  FAQ_CHECK_ARG(residual == nullptr || ldr >= n, "residual leading dimension too small");
   FAQ_CHECK_ARG(m >= 0 && n >= 0 && k > 0, "bad shape");
   FAQ_CHECK_ARG(m < (int64_t(1) << 31) && n < (int64_t(1) << 31) && k < (int64_t(1) << 31), "shape too large");
   FAQ_CHECK_ARG(lda >= k && ldb >= k && ldy >= n, "leading dimension too small");
@@ -433,6 +460,9 @@ extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64
   p.k = static_cast<int>(k);
   p.kblocks = static_cast<int>((k + BK - 1) / BK);
   p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.ldr = ldr;
+  p.r_vec = residual != nullptr && aligned16(residual) && ldr % 8 == 0;
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ldy = ldy;
   p.y_vec = aligned16(y) && ldy % 8 == 0;
@@ -465,4 +495,9 @@ extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64
                                 static_cast<int>(SMEM_BYTES)));
   gemm_bf16_tn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return launch_status("gemm_bf16_tn_kernel");
+}
+
+extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                                int64_t k, const void* bias, void* y, int64_t ldy, void* stream) {
+  return faq_gemm_bf16_tn_residual(a, lda, b, ldb, m, n, k, bias, nullptr, 0, y, ldy, stream);
 }

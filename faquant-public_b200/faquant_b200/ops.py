@@ -166,9 +166,11 @@ def hif4_pack_weight(
 
 
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None,
-              out: torch.Tensor | None = None) -> torch.Tensor:
-    """``a [m, k] @ b [n, k]^T (+ bias)`` in bf16 with fp32 accumulation (tcgen05)."""
-    device = _require_cuda(a, b, bias)
+              out: torch.Tensor | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """``a [m, k] @ b [n, k]^T (+ bias)`` in bf16 with fp32 accumulation (tcgen05); with
+    ``residual [m, n]`` (bf16) the result is ``residual + that`` with the eager bf16 add's
+    rounding (the product rounded to bf16 first), added in the GEMM's epilogue."""
+    device = _require_cuda(a, b, bias, residual)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
         raise TypeError("gemm_bf16 takes bfloat16 operands")
     if a.stride(-1) != 1:
@@ -191,7 +193,16 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
         bias = bias.to(device=device, dtype=torch.bfloat16).contiguous()
     if out is None:
         out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
-    _lib.call("faq_gemm_bf16_tn", a.data_ptr(), lda, b.data_ptr(), ldb, m, n, k, _ptr(bias), out.data_ptr(),
+    if residual is None:
+        _lib.call("faq_gemm_bf16_tn", a.data_ptr(), lda, b.data_ptr(), ldb, m, n, k, _ptr(bias), out.data_ptr(),
+                  out.stride(0) if m > 1 else n, _stream(device))
+        return out
+    if residual.dtype != torch.bfloat16 or residual.shape != (m, n):
+        raise ValueError("residual must be bfloat16 [m, n]")
+    if residual.stride(-1) != 1:
+        residual = residual.contiguous()
+    _lib.call("faq_gemm_bf16_tn_residual", a.data_ptr(), lda, b.data_ptr(), ldb, m, n, k, _ptr(bias),
+              residual.data_ptr(), residual.stride(0) if m > 1 else n, out.data_ptr(),
               out.stride(0) if m > 1 else n, _stream(device))
     return out
 

@@ -143,11 +143,19 @@ class TPHiF4Linear(nn.Module):
     overlap_chunks = 4
     overlap_min_rows = 4096
 
-    def forward(self, x: torch.Tensor, *, quantized: bool = False) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, *, quantized: bool = False, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """``residual + linear(x)`` when ``residual`` is given: on one rank the add is in
+        the GEMM epilogue (the same bits as the separate bf16 add); row-parallel ranks add
+        after the all-reduce."""
         xq = x if quantized else self.quantize_input(x)
         tp = self.reduce
         if tp is None or tp.world == 1:
-            return ops.gemm_bf16(xq, self.weight, self.bias)
+            return ops.gemm_bf16(xq, self.weight, self.bias, residual=residual)
+        y = self._row_parallel(xq)
+        return y if residual is None else residual + y
+
+    def _row_parallel(self, xq: torch.Tensor) -> torch.Tensor:
+        tp = self.reduce
         rows = xq.shape[0]
         if rows < self.overlap_min_rows:
             return tp.all_reduce_(ops.gemm_bf16(xq, self.weight, self.bias))
@@ -271,6 +279,9 @@ class Qwen3TPPrefill(nn.Module):
         super().__init__()
         self.cfg, self.tp, self.device = cfg, tp, device
         self.trace = None
+        # the residual adds in the o_proj / down_proj GEMM epilogues (off while a trace hook
+        # needs the projections' own outputs)
+        self.fuse_residual = True
         d = cfg.head_dim
         sl = qwen3_shard_slices(cfg, tp)
         hq, hkv = cfg.heads // tp.world, cfg.kv_heads // tp.world
@@ -319,7 +330,7 @@ class Qwen3TPPrefill(nn.Module):
         return t
 
     def _attention(self, layer: _Qwen3Layer, h: torch.Tensor, batch: int, seq: int, cos, sin,
-                   index: int = 0) -> torch.Tensor:
+                   index: int = 0, residual: torch.Tensor | None = None) -> torch.Tensor:
         cfg, d = self.cfg, self.cfg.head_dim
         qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
         nq, nk = layer.heads * d, layer.kv_heads * d
@@ -334,7 +345,7 @@ class Qwen3TPPrefill(nn.Module):
         vd = self._t("vd", index, ops.qk_prep(v, levels=cfg.levels, rotate=False)[0])
         out = ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=True, p_levels=cfg.levels,
                                  quantized_normalizer=True)  # [B, S, hq, d]
-        return self._t("o", index, layer.o(self._t("attention", index, out).view(batch * seq, nq)))
+        return self._t("o", index, layer.o(self._t("attention", index, out).view(batch * seq, nq), residual=residual))
 
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -342,14 +353,18 @@ class Qwen3TPPrefill(nn.Module):
         batch, seq = input_ids.shape
         cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
         x = torch.nn.functional.embedding(input_ids.reshape(-1), self.embed)  # [T, hidden]
+        fuse = self.fuse_residual and self.trace is None
         for i, layer in enumerate(self.layers):
-            x = x + self._attention(layer, ops.rms_norm(self._t("x", i, x), layer.input_norm, cfg.eps), batch, seq,
-                                    cos, sin, i)
+            h = ops.rms_norm(self._t("x", i, x), layer.input_norm, cfg.eps)
+            if fuse:
+                x = self._attention(layer, h, batch, seq, cos, sin, i, residual=x)
+            else:
+                x = x + self._attention(layer, h, batch, seq, cos, sin, i)
             x = self._t("x_mid", i, x)
             gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, ops.rms_norm(x, layer.post_norm,
                                                                                          cfg.eps))))
             a = self._t("act", i, ops.silu_mul(gu))
-            x = x + self._t("down", i, layer.down(a))
+            x = layer.down(a, residual=x) if fuse else x + self._t("down", i, layer.down(a))
         last = self._t("final", len(self.layers), x.view(batch, seq, -1)[:, -1])
         return torch.nn.functional.linear(rms_norm(last, self.final_norm, cfg.eps), self.lm_head).float()
 
@@ -445,6 +460,7 @@ class WanBlockTP(nn.Module):
         super().__init__()
         self.cfg, self.tp, self.device = cfg, tp, device
         self.trace = None  # trace(stage, 0, tensor) at each stage boundary, as in Qwen3TPPrefill
+        self.fuse_residual = True
         if cfg.heads % tp.world:
             raise ValueError("heads must divide by the TP size")
         d = cfg.head_dim
@@ -499,8 +515,9 @@ class WanBlockTP(nn.Module):
         vd = tr("vd", ops.qk_prep(heads(2 * n), levels=cfg.levels, rotate=False)[0])
         att = tr("attention", ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=False, p_levels=cfg.levels,
                                                  quantized_normalizer=True))  # [1, L, hl, d]
-        x = tr("x_mid", x + tr("o", self.o(att.view(seq, n))))
+        fuse = self.fuse_residual and self.trace is None  # residual adds in the o / ffn.2 epilogues
+        x = tr("x_mid", self.o(att.view(seq, n), residual=x) if fuse else x + tr("o", self.o(att.view(seq, n))))
         h = tr("norm2", ops.layer_norm(x, cfg.eps))
         f0 = tr("ffn0", self.ffn0(h))
         a = tr("act", ops.gelu_tanh(f0))
-        return x + tr("ffn2", self.ffn2(a))
+        return self.ffn2(a, residual=x) if fuse else x + tr("ffn2", self.ffn2(a))

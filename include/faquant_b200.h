@@ -120,6 +120,17 @@ int faq_hif4_pack_weight(const void* w, int w_dtype, int64_t n, int64_t k, int64
  */
 int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
                      int64_t n, int64_t k, const void* bias, void* y, int64_t ldy, void* stream);
+/*
+ * faq_gemm_bf16_tn with the residual add of a decoder layer in the epilogue:
+ * y = bf16(bf16(a . b^T + bias) + residual), residual [m, n] bf16 with leading dimension
+ * ldr -- the same bits as the GEMM followed by the eager bf16 add
+ * `hidden = residual + o_proj(x)` of Qwen3DecoderLayer (and Wan's x + attn / x + ffn).
+ * residual may be null (then it is faq_gemm_bf16_tn). No counterpart in the reference,
+ * which adds in a separate elementwise pass.
+ */
+int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
+                              int64_t n, int64_t k, const void* bias, const void* residual, int64_t ldr,
+                              void* y, int64_t ldy, void* stream);
 
 /*
  * K4 -- attention operand preparation for one of Q, K or V.

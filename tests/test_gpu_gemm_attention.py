@@ -95,6 +95,20 @@ def test_gemm_cta_pairs_equal_one_cta(tmp_path) -> None:
         assert torch.equal(a, b), (m, n, k)
 
 
+@pytest.mark.parametrize("m,n,k", [(300, 520, 200), (1000, 1000, 1024), (33, 48, 64), (2048, 4096, 512)])
+def test_gemm_residual_epilogue_is_the_separate_bf16_add(m: int, n: int, k: int) -> None:
+    """y = bf16(bf16(a b^T + bias) + residual): the same bits as the GEMM followed by the
+    eager bf16 add, on both GEMM kernels' shapes, ragged tiles and a strided residual."""
+    ops = _ops()
+    a = _hif4_operand(m, k, 30).to(DEV)
+    b = _hif4_operand(n, k, 31, 0.02).to(DEV)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(32)) * 0.1).to(torch.bfloat16).to(DEV)
+    wide = (torch.randn(m, n + 24, generator=torch.Generator().manual_seed(33)) * 3).to(torch.bfloat16).to(DEV)
+    for residual in (wide[:, :n].contiguous(), wide[:, :n]):  # contiguous and strided (ldr = n + 24)
+        fused = ops.gemm_bf16(a, b, bias, residual=residual)
+        assert torch.equal(fused, residual + ops.gemm_bf16(a, b, bias))
+
+
 def test_gemm_strided_and_tail_k() -> None:
     ops = _ops()
     a_full = _hif4_operand(200, 136, 4).to(DEV)

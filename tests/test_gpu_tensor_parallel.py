@@ -173,6 +173,24 @@ def test_qwen3_prefill_stages_match_the_oracle() -> None:
     assert logits.shape == (2, cfg.vocab) and _rel(logits, ref.float().numpy()) <= 1e-2
 
 
+def test_residual_adds_in_the_gemm_epilogue_are_the_same_bits() -> None:
+    """The o_proj / down_proj (Wan: o / ffn.2) residual adds run in the GEMM epilogue unless
+    a trace hook needs the projections' own outputs; the fused forwards give the same bits
+    as the separate bf16 adds."""
+    from faquant_b200.tensor_parallel import Qwen3TPPrefill, TPGroup, WanBlockTP, default_input_ids
+
+    model = Qwen3TPPrefill(_qwen_cfg(), TPGroup(), DEV)
+    ids = default_input_ids(2, 192, model.cfg.vocab, DEV, seed=4)
+    fused = model(ids)
+    model.fuse_residual = False
+    assert torch.equal(fused, model(ids))
+    block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
+    x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
+    fused = block(x)
+    block.fuse_residual = False
+    assert torch.equal(fused, block(x))
+
+
 def test_wan_block_stages_match_the_oracle() -> None:
     """Every stage of a Wan2.2 block at TP 1 against the reference's torch glue and the
     oracle: the LayerNorms, the W4A4 projections, the fused q/k RMSNorm over all heads +
