@@ -79,6 +79,20 @@ __device__ __forceinline__ float bf16_round(float x) {
 // fp32 value already exactly representable in bf16 -> its bf16 bits
 __device__ __forceinline__ uint32_t exact_bf16_bits(float x) { return __float_as_uint(x) >> 16; }
 
+// ---------------------------------------------------------------- activations (bf16 results)
+// SwiGLU of Qwen3MLP: bf16(bf16(silu(g)) * u), silu(g) = g / (1 + exp(-g)) in fp32.
+__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+  const float s = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+  return bf16_round(__fmul_rn(s, u));
+}
+// The DiT FFN's tanh GELU in fp32, rounded once: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh_bf16(float x) {
+  const float beta = 0.7978845608028654f;  // sqrt(2 / pi)
+  const float cube = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(beta, __fadd_rn(x, __fmul_rn(0.044715f, cube)));
+  return bf16_round(__fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner))));
+}
+
 __device__ __forceinline__ float pow2f(int e) {  // 2^e for -126 <= e <= 127
   return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
 }

@@ -86,10 +86,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
     unpack8(*reinterpret_cast<const uint4*>(gu + row * ld + col), g);
     unpack8(*reinterpret_cast<const uint4*>(gu + row * ld + f + col), u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float s = bf16_round(__fdiv_rn(g[j], __fadd_rn(1.0f, expf(-g[j]))));
-      y[j] = bf16_round(__fmul_rn(s, u[j]));
-    }
+    for (int j = 0; j < 8; ++j) y[j] = swiglu_bf16(g[j], u[j]);
     *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
   }
 }
@@ -160,18 +157,13 @@ __global__ void __launch_bounds__(256) gelu_tanh_kernel(const __nv_bfloat16* __r
                                                         int64_t cols, int64_t ld, __nv_bfloat16* __restrict__ out,
                                                         int64_t ldo) {
   const int64_t per_row = cols / 8, total = rows * per_row;
-  const float beta = 0.7978845608028654f;  // sqrt(2 / pi)
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t row = i / per_row, col = (i % per_row) * 8;
     float v[8], y[8];
     unpack8(*reinterpret_cast<const uint4*>(x + row * ld + col), v);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float cube = __fmul_rn(__fmul_rn(v[j], v[j]), v[j]);
-      const float inner = __fmul_rn(beta, __fadd_rn(v[j], __fmul_rn(0.044715f, cube)));
-      y[j] = bf16_round(__fmul_rn(__fmul_rn(0.5f, v[j]), __fadd_rn(1.0f, tanhf(inner))));
-    }
+    for (int j = 0; j < 8; ++j) y[j] = gelu_tanh_bf16(v[j]);
     *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
   }
 }

@@ -157,11 +157,12 @@ __global__ void __launch_bounds__(256) hif4_quantize_direct_kernel(const T* __re
 // channels, so no row needs staging: it streams like the direct kernel. A thread holds
 // 8 consecutive channels; the B/8 lanes of a block are consecutive lanes of one warp
 // (k is a multiple of max(64, B), so blocks never straddle a warp or a row). Element
-// pipeline as in the staged kernel below: input_scale rounded to x's dtype, the sign as
+// pipeline as in the staged kernel below (after the activation of ACT, if any, on the
+// loaded values -- faq_hif4_quantize_act): input_scale rounded to x's dtype, the sign as
 // an exact fp32 negation, butterflies in the reference's stage order (strides 1, 2, 4
 // inside the thread, 8 .. B/2 across lanes), the normalization, one rounding to x's
 // dtype, then HiF4 on the 8-lane 64-blocks.
-template <typename T, int LOG2B>
+template <typename T, int LOG2B, int ACT = 0>
 __global__ void __launch_bounds__(256) hif4_rotate_signs_kernel(const T* __restrict__ x, int64_t rows, int64_t k,
                                                                 int64_t ldx, const T* __restrict__ input_scale,
                                                                 const int8_t* __restrict__ signs, int levels,
@@ -179,7 +180,19 @@ __global__ void __launch_bounds__(256) hif4_rotate_signs_kernel(const T* __restr
     const int64_t c = live ? idx % chunks_per_row : 0;
     const int64_t col = c * 8;
     float v[8];
-    load8<T>(x + row * ldx + col, v, true, live ? 8 : 0);
+    if constexpr (ACT == FAQ_ACT_SWIGLU) {  // x is [rows, 2k]: gate | up, the product is bf16
+      float u[8];
+      load8<T>(x + row * ldx + col, v, true, live ? 8 : 0);
+      load8<T>(x + row * ldx + k + col, u, true, live ? 8 : 0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = swiglu_bf16(v[i], u[i]);
+    } else {
+      load8<T>(x + row * ldx + col, v, true, live ? 8 : 0);
+      if constexpr (ACT == FAQ_ACT_GELU_TANH) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = gelu_tanh_bf16(v[i]);
+      }
+    }
     if (input_scale != nullptr) {
       float sc[8];
       load8<T>(input_scale + col, sc, true, live ? 8 : 0);
@@ -1100,6 +1113,57 @@ extern "C" int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64
   if (x_dtype == FAQ_BF16)
     return launch_quantize<__nv_bfloat16>(x, rows, k, ldx, input_scale, signs, perm, rot_block, levels, o, s);
   return launch_quantize<float>(x, rows, k, ldx, input_scale, signs, perm, rot_block, levels, o, s);
+}
+
+extern "C" int faq_hif4_quantize_act(const void* x, int act, int64_t rows, int64_t k, int64_t ldx,
+                                     const void* input_scale, const int8_t* signs, int rot_block, int levels,
+                                     uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
+  FAQ_CHECK_ARG(act == FAQ_ACT_SWIGLU || act == FAQ_ACT_GELU_TANH, "act must be FAQ_ACT_SWIGLU or FAQ_ACT_GELU_TANH");
+  FAQ_CHECK_ARG(rows >= 0 && k > 0 && k % 64 == 0, "need rows >= 0 and k a positive multiple of 64");
+  FAQ_CHECK_ARG(x != nullptr || rows == 0, "x is null");
+  FAQ_CHECK_ARG(ldx >= (act == FAQ_ACT_SWIGLU ? 2 * k : k), "ldx too small for the activation's input");
+  FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
+  FAQ_CHECK_ARG(codes || meta || qdq || rows == 0, "all outputs are null");
+  FAQ_CHECK_ARG(qdq == nullptr || ldq >= k, "ldq < k");
+  FAQ_CHECK_ARG(!codes || (reinterpret_cast<uintptr_t>(codes) & 3) == 0, "codes must be 4-byte aligned");
+  FAQ_CHECK_ARG(!meta || (reinterpret_cast<uintptr_t>(meta) & 3) == 0, "meta must be 4-byte aligned");
+  FAQ_CHECK_ARG(signs != nullptr && (reinterpret_cast<uintptr_t>(signs) & 7) == 0,
+                "the fused activation path needs 8-byte aligned signs (a signs-only rotation)");
+  FAQ_CHECK_ARG(rot_block >= 8 && rot_block <= 256 && (rot_block & (rot_block - 1)) == 0 && k % rot_block == 0,
+                "rot_block must be a power of two in 8..256 dividing k");
+  FAQ_CHECK_ARG((x == nullptr || aligned16(x)) && ldx % 8 == 0 && (input_scale == nullptr || aligned16(input_scale)),
+                "x must be 16-byte aligned with ldx a multiple of 8");
+  QuantOut o{codes, meta, qdq, ldq, false};
+  o.qdq_vec = qdq && aligned16(qdq) && ldq % 8 == 0;
+  FAQ_CHECK_ARG(qdq == nullptr || o.qdq_vec, "qdq must be 16-byte aligned with ldq a multiple of 8");
+  if (rows == 0) return FAQ_OK;
+  int log2b = 0;
+  while ((1 << log2b) < rot_block) ++log2b;
+  const int64_t blocks = std::min<int64_t>((rows * (k / 8) + 255) / 256, static_cast<int64_t>(num_sms()) * 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* sc = static_cast<const __nv_bfloat16*>(input_scale);
+#define FAQ_ACT_CASE(L)                                                                                              \
+  case L:                                                                                                            \
+    if (act == FAQ_ACT_SWIGLU)                                                                                       \
+      hif4_rotate_signs_kernel<__nv_bfloat16, L, FAQ_ACT_SWIGLU>                                                     \
+          <<<static_cast<unsigned>(blocks), 256, 0, st>>>(xb, rows, k, ldx, sc, signs, levels, o);                   \
+    else                                                                                                             \
+      hif4_rotate_signs_kernel<__nv_bfloat16, L, FAQ_ACT_GELU_TANH>                                                  \
+          <<<static_cast<unsigned>(blocks), 256, 0, st>>>(xb, rows, k, ldx, sc, signs, levels, o);                   \
+    return launch_status("hif4_rotate_signs_kernel (fused activation)");
+  switch (log2b) {
+    FAQ_ACT_CASE(3)
+    FAQ_ACT_CASE(4)
+    FAQ_ACT_CASE(5)
+    FAQ_ACT_CASE(6)
+    FAQ_ACT_CASE(7)
+    FAQ_ACT_CASE(8)
+    default:
+      break;
+  }
+#undef FAQ_ACT_CASE
+  return fail(FAQ_ERR_UNSUPPORTED, "rot_block");
 }
 
 extern "C" int faq_hif4_dequantize(const uint8_t* codes, const uint32_t* meta, int64_t rows, int64_t k, void* out,

@@ -131,6 +131,50 @@ def hif4_quantize(
     return qdq, codes, meta
 
 
+ACTIVATIONS = {"swiglu": 1, "gelu_tanh": 2}  # FAQ_ACT_SWIGLU, FAQ_ACT_GELU_TANH
+
+
+def hif4_quantize_act(
+    x: torch.Tensor,
+    act: str,
+    *,
+    levels: str | int = "123",
+    input_scale: torch.Tensor | None = None,
+    signs: torch.Tensor,
+    rot_block: int,
+    want_qdq: bool = True,
+    want_codes: bool = False,
+) -> tuple[torch.Tensor | None, torch.Tensor | None, torch.Tensor | None]:
+    """:func:`hif4_quantize` of an activation's output, the activation fused into the load
+    (``faq_hif4_quantize_act``): ``act="swiglu"`` takes the gate|up tensor ``x [rows, 2k]``
+    and quantizes ``silu_mul(x)``; ``act="gelu_tanh"`` takes ``x [rows, k]`` and quantizes
+    ``gelu_tanh(x)`` -- the same outputs as the activation followed by
+    :func:`hif4_quantize`, without the activation's tensor. bf16, signs-only rotation
+    (block 8..256); returns ``(qdq [rows, k], codes, meta)``."""
+    if act not in ACTIVATIONS:
+        raise ValueError(f"act must be one of {sorted(ACTIVATIONS)}")
+    device = _require_cuda(x, input_scale, signs)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("hif4_quantize_act takes a rank-2 bfloat16 tensor")
+    rows = x.shape[0]
+    k = x.shape[1] // 2 if act == "swiglu" else x.shape[1]
+    if act == "swiglu" and x.shape[1] % 2:
+        raise ValueError("the SwiGLU input holds gate and up halves: an even width")
+    if x.stride(-1) != 1 or (rows > 1 and x.stride(0) % 8) or x.data_ptr() % 16:
+        x = x.contiguous()
+    ldx = x.stride(0) if rows > 1 else x.shape[1]
+    qdq = torch.empty((rows, k), dtype=torch.bfloat16, device=device) if want_qdq else None
+    codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=device) if want_codes else None
+    meta = torch.empty((rows, k // 64), dtype=torch.int32, device=device) if want_codes else None
+    if input_scale is not None:
+        input_scale = input_scale.to(device=device, dtype=torch.bfloat16).contiguous()
+    signs = signs.to(device=device, dtype=torch.int8).contiguous()
+    _lib.call("faq_hif4_quantize_act", x.data_ptr(), ACTIVATIONS[act], rows, k, ldx, _ptr(input_scale),
+              signs.data_ptr(), int(rot_block), levels_code(levels), _ptr(codes), _ptr(meta), _ptr(qdq), k,
+              _stream(device))
+    return qdq, codes, meta
+
+
 def hif4_dequantize(codes: torch.Tensor, meta: torch.Tensor, k: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     device = _require_cuda(codes, meta)
     rows = codes.shape[0]

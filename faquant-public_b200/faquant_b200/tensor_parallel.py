@@ -143,11 +143,25 @@ class TPHiF4Linear(nn.Module):
     overlap_chunks = 4
     overlap_min_rows = 4096
 
-    def forward(self, x: torch.Tensor, *, quantized: bool = False, residual: torch.Tensor | None = None) -> torch.Tensor:
-        """``residual + linear(x)`` when ``residual`` is given: on one rank the add is in
-        the GEMM epilogue (the same bits as the separate bf16 add); row-parallel ranks add
-        after the all-reduce."""
-        xq = x if quantized else self.quantize_input(x)
+    def activate_and_quantize(self, x: torch.Tensor, act: str) -> torch.Tensor:
+        """The input ``act(x)`` ("swiglu" on gate|up, or "gelu_tanh") quantized: in one pass
+        (``ops.hif4_quantize_act``) for a quantized projection with a signs-only rotation,
+        else the activation kernel then :meth:`quantize_input` -- the same values."""
+        r = self.rotation
+        if self.quantize and r.signs is not None and r.permutation is None and 8 <= r.block <= 256:
+            return ops.hif4_quantize_act(x, act, levels=self.levels, signs=r.signs, rot_block=r.block)[0]
+        return self.quantize_input(ops.silu_mul(x) if act == "swiglu" else ops.gelu_tanh(x))
+
+    def forward(self, x: torch.Tensor, *, quantized: bool = False, residual: torch.Tensor | None = None,
+                act: str | None = None) -> torch.Tensor:
+        """``residual + linear(act(x))``: ``act`` ("swiglu" / "gelu_tanh") is applied to the
+        input first, fused into its quantization where possible; with ``residual`` on one
+        rank the add is in the GEMM epilogue (the same bits as the separate bf16 add),
+        row-parallel ranks add after the all-reduce."""
+        if act is not None:
+            xq = self.activate_and_quantize(x, act)
+        else:
+            xq = x if quantized else self.quantize_input(x)
         tp = self.reduce
         if tp is None or tp.world == 1:
             return ops.gemm_bf16(xq, self.weight, self.bias, residual=residual)
@@ -363,8 +377,11 @@ class Qwen3TPPrefill(nn.Module):
             x = self._t("x_mid", i, x)
             gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, ops.rms_norm(x, layer.post_norm,
                                                                                          cfg.eps))))
-            a = self._t("act", i, ops.silu_mul(gu))
-            x = layer.down(a, residual=x) if fuse else x + self._t("down", i, layer.down(a))
+            if fuse:  # SwiGLU in the down_proj input quantization, the residual add in its epilogue
+                x = layer.down(gu, act="swiglu", residual=x)
+            else:
+                a = self._t("act", i, ops.silu_mul(gu))
+                x = x + self._t("down", i, layer.down(a))
         last = self._t("final", len(self.layers), x.view(batch, seq, -1)[:, -1])
         return torch.nn.functional.linear(rms_norm(last, self.final_norm, cfg.eps), self.lm_head).float()
 
@@ -519,5 +536,7 @@ class WanBlockTP(nn.Module):
         x = tr("x_mid", self.o(att.view(seq, n), residual=x) if fuse else x + tr("o", self.o(att.view(seq, n))))
         h = tr("norm2", ops.layer_norm(x, cfg.eps))
         f0 = tr("ffn0", self.ffn0(h))
+        if fuse:  # the GELU in the ffn.2 input quantization, the residual add in its epilogue
+            return self.ffn2(f0, act="gelu_tanh", residual=x)
         a = tr("act", ops.gelu_tanh(f0))
-        return self.ffn2(a, residual=x) if fuse else x + tr("ffn2", self.ffn2(a))
+        return x + tr("ffn2", self.ffn2(a))

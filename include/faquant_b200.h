@@ -56,6 +56,11 @@ extern "C" {
 #define FAQ_LEVELS_12 12
 #define FAQ_LEVELS_13 13
 
+/* activations fused into faq_hif4_quantize_act */
+#define FAQ_ACT_NONE 0
+#define FAQ_ACT_SWIGLU 1    /* x [rows, 2k] = gate | up: bf16(bf16(silu(gate)) * up) (Qwen3MLP) */
+#define FAQ_ACT_GELU_TANH 2 /* x [rows, k]: the tanh GELU rounded to bf16 (the DiT FFN) */
+
 /* Version of the library as major*10000 + minor*100 + patch. */
 int faq_version(void);
 
@@ -85,6 +90,19 @@ int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64
                       const void* input_scale, const int8_t* signs, const int64_t* perm,
                       int rot_block, int levels, uint8_t* codes, uint32_t* meta, void* qdq,
                       int64_t ldq, void* stream);
+/*
+ * faq_hif4_quantize of an activation's output, the activation fused into the load: `act`
+ * FAQ_ACT_SWIGLU reads x [rows, 2k] (gate in columns 0..k-1, up in k..2k-1) and quantizes
+ * bf16(bf16(silu(gate)) * up); FAQ_ACT_GELU_TANH reads x [rows, k] and quantizes its tanh
+ * GELU rounded to bf16 -- the same values faq_silu_mul / faq_gelu_tanh write, so the
+ * outputs are those of the activation followed by faq_hif4_quantize, without the
+ * activation's [rows, k] tensor in HBM. bf16 only, signs-only rotations (`signs`, 8-byte
+ * aligned, with rot_block 8..256) -- the row-parallel down_proj / ffn.2 inputs; k % 64 == 0,
+ * 16-byte aligned rows. No counterpart in the reference (separate passes there).
+ */
+int faq_hif4_quantize_act(const void* x, int act, int64_t rows, int64_t k, int64_t ldx,
+                          const void* input_scale, const int8_t* signs, int rot_block, int levels,
+                          uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
 
 /* Dequantize packed HiF4 rows back to out [rows, ldo] (bf16 or fp32).
  * The inverse of the packing above; replaces expand_hif4_parameters +

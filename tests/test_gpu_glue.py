@@ -105,6 +105,30 @@ def test_row_sumsq_segments() -> None:
         assert torch.allclose(got, ref, rtol=1e-5, atol=0)
 
 
+@pytest.mark.parametrize("act,block,levels", [("swiglu", 64, "123"), ("swiglu", 256, "12"),
+                                              ("gelu_tanh", 64, "123"), ("gelu_tanh", 8, "13")])
+def test_quantize_act_equals_activation_then_quantize(act: str, block: int, levels: str) -> None:
+    """faq_hif4_quantize_act (the activation fused into the row-parallel input
+    quantization) gives the bits of faq_silu_mul / faq_gelu_tanh followed by
+    faq_hif4_quantize: dequantized values, codes and meta, with and without input_scale."""
+    from faquant_b200 import ops
+
+    g = torch.Generator().manual_seed(block + len(act))
+    rows, k = 333, 1536
+    width = 2 * k if act == "swiglu" else k
+    x = (torch.randn(rows, width, generator=g) * 3).to(torch.bfloat16).to(DEV)
+    x[5, :64] = 0.0
+    signs = torch.from_numpy(np.random.default_rng(block).choice([-1, 1], k).astype(np.int8)).to(DEV)
+    scale = (0.5 + torch.rand(k, generator=g)).to(torch.bfloat16).to(DEV)
+    a = ops.silu_mul(x) if act == "swiglu" else ops.gelu_tanh(x)
+    for sc in (None, scale):
+        fused = ops.hif4_quantize_act(x, act, levels=levels, input_scale=sc, signs=signs, rot_block=block,
+                                      want_codes=True)
+        separate = ops.hif4_quantize(a, levels=levels, input_scale=sc, signs=signs, rot_block=block, want_codes=True)
+        for f, s in zip(fused, separate):
+            assert torch.equal(f, s)
+
+
 def _wan_operands(seq, heads, d=128, seed=7):
     g = torch.Generator().manual_seed(seed)
     qkv = (torch.randn(seq, 3 * heads * d, generator=g) * 2).to(torch.bfloat16)
