@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(THREADS, 2) decode_scores_kernel(const __grid_
     tma_prefetch_desc(&tmap_k);
   }
   __syncthreads();
+  // launched early behind the previous kernel of the stream (which may have written q or
+  // the cache): everything above touched only shared memory and the tensor map
+  grid_dependency_wait();
   allow_dependent_launch();  // pass 2 may start setting up on SMs this pass leaves
   auto load_k = [&](int64_t u, int stage) {  // thread 0: the tile as two 64-channel boxes
     const int tile = static_cast<int>(u % p.ntiles), bh = static_cast<int>(u / p.ntiles);
@@ -472,6 +475,7 @@ __global__ void __launch_bounds__(THREADS, 2) decode_pv_kernel(const __grid_cons
 __global__ void __launch_bounds__(4 * D) decode_combine_kernel(Params p) {
   __shared__ float s_o[4][D], s_l[4];
   grid_dependency_wait();  // launched early, behind pass 2
+  allow_dependent_launch();  // the next call's pass 1 may set up (it writes no part_*)
   const int bh = blockIdx.x, r = blockIdx.y, dd = threadIdx.x % D, grp = threadIdx.x / D;
   const int b = bh / p.hkv, hk = bh % p.hkv;
   const int64_t base = static_cast<int64_t>(bh) * p.nsplits * p.rows;
@@ -569,21 +573,25 @@ static int decode_launch(dec::Params& p, float* ws, void* stream) {
                                 static_cast<int>(s1)));
   const int64_t units = bh * p.ntiles;
   const unsigned grid1 = static_cast<unsigned>(std::min<int64_t>(units, static_cast<int64_t>(num_sms()) * 2));
-  dec::decode_scores_kernel<<<grid1, dec::THREADS, s1, st>>>(tk, p);
   FAQ_CUDA(cudaFuncSetAttribute(dec::decode_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(s2)));
-  // passes 2 and 3 start while the kernel before them drains (programmatic dependent
-  // launch); each waits on the device before it reads that kernel's results
+  // All three passes start while the kernel before them drains (programmatic dependent
+  // launch) and wait on the device before they read that kernel's results. Pass 1 writes
+  // only the scores and tile maxima, which no earlier decode kernel reads once passes 2
+  // and 3 of that call have started.
   cudaLaunchAttribute early[1];
   early[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   early[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(p.nsplits), static_cast<unsigned>(bh));
+  cfg.gridDim = dim3(grid1);
   cfg.blockDim = dim3(dec::THREADS);
-  cfg.dynamicSmemBytes = s2;
+  cfg.dynamicSmemBytes = s1;
   cfg.stream = st;
   cfg.attrs = early;
   cfg.numAttrs = 1;
+  FAQ_CUDA(cudaLaunchKernelEx(&cfg, dec::decode_scores_kernel, tk, p));
+  cfg.gridDim = dim3(static_cast<unsigned>(p.nsplits), static_cast<unsigned>(bh));
+  cfg.dynamicSmemBytes = s2;
   FAQ_CUDA(cudaLaunchKernelEx(&cfg, dec::decode_pv_kernel, tv, p));
   cfg.gridDim = dim3(static_cast<unsigned>(bh), static_cast<unsigned>(p.rows));
   cfg.blockDim = dim3(4 * dec::D);
