@@ -533,6 +533,214 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
   }
 }
 
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// a - b as one packed FMA: b * -1 + a, a single rounding of the exact difference
+__device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
+
+// ---------------------------------------------------------------- 32 values per lane
+// HiF4 of 32 consecutive bf16 values held by one lane as 16 pair words in channel order
+// (value 2q in the low half of w[q]): half of a 64-block whose other half the partner
+// lane (lane ^ 1, the even lane holding the lower half) holds; both lanes call it
+// together (one shuffle for the block maximum, one for the meta word).
+//   - sign bits from the bf16 pattern, cleared where the magnitude is zero: a -0.0
+//     quantizes to +0 as the reference's sign(-0.0) == 0 does;
+//   - per-4 / per-8 maxima in registers, the E6M2 scale and its reciprocal
+//     (hif4_scale), the level shifts (hif4_level_shifts), then per pair on FP32x2
+//       t = min(fl(fl(|x| 4qm) + 0.5), 7.5)  (== clamping the code to 7 after the floor)
+//       r = t + 2^23 rounded toward zero    (== 2^23 + floor(t))
+//       mag = r * ds/4 - 2^23 * ds/4        (one FMA, exact: code * ds/4 has <= 6 bits)
+//     with 4 qm = rec 2^(2 - sh), ds / 4 = s 2^(sh - 2) and -2^23 ds / 4 as exponent-field
+//     moves of rec and s (both normal, and they stay normal).
+// Outputs: the dequantized pair words q[16], the nibbles nib[4] (codes, when CODES) and
+// the block's meta word (in both lanes).
+template <bool CODES>
+__device__ __forceinline__ void hif4_quant32_lane(const uint32_t (&w)[16], int levels, uint32_t (&q)[16],
+                                                  uint32_t (&nib)[4], uint32_t& meta) {
+  uint32_t sgn[16];  // sign bits of each bf16 pair, clear on a zero half
+  float2 a[16];      // |x| pairs
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t m = w[i] & 0x7FFF7FFFu;
+    // bit 15 of each half of m + 0x7FFF is set iff that half's magnitude is nonzero
+    // (no carry crosses the halves: 0x7FFF + 0x7FFF < 2^16)
+    sgn[i] = w[i] & (m + 0x7FFF7FFFu) & 0x80008000u;
+    a[i] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+  }
+  float m3[8], m2[4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[2 * i].x, a[2 * i].y), fmaxf(a[2 * i + 1].x, a[2 * i + 1].y));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
+  float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
+  m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
+  const Hif4Scale sc = hif4_scale(m1, levels);
+  uint32_t lvbits = 0;  // bit s: lv2 of sub-block s, bit 4+j: lv3 of quarter j
+  const uint32_t rec_q0 = __float_as_uint(sc.rec) + (2u << 23);  // 4 * rec
+  const uint32_t s_d0 = __float_as_uint(sc.s) - (2u << 23);      // s / 4
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    nib[s] = 0;
+    const float2 rab = __fmul2_rn(make_float2(m3[2 * s], m3[2 * s + 1]), make_float2(sc.rec, sc.rec));
+    uint32_t ea, eb;  // (lv2 + lv3) << 23 of the two quarters
+    const uint32_t lv2 = hif4_level_shifts(rab.x, rab.y, levels, ea, eb);
+    const uint32_t la = (ea >> 23) - lv2, lb = (eb >> 23) - lv2;
+    lvbits |= (lv2 << s) | (la << (4 + 2 * s)) | (lb << (5 + 2 * s));
+    const float2 qm_a = make_float2(__uint_as_float(rec_q0 - ea), __uint_as_float(rec_q0 - ea));
+    const float2 qm_b = make_float2(__uint_as_float(rec_q0 - eb), __uint_as_float(rec_q0 - eb));
+    const float2 ds_a = make_float2(__uint_as_float(s_d0 + ea), __uint_as_float(s_d0 + ea));
+    const float2 ds_b = make_float2(__uint_as_float(s_d0 + eb), __uint_as_float(s_d0 + eb));
+    const float2 of_a = make_float2(__uint_as_float(s_d0 + ea + 0x8B800000u), __uint_as_float(s_d0 + ea + 0x8B800000u));
+    const float2 of_b = make_float2(__uint_as_float(s_d0 + eb + 0x8B800000u), __uint_as_float(s_d0 + eb + 0x8B800000u));
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {  // pair 4 s + h, in quarter h / 2 of sub-block s
+      const int i = 4 * s + h;
+      float2 t = __fadd2_rn(__fmul2_rn(a[i], h < 2 ? qm_a : qm_b), make_float2(0.5f, 0.5f));
+      t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
+      const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
+      const float2 mag = __ffma2_rn(r, h < 2 ? ds_a : ds_b, h < 2 ? of_a : of_b);
+      q[i] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[i];
+      if constexpr (CODES) {
+        const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[i] >> 12) & 8u);  // r = 2^23 + code
+        const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[i] >> 28) & 8u);
+        nib[s] |= (na | (nb << 4)) << (8 * h);
+      }
+    }
+  }
+  const int half = threadIdx.x & 1;
+  uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
+  mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
+  meta = mb | sc.code;
+}
+
+// Stores of hif4_quant32_lane's outputs for channels col .. col + 31 of `row` (k % 64 == 0,
+// 16-byte aligned qdq rows and codes).
+__device__ __forceinline__ void store_quant32(const QuantOut& o, int64_t row, int64_t k, int64_t col,
+                                              const uint32_t (&q)[16], const uint32_t (&nib)[4], uint32_t meta,
+                                              bool codes) {
+  if (o.qdq) {
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) dst[s] = make_uint4(q[4 * s], q[4 * s + 1], q[4 * s + 2], q[4 * s + 3]);
+  }
+  if (codes && o.codes)
+    *reinterpret_cast<uint4*>(o.codes + row * (k / 2) + col / 2) = make_uint4(nib[0], nib[1], nib[2], nib[3]);
+  if (o.meta && (threadIdx.x & 1) == 0) o.meta[row * (k / 64) + col / 64] = meta;
+}
+
+// ---------------------------------------------------------------- K1, signs-only, 64-channel blocks
+// The row-parallel inputs (the reference's "signs" construction with 64-channel blocks,
+// bf16): a lane holds 32 consecutive channels, half of a block, and its partner lane
+// (lane ^ 1) the other half. Strides 1..16 run inside the lane on FP32x2 pairs, stride 32
+// with one exchange between the partners (the reference's stage order), then the
+// normalization by 1/8 (exact), one rounding to bf16 and hif4_quant32_lane -- the
+// arithmetic of hif4_rotate_signs_kernel with a quarter of its exchanges. Work items
+// (row, half block) run halves fastest, so a warp reads 2 KB of a row in 16-byte loads.
+// ACT fuses the activation into the load as in hif4_rotate_signs_kernel.
+template <int ACT, bool CODES>
+__global__ void __launch_bounds__(256) hif4_rotate_signs64_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                                  int64_t k, int64_t ldx,
+                                                                  const __nv_bfloat16* __restrict__ input_scale,
+                                                                  const int8_t* __restrict__ signs, int levels,
+                                                                  QuantOut o) {
+  const int64_t halves = k / 32;
+  const int64_t total = rows * halves;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t total_warps = (total + 31) / 32 * 32;  // whole warps: partners exchange
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx - lane < total_warps;
+       idx += stride) {
+    const bool live = idx < total;
+    const int64_t row = live ? idx / halves : 0, col = live ? (idx % halves) * 32 : 0;
+    const __nv_bfloat16* xr = x + row * ldx + col;
+    uint32_t w[16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint4 v = live ? __ldg(reinterpret_cast<const uint4*>(xr) + u) : make_uint4(0, 0, 0, 0);
+      w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
+    }
+    float2 p[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+    if constexpr (ACT == FAQ_ACT_SWIGLU) {  // x is [rows, 2k]: gate | up
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 v = live ? __ldg(reinterpret_cast<const uint4*>(xr + k) + u) : make_uint4(0, 0, 0, 0);
+        const uint32_t up[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2& g = p[4 * u + h];
+          g = make_float2(swiglu_bf16(g.x, __uint_as_float(up[h] << 16)),
+                          swiglu_bf16(g.y, __uint_as_float(up[h] & 0xFFFF0000u)));
+        }
+      }
+    } else if constexpr (ACT == FAQ_ACT_GELU_TANH) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) p[i] = make_float2(gelu_tanh_bf16(p[i].x), gelu_tanh_bf16(p[i].y));
+    }
+    if (input_scale != nullptr) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 v = live ? __ldg(reinterpret_cast<const uint4*>(input_scale + col) + u) : make_uint4(0, 0, 0, 0);
+        const uint32_t sc[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float2& e = p[4 * u + h];
+          e = make_float2(bf16_round(__fmul_rn(e.x, __uint_as_float(sc[h] << 16))),
+                          bf16_round(__fmul_rn(e.y, __uint_as_float(sc[h] & 0xFFFF0000u))));
+        }
+      }
+    }
+    // int8 signs: a negative one flips the sign bit (x * -1, exact)
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint4 v = live ? __ldg(reinterpret_cast<const uint4*>(signs + col) + u) : make_uint4(0, 0, 0, 0);
+      const uint32_t sg[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        // bytes 4h .. 4h + 3 of this 16-byte run: values 16 u + 4 h .. + 3, pairs 8 u + 2 h, + 1
+        float2& a = p[8 * u + 2 * h];
+        float2& b = p[8 * u + 2 * h + 1];
+        a.x = __uint_as_float(__float_as_uint(a.x) ^ ((sg[h] << 24) & 0x80000000u));
+        a.y = __uint_as_float(__float_as_uint(a.y) ^ ((sg[h] << 16) & 0x80000000u));
+        b.x = __uint_as_float(__float_as_uint(b.x) ^ ((sg[h] << 8) & 0x80000000u));
+        b.y = __uint_as_float(__float_as_uint(b.y) ^ (sg[h] & 0x80000000u));
+      }
+    }
+    // stride 1 inside each pair, strides 2 .. 16 between pairs (distance d = stride / 2)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) p[i] = make_float2(__fadd_rn(p[i].x, p[i].y), __fsub_rn(p[i].x, p[i].y));
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if ((i & d) == 0) {
+          const float2 l = p[i], r = p[i + d];
+          p[i] = f2add(l, r);
+          p[i + d] = f2sub(l, r);
+        }
+      }
+    }
+    // stride 32: the lower half (even lane) keeps a + b, the upper b's lane a - b
+    const bool upper = lane & 1;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float ox = __shfl_xor_sync(0xffffffffu, p[i].x, 1);
+      const float oy = __shfl_xor_sync(0xffffffffu, p[i].y, 1);
+      p[i] = upper ? make_float2(__fsub_rn(ox, p[i].x), __fsub_rn(oy, p[i].y))
+                   : make_float2(__fadd_rn(p[i].x, ox), __fadd_rn(p[i].y, oy));
+    }
+    // / sqrt(64) = * 2^-3 (exact), one rounding to bf16, as pair words
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const __nv_bfloat162 b2 = __float22bfloat162_rn(__fmul2_rn(p[i], make_float2(0.125f, 0.125f)));
+      w[i] = *reinterpret_cast<const uint32_t*>(&b2);
+    }
+    uint32_t q[16], nib[4], meta;
+    hif4_quant32_lane<CODES>(w, levels, q, nib, meta);
+    if (live) store_quant32(o, row, k, col, q, nib, meta, CODES);
+  }
+}
+
 // ---------------------------------------------------------------- K1 v4, rotation, bf16 rows
 // Throughput path for bf16 rows with k % 1024 == 0, k <= 16384 and 32 <= block <= 1024
 // (all HiSQ and r64 shapes of the BASELINE configurations). It is issue-bound (a
@@ -565,9 +773,6 @@ __global__ void __launch_bounds__(512) hif4_rotate_bf16_kernel(const __nv_bfloat
 // the row loop and the warps of a CTA drift freely over a row. The launch bounds hold
 // every width class to the registers of 20 resident warps per SM (the shared memory of a
 // 4-warp CTA allows 5).
-__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
-// a - b as one packed FMA: b * -1 + a, a single rounding of the exact difference
-__device__ __forceinline__ float2 f2sub(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
 
 // map entry w = ((chunk * 4 + t8) * 32 + lane) * 8 + e8 describes output channel
 // chunk * 1024 + 32 lane + 8 t8 + e8
@@ -739,82 +944,19 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
     // partner lane l ^ 1 holds the other half)
     {
       const int col = (ch << 10) + 32 * lane;
-      uint32_t sgn[16];  // sign bits of each bf16 pair, clear on a zero half
-      float2 a[16];      // |x| pairs, in channel order
+      uint32_t w[16];
       {
         const uint4* src = reinterpret_cast<const uint4*>(s_outw + 32 * lane);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const uint4 v = src[(u + rot) & 3];
-          const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const uint32_t w = w4[h];
-            const uint32_t m = w & 0x7FFF7FFFu;
-            // bit 15 of each half of m + 0x7FFF is set iff that half's magnitude is nonzero
-            // (no carry crosses the halves: 0x7FFF + 0x7FFF < 2^16)
-            sgn[4 * u + h] = w & (m + 0x7FFF7FFFu) & 0x80008000u;
-            a[4 * u + h] = make_float2(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
-          }
+          w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
         }
       }
       __syncwarp();  // the scratch is free for the next row's transpose
-      float m3[8], m2[4];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m3[i] = fmaxf(fmaxf(a[2 * i].x, a[2 * i].y), fmaxf(a[2 * i + 1].x, a[2 * i + 1].y));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) m2[i] = fmaxf(m3[2 * i], m3[2 * i + 1]);
-      float m1 = fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3]));
-      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, 1));
-      const Hif4Scale sc = hif4_scale(m1, levels);
-      uint32_t lvbits = 0;  // bit s: lv2 of sub-block s, bit 4+j: lv3 of quarter j
-      const uint32_t rec_q0 = __float_as_uint(sc.rec) + (2u << 23);  // 4 * rec
-      const uint32_t s_d0 = __float_as_uint(sc.s) - (2u << 23);      // s / 4
-      uint32_t nib[4] = {0, 0, 0, 0};
-      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(o.qdq) + row * o.ldq + col;
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const float2 rab = __fmul2_rn(make_float2(m3[2 * s], m3[2 * s + 1]), make_float2(sc.rec, sc.rec));
-        uint32_t ea, eb;  // (lv2 + lv3) << 23 of the two quarters
-        const uint32_t lv2 = hif4_level_shifts(rab.x, rab.y, levels, ea, eb);
-        const uint32_t la = (ea >> 23) - lv2, lb = (eb >> 23) - lv2;
-        lvbits |= (lv2 << s) | (la << (4 + 2 * s)) | (lb << (5 + 2 * s));
-        // 4 qm = rec * 2^(2 - sh) and ds / 4 = s * 2^(sh - 2) by moving the exponent field
-        // (rec and s are normal and stay normal); off = -2^23 * ds / 4 likewise
-        const float2 qm_a = make_float2(__uint_as_float(rec_q0 - ea), __uint_as_float(rec_q0 - ea));
-        const float2 qm_b = make_float2(__uint_as_float(rec_q0 - eb), __uint_as_float(rec_q0 - eb));
-        const float2 ds_a = make_float2(__uint_as_float(s_d0 + ea), __uint_as_float(s_d0 + ea));
-        const float2 ds_b = make_float2(__uint_as_float(s_d0 + eb), __uint_as_float(s_d0 + eb));
-        const float2 of_a = make_float2(__uint_as_float(s_d0 + ea + 0x8B800000u), __uint_as_float(s_d0 + ea + 0x8B800000u));
-        const float2 of_b = make_float2(__uint_as_float(s_d0 + eb + 0x8B800000u), __uint_as_float(s_d0 + eb + 0x8B800000u));
-        uint32_t packed[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          // pair q = values 2q, 2q+1 of sub-block s, in quarter h / 2:
-          //   t = min(fl(fl(|x| 4qm) + 0.5), 7.5)  (== clamping the code to 7 after the floor)
-          //   r = t + 2^23 rounded toward zero    (== 2^23 + floor(t))
-          //   mag = r * ds/4 - 2^23 * ds/4        (one FMA, exact: code * ds/4 has <= 6 bits)
-          const int q = 4 * s + h;
-          float2 t = __fadd2_rn(__fmul2_rn(a[q], h < 2 ? qm_a : qm_b), make_float2(0.5f, 0.5f));
-          t = make_float2(fminf(t.x, 7.5f), fminf(t.y, 7.5f));
-          const float2 r = __fadd2_rz(t, make_float2(8388608.0f, 8388608.0f));
-          const float2 mag = __ffma2_rn(r, h < 2 ? ds_a : ds_b, h < 2 ? of_a : of_b);
-          packed[h] = __byte_perm(__float_as_uint(mag.x), __float_as_uint(mag.y), 0x7632) | sgn[q];
-          if constexpr (CODES) {
-            const uint32_t na = (__float_as_uint(r.x) & 7u) | ((sgn[q] >> 12) & 8u);  // r = 2^23 + code
-            const uint32_t nb = (__float_as_uint(r.y) & 7u) | ((sgn[q] >> 28) & 8u);
-            nib[s] |= (na | (nb << 4)) << (8 * h);
-          }
-        }
-        if (o.qdq) *reinterpret_cast<uint4*>(dst + 8 * s) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      }
-      const int half = lane & 1;
-      uint32_t mb = ((lvbits & 0xFu) << (8 + 4 * half)) | (((lvbits >> 4) & 0xFFu) << (16 + 8 * half));
-      mb |= __shfl_xor_sync(0xffffffffu, mb, 1);
-      if constexpr (CODES) {
-        if (o.codes) *reinterpret_cast<uint4*>(o.codes + row * (k / 2) + col / 2) = make_uint4(nib[0], nib[1], nib[2], nib[3]);
-      }
-      if (o.meta && half == 0) o.meta[row * (k / 64) + col / 64] = mb | sc.code;
+      uint32_t q[16], nib[4], meta;
+      hif4_quant32_lane<CODES>(w, levels, q, nib, meta);
+      store_quant32(o, row, k, col, q, nib, meta, CODES);
     }
     // refill this buffer with the row after next once every warp has gathered from it
     if (loader) {
@@ -945,6 +1087,24 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
   int block = rot_block == 0 ? 1 : rot_block;
   int log2b = 0;
   while ((1 << log2b) < block) ++log2b;
+  // signs without a permutation in 64-channel blocks, bf16: two lanes per block
+  if constexpr (sizeof(T) == 2) {
+    if (perm == nullptr && log2b == 6 && k % 64 == 0 && x_vec && (o.qdq == nullptr || o.qdq_vec) &&
+        aligned16(signs) && (o.codes == nullptr || aligned16(o.codes))) {
+      const int64_t threads = rows * (k / 32);
+      const int64_t blocks = std::min<int64_t>((threads + 255) / 256, static_cast<int64_t>(sms) * 8);
+      if (blocks == 0) return FAQ_OK;
+      const auto* xb = static_cast<const __nv_bfloat16*>(x);
+      const auto* sc = static_cast<const __nv_bfloat16*>(input_scale);
+      if (o.codes != nullptr)
+        hif4_rotate_signs64_kernel<FAQ_ACT_NONE, true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            xb, rows, k, ldx, sc, signs, levels, o);
+      else
+        hif4_rotate_signs64_kernel<FAQ_ACT_NONE, false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+            xb, rows, k, ldx, sc, signs, levels, o);
+      return launch_status("hif4_rotate_signs64_kernel");
+    }
+  }
   // signs without a permutation: blocks are independent, the row streams (no staging)
   if (perm == nullptr && log2b >= 3 && log2b <= 8 && k % 64 == 0 && k % block == 0 && x_vec &&
       (o.qdq == nullptr || o.qdq_vec) &&
@@ -1139,10 +1299,23 @@ extern "C" int faq_hif4_quantize_act(const void* x, int act, int64_t rows, int64
   if (rows == 0) return FAQ_OK;
   int log2b = 0;
   while ((1 << log2b) < rot_block) ++log2b;
-  const int64_t blocks = std::min<int64_t>((rows * (k / 8) + 255) / 256, static_cast<int64_t>(num_sms()) * 16);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   const auto* sc = static_cast<const __nv_bfloat16*>(input_scale);
+  if (log2b == 6 && aligned16(signs) && (codes == nullptr || aligned16(codes))) {  // two lanes per block
+    const int64_t blocks64 = std::min<int64_t>((rows * (k / 32) + 255) / 256, static_cast<int64_t>(num_sms()) * 8);
+    const bool cd = codes != nullptr;
+    if (act == FAQ_ACT_SWIGLU) {
+      auto kern = cd ? hif4_rotate_signs64_kernel<FAQ_ACT_SWIGLU, true> : hif4_rotate_signs64_kernel<FAQ_ACT_SWIGLU, false>;
+      kern<<<static_cast<unsigned>(blocks64), 256, 0, st>>>(xb, rows, k, ldx, sc, signs, levels, o);
+    } else {
+      auto kern = cd ? hif4_rotate_signs64_kernel<FAQ_ACT_GELU_TANH, true>
+                     : hif4_rotate_signs64_kernel<FAQ_ACT_GELU_TANH, false>;
+      kern<<<static_cast<unsigned>(blocks64), 256, 0, st>>>(xb, rows, k, ldx, sc, signs, levels, o);
+    }
+    return launch_status("hif4_rotate_signs64_kernel (fused activation)");
+  }
+  const int64_t blocks = std::min<int64_t>((rows * (k / 8) + 255) / 256, static_cast<int64_t>(num_sms()) * 16);
 #define FAQ_ACT_CASE(L)                                                                                              \
   case L:                                                                                                            \
     if (act == FAQ_ACT_SWIGLU)                                                                                       \
