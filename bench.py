@@ -68,6 +68,30 @@ def peaks() -> tuple[dict, str]:
 
 
 # ------------------------------------------------------------------ distributed
+def gpu_numa_cpus(device) -> tuple[int, set[int]] | None:
+    """The NUMA node the GPU's PCIe slot hangs off and that node's CPUs (from sysfs), or
+    None where the box does not say. Pinned host buffers placed on that node keep the
+    host <-> device copies off the socket interconnect."""
+    import torch
+
+    try:
+        prop = torch.cuda.get_device_properties(device)
+        bus = f"{getattr(prop, 'pci_domain_id', 0):04x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/numa_node") as f:
+            node = int(f.read().strip())
+        if node < 0:
+            return None
+        with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+            cpus: set[int] = set()
+            for part in f.read().strip().split(","):
+                lo, _, hi = part.partition("-")
+                cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        return (node, cpus) if cpus else None
+    except (AssertionError, AttributeError, OSError, RuntimeError, ValueError):
+        return None
+
+
 def dist_env() -> tuple[int, int, int]:
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -403,6 +427,11 @@ def main_arm(args) -> None:
         from faquant_b200.quantization import FakeQuantLinear
 
         mods, host_x, host_y = [], [], []
+        # allocate (and so place) the pinned buffers from CPUs of the GPU's NUMA node
+        numa = gpu_numa_cpus(device)
+        saved_affinity = os.sched_getaffinity(0)
+        if numa is not None:
+            os.sched_setaffinity(0, numa[1])
         for L in layers:
             lin = torch.nn.Linear(L["k"], L["n"], bias=False, device="meta")
             lin.weight = torch.nn.Parameter(L["w"], requires_grad=False)
@@ -413,6 +442,8 @@ def main_arm(args) -> None:
             mods.append(m)
             host_x.append(L["x"].cpu().pin_memory())
             host_y.append(torch.empty(T_TOKENS, L["n"], dtype=torch.bfloat16).pin_memory())
+            host_y[-1].zero_()  # touch the pages here, on this node
+        os.sched_setaffinity(0, saved_affinity)
 
         # The projections' host copies are pipelined with their compute, as a serving loop
         # streams batches: inputs go up on one side stream, outputs come down on another
@@ -466,7 +497,8 @@ def main_arm(args) -> None:
         e2e = {"value": linear_flops() * world / (float(e_ms.item()) * 1e-3) / 1e12, "unit": "TFLOPS",
                "ms_per_step": float(e_ms.item()),
                "h2d_bytes_per_step": sum(h.numel() * 2 for h in host_x),
-               "d2h_bytes_per_step": sum(h.numel() * 2 for h in host_y)}
+               "d2h_bytes_per_step": sum(h.numel() * 2 for h in host_y),
+               "host_numa_node": None if numa is None else numa[0]}
 
     if rank == 0:
         traffic = None
