@@ -33,44 +33,64 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {  // values already
                     exact_bf16_bits(v[6]) | (exact_bf16_bits(v[7]) << 16));
 }
 
-// One CTA (256 threads) per row; up to CHUNKS 8-value chunks per thread stay in
-// registers between the reduction and the scaling (k <= 256 * 8 * CHUNKS).
-template <int CHUNKS>
+// One CTA per row, warp w owning the 1024-channel chunks w, w + W, ...; the row's packed
+// bf16 values stay in registers between the reduction and the scaling. The fp32 sum of
+// squares has a fixed order that the fused norm of K1 (faq_hif4_quantize_rms_norm)
+// repeats bit for bit: lane l of chunk c sums the squares of channels 1024 c + 32 l ..
+// + 31 -- its four 8-channel units in the order u = (i + ((l >> 1) & 3)) & 3, i = 0..3
+// (the order in which K1 reads them from shared memory without bank conflicts), the even
+// and the odd channels in two running sums added at the end; the lanes' sums meet in an
+// xor tree (16, 8, 4, 2, 1); the chunks' sums are added in chunk order.
+template <int CH>
 __global__ void __launch_bounds__(256) rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                       int64_t ldx, const __nv_bfloat16* __restrict__ w, float eps,
                                                       __nv_bfloat16* __restrict__ out, int64_t ldo) {
-  __shared__ float partial[8];
-  const int tid = threadIdx.x, chunks = k / 8;
+  __shared__ float partial[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+  const int nchunks = (k + 1023) / 1024, rot = (lane >> 1) & 3;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[CHUNKS][8];
-    float ss = 0.0f;
+    uint4 v[CH][4];
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int ch = tid + c * 256;
-      if (ch < chunks) {
-        unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + ch * 8), v[c]);
+    for (int c = 0; c < CH; ++c) {
+      const int chunk = warp + c * W;
+      float2 ss2 = make_float2(0.0f, 0.0f);  // even and odd channels, each in turn
 #pragma unroll
-        for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(v[c][i], v[c][i]));
+      for (int u = 0; u < 4; ++u) {  // slot u holds unit (u + rot) & 3
+        const int col = chunk * 1024 + 32 * lane + 8 * ((u + rot) & 3);
+        v[c][u] = chunk < nchunks && col < k ? *reinterpret_cast<const uint4*>(x + row * ldx + col)
+                                             : make_uint4(0, 0, 0, 0);
+        float f[8];
+        unpack8(v[c][u], f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 ab = make_float2(f[2 * i], f[2 * i + 1]);
+          ss2 = __fadd2_rn(ss2, __fmul2_rn(ab, ab));
+        }
       }
-    }
+      float ss = __fadd_rn(ss2.x, ss2.y);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-    if ((tid & 31) == 0) partial[tid >> 5] = ss;
+      for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0 && chunk < nchunks) partial[chunk] = ss;
+    }
     __syncthreads();
     float total = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) total = __fadd_rn(total, partial[i]);
+    for (int c = 0; c < nchunks; ++c) total = __fadd_rn(total, partial[c]);
     __syncthreads();  // partial[] is rewritten by the next row
     const float r = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps));
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int ch = tid + c * 256;
-      if (ch < chunks) {
-        float wv[8], y[8];
-        unpack8(*reinterpret_cast<const uint4*>(w + ch * 8), wv);
+    for (int c = 0; c < CH; ++c) {
+      const int chunk = warp + c * W;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(wv[i], bf16_round(__fmul_rn(v[c][i], r))));
-        *reinterpret_cast<uint4*>(out + row * ldo + ch * 8) = pack8(y);
+      for (int u = 0; u < 4; ++u) {
+        const int col = chunk * 1024 + 32 * lane + 8 * ((u + rot) & 3);
+        if (chunk < nchunks && col < k) {
+          float f[8], wv[8], y[8];
+          unpack8(v[c][u], f);
+          unpack8(*reinterpret_cast<const uint4*>(w + col), wv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(wv[i], bf16_round(__fmul_rn(f[i], r))));
+          *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
+        }
       }
     }
   }
@@ -214,17 +234,16 @@ extern "C" int faq_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx,
   const auto* xp = static_cast<const __nv_bfloat16*>(x);
   const auto* wp = static_cast<const __nv_bfloat16*>(weight);
   auto* op = static_cast<__nv_bfloat16*>(out);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int chunks = static_cast<int>(k / 8), per_thread = (chunks + 255) / 256;
-  if (per_thread <= 2)
-    rms_norm_kernel<2><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
-  else if (per_thread <= 4)
-    rms_norm_kernel<4><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
-  else if (per_thread <= 8)
-    rms_norm_kernel<8><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  const int nchunks = static_cast<int>((k + 1023) / 1024);  // <= 32
+  const int W = std::min(nchunks, 8), per_warp = (nchunks + W - 1) / W;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 16));
+  if (per_warp == 1)
+    rms_norm_kernel<1><<<grid, 32 * W, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+  else if (per_warp == 2)
+    rms_norm_kernel<2><<<grid, 32 * W, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
   else
-    rms_norm_kernel<16><<<grid, 256, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
+    rms_norm_kernel<4><<<grid, 32 * W, 0, st>>>(xp, rows, static_cast<int>(k), ldx, wp, eps, op, ldo);
   return launch_status("rms_norm_kernel");
 }
 

@@ -175,6 +175,50 @@ def hif4_quantize_act(
     return qdq, codes, meta
 
 
+def rms_norm_quantize_supported(k: int, rot_block: int | None) -> bool:
+    """Whether :func:`hif4_quantize_rms_norm` takes a row of ``k`` channels rotated in
+    blocks of ``rot_block`` (the K1 v4 shapes: k % 1024 == 0, k <= 16384, 32..1024)."""
+    return (rot_block is not None and k % 1024 == 0 and k <= 16384 and 32 <= rot_block <= 1024
+            and rot_block & (rot_block - 1) == 0)
+
+
+def hif4_quantize_rms_norm(
+    x: torch.Tensor,
+    norm_weight: torch.Tensor,
+    eps: float,
+    *,
+    levels: str | int = "123",
+    input_scale: torch.Tensor | None = None,
+    signs: torch.Tensor,
+    permutation: torch.Tensor | None = None,
+    rot_block: int,
+    want_meta: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """:func:`hif4_quantize` of ``rms_norm(x, norm_weight, eps)`` in one pass
+    (``faq_hif4_quantize_rms_norm``): the same bits as :func:`rms_norm` followed by
+    :func:`hif4_quantize`, without the normalized tensor in memory. bf16 ``x [rows, k]``
+    with ``rms_norm_quantize_supported(k, rot_block)``; returns ``(qdq, meta)``."""
+    device = _require_cuda(x, norm_weight, input_scale, signs, permutation)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("hif4_quantize_rms_norm takes a rank-2 bfloat16 tensor")
+    rows, k = x.shape
+    if x.stride(-1) != 1 or (rows > 1 and x.stride(0) % 8) or x.data_ptr() % 16:
+        x = x.contiguous()
+    ldx = x.stride(0) if rows > 1 else k
+    qdq = torch.empty((rows, k), dtype=torch.bfloat16, device=device)
+    meta = torch.empty((rows, k // 64), dtype=torch.int32, device=device) if want_meta else None
+    norm_weight = norm_weight.to(device=device, dtype=torch.bfloat16).contiguous()
+    if input_scale is not None:
+        input_scale = input_scale.to(device=device, dtype=torch.bfloat16).contiguous()
+    signs = signs.to(device=device, dtype=torch.int8).contiguous()
+    if permutation is not None:
+        permutation = permutation.to(device=device, dtype=torch.int64).contiguous()
+    _lib.call("faq_hif4_quantize_rms_norm", x.data_ptr(), rows, k, ldx, norm_weight.data_ptr(), float(eps),
+              _ptr(input_scale), signs.data_ptr(), _ptr(permutation), int(rot_block), levels_code(levels),
+              _ptr(meta), qdq.data_ptr(), k, _stream(device))
+    return qdq, meta
+
+
 def hif4_dequantize(codes: torch.Tensor, meta: torch.Tensor, k: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
     device = _require_cuda(codes, meta)
     rows = codes.shape[0]

@@ -152,13 +152,27 @@ class TPHiF4Linear(nn.Module):
             return ops.hif4_quantize_act(x, act, levels=self.levels, signs=r.signs, rot_block=r.block)[0]
         return self.quantize_input(ops.silu_mul(x) if act == "swiglu" else ops.gelu_tanh(x))
 
+    def norm_and_quantize(self, x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+        """The input ``rms_norm(x, weight, eps)`` quantized: in one pass
+        (``ops.hif4_quantize_rms_norm``: the norm inside K1, nothing written between) for a
+        quantized projection with a rotation K1 v4 takes, else the norm kernel then
+        :meth:`quantize_input` -- the same values."""
+        r = self.rotation
+        if self.quantize and r.signs is not None and ops.rms_norm_quantize_supported(x.shape[-1], r.block):
+            return ops.hif4_quantize_rms_norm(x, weight, eps, levels=self.levels, signs=r.signs,
+                                              permutation=r.permutation, rot_block=r.block)[0]
+        return self.quantize_input(ops.rms_norm(x, weight, eps))
+
     def forward(self, x: torch.Tensor, *, quantized: bool = False, residual: torch.Tensor | None = None,
-                act: str | None = None) -> torch.Tensor:
+                act: str | None = None, norm: tuple[torch.Tensor, float] | None = None) -> torch.Tensor:
         """``residual + linear(act(x))``: ``act`` ("swiglu" / "gelu_tanh") is applied to the
-        input first, fused into its quantization where possible; with ``residual`` on one
+        input first, fused into its quantization where possible; ``norm = (weight, eps)``
+        applies the RMSNorm to the input first, likewise fused; with ``residual`` on one
         rank the add is in the GEMM epilogue (the same bits as the separate bf16 add),
         row-parallel ranks add after the all-reduce."""
-        if act is not None:
+        if norm is not None:
+            xq = self.norm_and_quantize(x, *norm)
+        elif act is not None:
             xq = self.activate_and_quantize(x, act)
         else:
             xq = x if quantized else self.quantize_input(x)
@@ -344,9 +358,15 @@ class Qwen3TPPrefill(nn.Module):
         return t
 
     def _attention(self, layer: _Qwen3Layer, h: torch.Tensor, batch: int, seq: int, cos, sin,
-                   index: int = 0, residual: torch.Tensor | None = None) -> torch.Tensor:
+                   index: int = 0, residual: torch.Tensor | None = None,
+                   norm: tuple[torch.Tensor, float] | None = None) -> torch.Tensor:
+        """``h`` is the normalized input, or with ``norm`` the raw one (the norm is then
+        fused into the qkv input quantization)."""
         cfg, d = self.cfg, self.cfg.head_dim
-        qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
+        if norm is None:
+            qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
+        else:
+            qkv = self._t("qkv", index, layer.qkv(h, norm=norm))
         nq, nk = layer.heads * d, layer.kv_heads * d
         # q_norm/k_norm, RoPE, Hadamard and HiF4 in one K4 pass per operand
         q = qkv[:, :nq].view(batch, seq, layer.heads, d).transpose(1, 2)
@@ -369,14 +389,14 @@ class Qwen3TPPrefill(nn.Module):
         x = torch.nn.functional.embedding(input_ids.reshape(-1), self.embed)  # [T, hidden]
         fuse = self.fuse_residual and self.trace is None
         for i, layer in enumerate(self.layers):
-            h = ops.rms_norm(self._t("x", i, x), layer.input_norm, cfg.eps)
-            if fuse:
-                x = self._attention(layer, h, batch, seq, cos, sin, i, residual=x)
+            if fuse:  # the norms inside the qkv / gate_up input quantization, the residual adds in the epilogues
+                x = self._attention(layer, x, batch, seq, cos, sin, i, residual=x, norm=(layer.input_norm, cfg.eps))
+                gu = layer.gate_up(x, norm=(layer.post_norm, cfg.eps))
             else:
-                x = x + self._attention(layer, h, batch, seq, cos, sin, i)
-            x = self._t("x_mid", i, x)
-            gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, ops.rms_norm(x, layer.post_norm,
-                                                                                         cfg.eps))))
+                h = ops.rms_norm(self._t("x", i, x), layer.input_norm, cfg.eps)
+                x = self._t("x_mid", i, x + self._attention(layer, h, batch, seq, cos, sin, i))
+                gu = self._t("gate_up", i, layer.gate_up(self._t("post_norm", i, ops.rms_norm(x, layer.post_norm,
+                                                                                             cfg.eps))))
             if fuse:  # SwiGLU in the down_proj input quantization, the residual add in its epilogue
                 x = layer.down(gu, act="swiglu", residual=x)
             else:

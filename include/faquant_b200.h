@@ -91,6 +91,22 @@ int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64
                       int rot_block, int levels, uint8_t* codes, uint32_t* meta, void* qdq,
                       int64_t ldq, void* stream);
 /*
+ * K1 with the decoder layer's RMSNorm fused in front (the "per norm" HiSQ readers of a
+ * Qwen3 layer: input_layernorm -> q/k/v, post_attention_layernorm -> gate/up): each row
+ * x [rows, k] bf16 is normalized as faq_rms_norm does, bf16(w * bf16(x * rsqrt(mean(x^2)
+ * + eps))) with the same fp32 summation order, so the same bits, then (optionally
+ * times input_scale, rounded) rotated with signs / perm / rot_block and HiF4-quantized
+ * exactly as faq_hif4_quantize. The normalized tensor never goes to memory. Replaces the
+ * pair Qwen3RMSNorm (modeling_qwen3 as the reference's models use it) then the input
+ * path of FakeQuantLinear.forward (src/faquant/quantization.py:200-221). bf16 only;
+ * qdq is required, meta optional (codes: use the unfused pair). FAQ_ERR_UNSUPPORTED
+ * unless k % 1024 == 0, k <= 16384 and 32 <= rot_block <= 1024.
+ */
+int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
+                               float eps, const void* input_scale, const int8_t* signs, const int64_t* perm,
+                               int rot_block, int levels, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
+
+/*
  * faq_hif4_quantize of an activation's output, the activation fused into the load: `act`
  * FAQ_ACT_SWIGLU reads x [rows, 2k] (gate in columns 0..k-1, up in k..2k-1) and quantizes
  * bf16(bf16(silu(gate)) * up); FAQ_ACT_GELU_TANH reads x [rows, k] and quantizes its tanh

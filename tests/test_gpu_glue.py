@@ -129,6 +129,46 @@ def test_quantize_act_equals_activation_then_quantize(act: str, block: int, leve
             assert torch.equal(f, s)
 
 
+@pytest.mark.parametrize("k,block", [(1024, 1024), (4096, 1024), (5120, 1024), (5120, 64), (12288, 32), (16384, 1024)])
+def test_quantize_rms_norm_equals_norm_then_quantize(k: int, block: int) -> None:
+    """faq_hif4_quantize_rms_norm (the decoder layer's RMSNorm inside K1) gives the bits of
+    faq_rms_norm followed by faq_hif4_quantize with the same HiSQ rotation: dequantized
+    values and meta, ragged row counts, with and without input_scale, two level sets."""
+    from faquant_b200 import ops
+    from faquant_b200.hisq_rotation import derive_hisq_rotation
+
+    g = torch.Generator().manual_seed(k + block)
+    rot = derive_hisq_rotation("model.layers.0.self_attn.q_proj", k, seed=17, block_size=block)
+    signs, perm = rot.signs.to(DEV), rot.permutation.to(DEV)
+    w = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16).to(DEV)
+    scale = (0.5 + torch.rand(k, generator=g)).to(torch.bfloat16).to(DEV)
+    assert ops.rms_norm_quantize_supported(k, block)
+    for rows, levels, sc in ((37, "123", None), (1, "12", scale), (300, "123", scale)):
+        x = (torch.randn(rows, k, generator=g) * 3).to(torch.bfloat16).to(DEV)
+        x[0, :1024] = 0.0  # a zero chunk
+        x[-1, :] *= 1e-3
+        fused, fmeta = ops.hif4_quantize_rms_norm(x, w, 1e-6, levels=levels, input_scale=sc, signs=signs,
+                                                  permutation=perm, rot_block=block, want_meta=True)
+        h = ops.rms_norm(x, w, 1e-6)
+        qdq, _, meta = ops.hif4_quantize(h, levels=levels, input_scale=sc, signs=signs, permutation=perm,
+                                         rot_block=block, want_codes=True)
+        assert torch.equal(fused, qdq), (rows, levels)
+        assert torch.equal(fmeta, meta), (rows, levels)
+    empty, _ = ops.hif4_quantize_rms_norm(torch.zeros(0, k, dtype=torch.bfloat16, device=DEV), w, 1e-6,
+                                          signs=signs, permutation=perm, rot_block=block)
+    assert empty.shape == (0, k)
+
+
+def test_quantize_rms_norm_rejects_unsupported_shapes() -> None:
+    from faquant_b200 import ops
+
+    x = torch.zeros(4, 1536, dtype=torch.bfloat16, device=DEV)
+    signs = torch.ones(1536, dtype=torch.int8, device=DEV)
+    assert not ops.rms_norm_quantize_supported(1536, 64)
+    with pytest.raises(NotImplementedError):
+        ops.hif4_quantize_rms_norm(x, torch.ones(1536, device=DEV), 1e-6, signs=signs, rot_block=64)
+
+
 def _wan_operands(seq, heads, d=128, seed=7):
     g = torch.Generator().manual_seed(seed)
     qkv = (torch.randn(seq, 3 * heads * d, generator=g) * 2).to(torch.bfloat16)
