@@ -15,6 +15,8 @@
 
 from __future__ import annotations
 
+import dataclasses
+
 import os
 import socket
 
@@ -179,11 +181,14 @@ def test_residual_adds_in_the_gemm_epilogue_are_the_same_bits() -> None:
     as the separate bf16 adds."""
     from faquant_b200.tensor_parallel import Qwen3TPPrefill, TPGroup, WanBlockTP, default_input_ids
 
-    model = Qwen3TPPrefill(_qwen_cfg(), TPGroup(), DEV)
-    ids = default_input_ids(2, 192, model.cfg.vocab, DEV, seed=4)
-    fused = model(ids)
-    model.fuse_residual = False
-    assert torch.equal(fused, model(ids))
+    # hidden 1024 also takes the RMSNorms into the qkv / gate_up input quantization
+    # (faq_hif4_quantize_rms_norm needs k % 1024 == 0); hidden 512 keeps them separate
+    for cfg in (_qwen_cfg(), dataclasses.replace(_qwen_cfg(), hidden=1024, column_block=1024)):
+        model = Qwen3TPPrefill(cfg, TPGroup(), DEV)
+        ids = default_input_ids(2, 192, model.cfg.vocab, DEV, seed=4)
+        fused = model(ids)
+        model.fuse_residual = False
+        assert torch.equal(fused, model(ids)), cfg.hidden
     block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
     x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
     fused = block(x)
