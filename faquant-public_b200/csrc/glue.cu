@@ -111,67 +111,90 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
   }
 }
 
-// One CTA (256 threads) per row, the row in registers: the mean, then the sum of squared
-// deviations from it (two passes over registers, one over HBM).
-template <int CHUNKS>
+// One CTA per row, warp w owning the 1024-channel chunks w, w + W, ...: the mean, then the
+// biased variance around it, each summed in the order faq_rms_norm uses (lane units
+// (i + ((l >> 1) & 3)) & 3, even and odd channels in two running sums, an xor tree over
+// the lanes, the chunks in order), which the fused norm of K1
+// (faq_hif4_quantize_layer_norm) repeats bit for bit.
+template <int CH>
 __global__ void __launch_bounds__(256) layer_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int k,
                                                         int64_t ldx, float eps, __nv_bfloat16* __restrict__ out,
                                                         int64_t ldo) {
-  __shared__ float partial[2][8];
-  const int tid = threadIdx.x, chunks = k / 8;
-  const float inv_k = 1.0f / static_cast<float>(k);
+  __shared__ float partial[2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+  const int nchunks = (k + 1023) / 1024, rot = (lane >> 1) & 3;
+  const float inv_k = __fdiv_rn(1.0f, static_cast<float>(k));
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    float v[CHUNKS][8];
-    float sum = 0.0f;
+    uint4 v[CH][4];
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int ch = tid + c * 256;
-      if (ch < chunks) {
-        unpack8(*reinterpret_cast<const uint4*>(x + row * ldx + ch * 8), v[c]);
+    for (int c = 0; c < CH; ++c) {
+      const int chunk = warp + c * W;
+      float2 s2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum = __fadd_rn(sum, v[c][i]);
+      for (int u = 0; u < 4; ++u) {  // slot u holds unit (u + rot) & 3
+        const int col = chunk * 1024 + 32 * lane + 8 * ((u + rot) & 3);
+        v[c][u] = chunk < nchunks && col < k ? *reinterpret_cast<const uint4*>(x + row * ldx + col)
+                                             : make_uint4(0, 0, 0, 0);
+        float f[8];
+        unpack8(v[c][u], f);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s2 = __fadd2_rn(s2, make_float2(f[2 * i], f[2 * i + 1]));
       }
-    }
+      float sum = __fadd_rn(s2.x, s2.y);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-    if ((tid & 31) == 0) partial[0][tid >> 5] = sum;
+      for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+      if (lane == 0 && chunk < nchunks) partial[0][chunk] = sum;
+    }
     __syncthreads();
     float total = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) total = __fadd_rn(total, partial[0][i]);
+    for (int c = 0; c < nchunks; ++c) total = __fadd_rn(total, partial[0][c]);
     const float mean = __fmul_rn(total, inv_k);
-    float dev = 0.0f;
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      if (tid + c * 256 < chunks) {
+    for (int c = 0; c < CH; ++c) {
+      const int chunk = warp + c * W;
+      float2 d2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float e = __fsub_rn(v[c][i], mean);
-          dev = __fadd_rn(dev, __fmul_rn(e, e));
+      for (int u = 0; u < 4; ++u) {
+        const int col = chunk * 1024 + 32 * lane + 8 * ((u + rot) & 3);
+        if (chunk < nchunks && col < k) {
+          float f[8];
+          unpack8(v[c][u], f);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 e = __ffma2_rn(make_float2(mean, mean), make_float2(-1.0f, -1.0f),
+                                        make_float2(f[2 * i], f[2 * i + 1]));
+            d2 = __fadd2_rn(d2, __fmul2_rn(e, e));
+          }
         }
       }
-    }
+      float dev = __fadd_rn(d2.x, d2.y);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dev = __fadd_rn(dev, __shfl_xor_sync(0xffffffffu, dev, o));
-    if ((tid & 31) == 0) partial[1][tid >> 5] = dev;
+      for (int o = 16; o > 0; o >>= 1) dev = __fadd_rn(dev, __shfl_xor_sync(0xffffffffu, dev, o));
+      if (lane == 0 && chunk < nchunks) partial[1][chunk] = dev;
+    }
     __syncthreads();
     float var = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) var = __fadd_rn(var, partial[1][i]);
+    for (int c = 0; c < nchunks; ++c) var = __fadd_rn(var, partial[1][c]);
     __syncthreads();  // partial[] is rewritten by the next row
     const float r = rsqrtf(__fadd_rn(__fmul_rn(var, inv_k), eps));
 #pragma unroll
-    for (int c = 0; c < CHUNKS; ++c) {
-      const int ch = tid + c * 256;
-      if (ch < chunks) {
-        float y[8];
+    for (int c = 0; c < CH; ++c) {
+      const int chunk = warp + c * W;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(__fsub_rn(v[c][i], mean), r));
-        *reinterpret_cast<uint4*>(out + row * ldo + ch * 8) = pack8(y);
+      for (int u = 0; u < 4; ++u) {
+        const int col = chunk * 1024 + 32 * lane + 8 * ((u + rot) & 3);
+        if (chunk < nchunks && col < k) {
+          float f[8], y[8];
+          unpack8(v[c][u], f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = bf16_round(__fmul_rn(__fsub_rn(f[i], mean), r));
+          *reinterpret_cast<uint4*>(out + row * ldo + col) = pack8(y);
+        }
       }
     }
   }
 }
+
 
 __global__ void __launch_bounds__(256) gelu_tanh_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
                                                         int64_t cols, int64_t ld, __nv_bfloat16* __restrict__ out,
@@ -274,18 +297,17 @@ extern "C" int faq_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ld
   FAQ_CHECK_ARG(eps >= 0.0f, "eps must be non-negative");
   const auto* xp = static_cast<const __nv_bfloat16*>(x);
   auto* op = static_cast<__nv_bfloat16*>(out);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int chunks = static_cast<int>(k / 8), per_thread = (chunks + 255) / 256;
+  const int nchunks = static_cast<int>((k + 1023) / 1024);  // <= 32
+  const int W = std::min(nchunks, 8), per_warp = (nchunks + W - 1) / W;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 16));
   const int kk = static_cast<int>(k);
-  if (per_thread <= 1)
-    layer_norm_kernel<1><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
-  else if (per_thread <= 3)
-    layer_norm_kernel<3><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
-  else if (per_thread <= 8)
-    layer_norm_kernel<8><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  if (per_warp == 1)
+    layer_norm_kernel<1><<<grid, 32 * W, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+  else if (per_warp == 2)
+    layer_norm_kernel<2><<<grid, 32 * W, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
   else
-    layer_norm_kernel<16><<<grid, 256, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
+    layer_norm_kernel<4><<<grid, 32 * W, 0, st>>>(xp, rows, kk, ldx, eps, op, ldo);
   return launch_status("layer_norm_kernel");
 }
 

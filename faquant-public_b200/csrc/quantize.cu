@@ -788,24 +788,34 @@ __device__ __forceinline__ float v4_gathered(const unsigned char* in, uint32_t o
   return __uint_as_float(bits ^ sign);
 }
 
-// the two channels of one map word (low entry -> .x); NORM applies the RMSNorm first,
-// bf16(gamma * bf16(x * rn)), on the bf16 pair (cvt.rn.bf16x2 rounds each half as
-// bf16_round does)
-template <bool NORM>
-__device__ __forceinline__ float2 v4_gathered2(const unsigned char* in, const unsigned char* gam, float rn, uint32_t m,
-                                               const __nv_bfloat16* __restrict__ input_scale) {
+// fused norms of K1 v4
+constexpr int kNormNone = 0, kNormRms = 1, kNormLayer = 2;
+
+// the two channels of one map word (low entry -> .x); NORM == kNormRms applies the RMSNorm
+// first, bf16(gamma * bf16(x * rn)), NORM == kNormLayer the affine-free LayerNorm,
+// bf16((x - mu) * rn), on the pair (cvt.rn.bf16x2 rounds each half as bf16_round does)
+template <int NORM>
+__device__ __forceinline__ float2 v4_gathered2(const unsigned char* in, const unsigned char* gam, float rn, float mu,
+                                               uint32_t m, const __nv_bfloat16* __restrict__ input_scale) {
   const uint32_t oa = m & 0x7FFFu, ob = (m >> 16) & 0x7FFFu;
   const uint32_t sa = (m << 16) & 0x80000000u, sb = m & 0x80000000u;
-  if constexpr (!NORM) {
+  if constexpr (NORM == kNormNone) {
     return make_float2(v4_gathered(in, oa, sa, input_scale), v4_gathered(in, ob, sb, input_scale));
   } else {
     const float2 xv = make_float2(__uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(in + oa)) << 16),
                                   __uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(in + ob)) << 16));
-    const float2 gv = make_float2(__uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(gam + oa)) << 16),
+    [[maybe_unused]] const float2 gv = make_float2(__uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(gam + oa)) << 16),
                                   __uint_as_float(static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(gam + ob)) << 16));
-    __nv_bfloat162 t = __float22bfloat162_rn(__fmul2_rn(xv, make_float2(rn, rn)));
-    uint32_t tb = *reinterpret_cast<const uint32_t*>(&t);
-    t = __float22bfloat162_rn(__fmul2_rn(gv, make_float2(__uint_as_float(tb << 16), __uint_as_float(tb & 0xFFFF0000u))));
+    __nv_bfloat162 t;
+    uint32_t tb;
+    if constexpr (NORM == kNormRms) {
+      t = __float22bfloat162_rn(__fmul2_rn(xv, make_float2(rn, rn)));
+      tb = *reinterpret_cast<const uint32_t*>(&t);
+      t = __float22bfloat162_rn(__fmul2_rn(gv, make_float2(__uint_as_float(tb << 16), __uint_as_float(tb & 0xFFFF0000u))));
+    } else {  // x - mu as one rounding of the exact difference, then the scale
+      t = __float22bfloat162_rn(__fmul2_rn(__ffma2_rn(make_float2(mu, mu), make_float2(-1.0f, -1.0f), xv),
+                                           make_float2(rn, rn)));
+    }
     tb = *reinterpret_cast<const uint32_t*>(&t);
     uint32_t ba = tb << 16, bb = tb & 0xFFFF0000u;
     if (input_scale != nullptr) {
@@ -820,13 +830,13 @@ constexpr int kK1Warps = 20;  // resident warps per SM the launch bounds size re
 
 // dynamic shared memory of K1 v4: barriers, map (2 B per channel), two row buffers, one
 // 32 x 34 float transpose scratch per warp; with the norm, its weight and the partial sums
-inline size_t v4_smem_bytes(int64_t k, bool norm) {
+inline size_t v4_smem_bytes(int64_t k, int norm) {
   const size_t w = static_cast<size_t>(k / 1024);
   return 64 + static_cast<size_t>(k) * 2 + static_cast<size_t>(k) * 4 + w * 32 * 34 * 4 +
-         (norm ? static_cast<size_t>(k) * 2 + 128 : 0);
+         (norm == kNormRms ? static_cast<size_t>(k) * 2 + 128 : norm == kNormLayer ? 256 : 0);
 }
 
-template <int LOG2B, bool CODES, int MAXW, bool NORM = false>
+template <int LOG2B, bool CODES, int MAXW, int NORM = kNormNone>
 __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MAXW : 1) hif4_rotate_v4_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t rows, int k, int64_t ldx,
     const __nv_bfloat16* __restrict__ input_scale, const int8_t* __restrict__ signs,
@@ -838,12 +848,12 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
   const int W = blockDim.x >> 5;  // == k / 1024
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
   uint64_t* empty = full + 2;
-  uint64_t* normbar = full + 4;  // NORM, [2] by row parity: every warp's sum of squares is in s_part
+  uint64_t* normbar = full + 4;  // NORM, [kind][2] by row parity: every warp's partial sum is in s_part
   unsigned char* s_map = smem_raw + 64;
   unsigned char* s_in = s_map + static_cast<size_t>(k) * 2;                    // [2][k] bf16
   float* s_tr = reinterpret_cast<float*>(s_in + static_cast<size_t>(k) * 4);  // [W][32 * TS]
   unsigned char* s_gamma = reinterpret_cast<unsigned char*>(s_tr + W * 32 * TS);  // NORM: [k] bf16
-  float* s_part = reinterpret_cast<float*>(s_gamma + static_cast<size_t>(k) * 2);  // NORM: [2][16]
+  float* s_part = reinterpret_cast<float*>(s_gamma + (NORM == kNormRms ? static_cast<size_t>(k) * 2 : 0));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t row_bytes = static_cast<uint32_t>(k) * 2;
   const int64_t G = gridDim.x;
@@ -856,9 +866,8 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
     mbar_init(smem_addr(&full[1]), 1);
     mbar_init(smem_addr(&empty[0]), W);
     mbar_init(smem_addr(&empty[1]), W);
-    if constexpr (NORM) {
-      mbar_init(smem_addr(&normbar[0]), W);
-      mbar_init(smem_addr(&normbar[1]), W);
+    if constexpr (NORM != kNormNone) {
+      for (int b = 0; b < (NORM == kNormLayer ? 4 : 2); ++b) mbar_init(smem_addr(&normbar[b]), W);
     }
     fence_barrier_init();
     for (int b = 0; b < 2; ++b) {
@@ -892,7 +901,7 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
       }
     }
   }
-  if constexpr (NORM) {  // the norm weight in channel order (k % 1024 == 0: whole 16-byte units)
+  if constexpr (NORM == kNormRms) {  // the norm weight in channel order (k % 1024 == 0: whole 16-byte units)
     for (int i = tid; i < k / 8; i += static_cast<int>(blockDim.x))
       reinterpret_cast<uint4*>(s_gamma)[i] = __ldg(reinterpret_cast<const uint4*>(gamma) + i);
   }
@@ -909,8 +918,8 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
     if (!mbar_wait_warp(smem_addr(&full[buf]), (it >> 1) & 1, 31, it)) break;
     if (loader) pending &= ~(1u << buf);
     const unsigned char* in = s_in + buf * row_bytes;
-    float rn = 0.0f;  // NORM: rsqrt(mean(x^2) + eps) of this row
-    if constexpr (NORM) {
+    float rn = 0.0f, mu = 0.0f;  // NORM: the row's rsqrt(... + eps) and (LayerNorm) mean
+    if constexpr (NORM == kNormRms) {
       // the sum of squares in the order of faq_rms_norm: lane l of chunk c takes its four
       // 8-channel units u = (i + rot) & 3, i = 0..3 (conflict-free 16-byte reads), even and
       // odd channels in two running sums added at the end, then an xor tree over the lanes,
@@ -941,6 +950,53 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
       float total = 0.0f;
       for (int c = 0; c < W; ++c) total = __fadd_rn(total, part[c]);
       rn = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps));
+    } else if constexpr (NORM == kNormLayer) {
+      // mean, then the biased variance around it, in the order of faq_layer_norm: per lane
+      // the four units u = (i + rot) & 3, even and odd channels in two running sums, an
+      // xor tree over the lanes, the chunks in order, each sum published and awaited
+      const uint4* src = reinterpret_cast<const uint4*>(in + static_cast<size_t>(ch) * 2048 + 64 * lane);
+      float2 xv[16];
+      float2 s2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = src[(i + rot) & 3];
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          xv[4 * i + h] = make_float2(__uint_as_float(wv[h] << 16), __uint_as_float(wv[h] & 0xFFFF0000u));
+          s2 = __fadd2_rn(s2, xv[4 * i + h]);
+        }
+      }
+      const float inv_k = __fdiv_rn(1.0f, static_cast<float>(k));
+      float* part = s_part + 32 * (it & 1);
+      float sum = __fadd_rn(s2.x, s2.y);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+      if (lane == 0) {
+        part[ch] = sum;
+        mbar_arrive(smem_addr(&normbar[it & 1]));
+      }
+      if (!mbar_wait_warp(smem_addr(&normbar[it & 1]), (it >> 1) & 1, 33, it)) break;
+      float total = 0.0f;
+      for (int c = 0; c < W; ++c) total = __fadd_rn(total, part[c]);
+      mu = __fmul_rn(total, inv_k);
+      float2 d2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 e = __ffma2_rn(make_float2(mu, mu), make_float2(-1.0f, -1.0f), xv[i]);
+        d2 = __fadd2_rn(d2, __fmul2_rn(e, e));
+      }
+      float dev = __fadd_rn(d2.x, d2.y);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dev = __fadd_rn(dev, __shfl_xor_sync(0xffffffffu, dev, off));
+      if (lane == 0) {
+        part[16 + ch] = dev;
+        mbar_arrive(smem_addr(&normbar[2 + (it & 1)]));
+      }
+      if (!mbar_wait_warp(smem_addr(&normbar[2 + (it & 1)]), (it >> 1) & 1, 34, it)) break;
+      float var = 0.0f;
+      for (int c = 0; c < W; ++c) var = __fadd_rn(var, part[16 + c]);
+      rn = rsqrtf(__fadd_rn(__fmul_rn(var, inv_k), eps));
     }
     float2 p[16];
 #pragma unroll
@@ -949,7 +1005,7 @@ __global__ void __launch_bounds__(MAXW * 32, kK1Warps / MAXW > 0 ? kK1Warps / MA
       const uint32_t m[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h)
-        p[4 * t8 + h] = v4_gathered2<NORM>(in, s_gamma, rn, m[h], input_scale);
+        p[4 * t8 + h] = v4_gathered2<NORM>(in, s_gamma, rn, mu, m[h], input_scale);
     }
     // stride 1: inside each float2 (the gathered values are consumed here)
 #pragma unroll
@@ -1216,7 +1272,7 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
       // one warp per 1024-chunk: barriers, map (2 B per channel), two row buffers, one
       // 32 x 34 float transpose scratch per warp
       const int W = static_cast<int>(k / 1024);
-      const size_t smem4 = v4_smem_bytes(k, false);
+      const size_t smem4 = v4_smem_bytes(k, kNormNone);
       if (smem4 <= 200 * 1024) {
         const int per_sm = std::max(1, std::min(16, static_cast<int>((227 * 1024) / (smem4 + 1024))));
         const int64_t blocks4 = std::min<int64_t>(rows, static_cast<int64_t>(sms) * per_sm);
@@ -1353,13 +1409,16 @@ extern "C" int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64
   return launch_quantize<float>(x, rows, k, ldx, input_scale, signs, perm, rot_block, levels, o, s);
 }
 
-extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
-                                          float eps, const void* input_scale, const int8_t* signs,
-                                          const int64_t* perm, int rot_block, int levels, uint32_t* meta, void* qdq,
-                                          int64_t ldq, void* stream) {
+namespace faq {
+// K1 v4 behind a fused norm (kNormRms with its weight, kNormLayer without one)
+template <int NORM>
+int quantize_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight, float eps,
+                  const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block, int levels,
+                  uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
   FAQ_CHECK_ARG(rows >= 0 && k > 0, "need rows >= 0 and k > 0");
   FAQ_CHECK_ARG(x != nullptr || rows == 0, "x is null");
-  FAQ_CHECK_ARG(norm_weight != nullptr && aligned16(norm_weight), "norm_weight must be non-null and 16-byte aligned");
+  FAQ_CHECK_ARG(NORM != kNormRms || (norm_weight != nullptr && aligned16(norm_weight)),
+                "norm_weight must be non-null and 16-byte aligned");
   FAQ_CHECK_ARG(eps >= 0.0f, "eps must be non-negative");
   FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
   FAQ_CHECK_ARG(qdq != nullptr || rows == 0, "the fused norm writes the QDQ operand: qdq is required");
@@ -1375,7 +1434,7 @@ extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k
   if (k % 1024 != 0 || k > 16384)
     return fail(FAQ_ERR_UNSUPPORTED, "the fused norm needs k a multiple of 1024, at most 16384");
   if (rows == 0) return FAQ_OK;
-  const size_t smem = v4_smem_bytes(k, true);
+  const size_t smem = v4_smem_bytes(k, NORM);
   if (smem > 200 * 1024) return fail(FAQ_ERR_UNSUPPORTED, "row too long for the fused norm's shared memory");
   int log2b = 0;
   while ((1 << log2b) < rot_block) ++log2b;
@@ -1387,13 +1446,13 @@ extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define FAQ_ROTN_LAUNCH(L, MW)                                                                                       \
   {                                                                                                                \
-    auto kern = hif4_rotate_v4_kernel<L, false, MW, true>;                                                          \
+    auto kern = hif4_rotate_v4_kernel<L, false, MW, NORM>;                                                          \
     FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));    \
     kern<<<static_cast<unsigned>(grid), W * 32, smem, st>>>(                                                       \
         static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                       \
         static_cast<const __nv_bfloat16*>(input_scale), signs, perm, levels, o,                                     \
         static_cast<const __nv_bfloat16*>(norm_weight), eps);                                                       \
-    return launch_status("hif4_rotate_v4_kernel (fused RMSNorm)");                                                 \
+    return launch_status("hif4_rotate_v4_kernel (fused norm)");                                                 \
   }
 #define FAQ_ROTN_CASE(L)                   \
   case L:                                  \
@@ -1414,6 +1473,23 @@ extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k
 #undef FAQ_ROTN_CASE
 #undef FAQ_ROTN_LAUNCH
   return fail(FAQ_ERR_UNSUPPORTED, "rot_block outside 32..1024");
+}
+}  // namespace faq
+
+extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
+                                          float eps, const void* input_scale, const int8_t* signs,
+                                          const int64_t* perm, int rot_block, int levels, uint32_t* meta, void* qdq,
+                                          int64_t ldq, void* stream) {
+  return faq::quantize_norm<faq::kNormRms>(x, rows, k, ldx, norm_weight, eps, input_scale, signs, perm, rot_block,
+                                           levels, meta, qdq, ldq, stream);
+}
+
+extern "C" int faq_hif4_quantize_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps,
+                                            const void* input_scale, const int8_t* signs, const int64_t* perm,
+                                            int rot_block, int levels, uint32_t* meta, void* qdq, int64_t ldq,
+                                            void* stream) {
+  return faq::quantize_norm<faq::kNormLayer>(x, rows, k, ldx, nullptr, eps, input_scale, signs, perm, rot_block,
+                                             levels, meta, qdq, ldq, stream);
 }
 
 extern "C" int faq_hif4_quantize_act(const void* x, int act, int64_t rows, int64_t k, int64_t ldx,

@@ -184,7 +184,7 @@ def rms_norm_quantize_supported(k: int, rot_block: int | None) -> bool:
 
 def hif4_quantize_rms_norm(
     x: torch.Tensor,
-    norm_weight: torch.Tensor,
+    norm_weight: torch.Tensor | None,
     eps: float,
     *,
     levels: str | int = "123",
@@ -197,7 +197,10 @@ def hif4_quantize_rms_norm(
     """:func:`hif4_quantize` of ``rms_norm(x, norm_weight, eps)`` in one pass
     (``faq_hif4_quantize_rms_norm``): the same bits as :func:`rms_norm` followed by
     :func:`hif4_quantize`, without the normalized tensor in memory. bf16 ``x [rows, k]``
-    with ``rms_norm_quantize_supported(k, rot_block)``; returns ``(qdq, meta)``."""
+    with ``rms_norm_quantize_supported(k, rot_block)``; returns ``(qdq, meta)``.
+    ``norm_weight=None`` takes the affine-free LayerNorm instead
+    (``faq_hif4_quantize_layer_norm``, the bits of :func:`layer_norm` then
+    :func:`hif4_quantize`)."""
     device = _require_cuda(x, norm_weight, input_scale, signs, permutation)
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise TypeError("hif4_quantize_rms_norm takes a rank-2 bfloat16 tensor")
@@ -207,15 +210,18 @@ def hif4_quantize_rms_norm(
     ldx = x.stride(0) if rows > 1 else k
     qdq = torch.empty((rows, k), dtype=torch.bfloat16, device=device)
     meta = torch.empty((rows, k // 64), dtype=torch.int32, device=device) if want_meta else None
-    norm_weight = norm_weight.to(device=device, dtype=torch.bfloat16).contiguous()
     if input_scale is not None:
         input_scale = input_scale.to(device=device, dtype=torch.bfloat16).contiguous()
     signs = signs.to(device=device, dtype=torch.int8).contiguous()
     if permutation is not None:
         permutation = permutation.to(device=device, dtype=torch.int64).contiguous()
-    _lib.call("faq_hif4_quantize_rms_norm", x.data_ptr(), rows, k, ldx, norm_weight.data_ptr(), float(eps),
-              _ptr(input_scale), signs.data_ptr(), _ptr(permutation), int(rot_block), levels_code(levels),
-              _ptr(meta), qdq.data_ptr(), k, _stream(device))
+    tail = (_ptr(input_scale), signs.data_ptr(), _ptr(permutation), int(rot_block), levels_code(levels), _ptr(meta),
+            qdq.data_ptr(), k, _stream(device))
+    if norm_weight is None:
+        _lib.call("faq_hif4_quantize_layer_norm", x.data_ptr(), rows, k, ldx, float(eps), *tail)
+    else:
+        norm_weight = norm_weight.to(device=device, dtype=torch.bfloat16).contiguous()
+        _lib.call("faq_hif4_quantize_rms_norm", x.data_ptr(), rows, k, ldx, norm_weight.data_ptr(), float(eps), *tail)
     return qdq, meta
 
 

@@ -152,16 +152,17 @@ class TPHiF4Linear(nn.Module):
             return ops.hif4_quantize_act(x, act, levels=self.levels, signs=r.signs, rot_block=r.block)[0]
         return self.quantize_input(ops.silu_mul(x) if act == "swiglu" else ops.gelu_tanh(x))
 
-    def norm_and_quantize(self, x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
-        """The input ``rms_norm(x, weight, eps)`` quantized: in one pass
-        (``ops.hif4_quantize_rms_norm``: the norm inside K1, nothing written between) for a
-        quantized projection with a rotation K1 v4 takes, else the norm kernel then
-        :meth:`quantize_input` -- the same values."""
+    def norm_and_quantize(self, x: torch.Tensor, weight: torch.Tensor | None, eps: float) -> torch.Tensor:
+        """The input ``rms_norm(x, weight, eps)`` (``weight=None``: ``layer_norm(x, eps)``)
+        quantized: in one pass (``ops.hif4_quantize_rms_norm``: the norm inside K1, nothing
+        written between) for a quantized projection with a rotation K1 v4 takes, else the
+        norm kernel then :meth:`quantize_input` -- the same values."""
         r = self.rotation
         if self.quantize and r.signs is not None and ops.rms_norm_quantize_supported(x.shape[-1], r.block):
             return ops.hif4_quantize_rms_norm(x, weight, eps, levels=self.levels, signs=r.signs,
                                               permutation=r.permutation, rot_block=r.block)[0]
-        return self.quantize_input(ops.rms_norm(x, weight, eps))
+        h = ops.layer_norm(x, eps) if weight is None else ops.rms_norm(x, weight, eps)
+        return self.quantize_input(h)
 
     def forward(self, x: torch.Tensor, *, quantized: bool = False, residual: torch.Tensor | None = None,
                 act: str | None = None, norm: tuple[torch.Tensor, float] | None = None) -> torch.Tensor:
@@ -539,8 +540,11 @@ class WanBlockTP(nn.Module):
         cfg, d, hl = self.cfg, self.cfg.head_dim, self.h_local
         seq = x.shape[0]
         tr = (lambda stage, t: (self.trace(stage, 0, t), t)[1]) if self.trace is not None else (lambda stage, t: t)
-        h = tr("norm1", ops.layer_norm(x, cfg.eps))
-        qkv = tr("qkv", self.qkv(h))
+        fuse = self.fuse_residual and self.trace is None  # norms in the readers' K1, residual adds in epilogues
+        if fuse:
+            qkv = self.qkv(x, norm=(None, cfg.eps))
+        else:
+            qkv = tr("qkv", self.qkv(tr("norm1", ops.layer_norm(x, cfg.eps))))
         n = hl * d
         # per-head sums of squares of q and k: [world, L, 2 hl] after the gather
         head_ss = self.tp.all_gather(ops.row_sumsq(qkv[:, :2 * n], segments=2 * hl))
@@ -552,10 +556,11 @@ class WanBlockTP(nn.Module):
         vd = tr("vd", ops.qk_prep(heads(2 * n), levels=cfg.levels, rotate=False)[0])
         att = tr("attention", ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=False, p_levels=cfg.levels,
                                                  quantized_normalizer=True))  # [1, L, hl, d]
-        fuse = self.fuse_residual and self.trace is None  # residual adds in the o / ffn.2 epilogues
         x = tr("x_mid", self.o(att.view(seq, n), residual=x) if fuse else x + tr("o", self.o(att.view(seq, n))))
-        h = tr("norm2", ops.layer_norm(x, cfg.eps))
-        f0 = tr("ffn0", self.ffn0(h))
+        if fuse:
+            f0 = self.ffn0(x, norm=(None, cfg.eps))
+        else:
+            f0 = tr("ffn0", self.ffn0(tr("norm2", ops.layer_norm(x, cfg.eps))))
         if fuse:  # the GELU in the ffn.2 input quantization, the residual add in its epilogue
             return self.ffn2(f0, act="gelu_tanh", residual=x)
         a = tr("act", ops.gelu_tanh(f0))

@@ -105,6 +105,17 @@ int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64
 int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
                                float eps, const void* input_scale, const int8_t* signs, const int64_t* perm,
                                int rot_block, int levels, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
+/*
+ * The same with the Wan DiT block's affine-free LayerNorm in front (norm1 -> qkv, norm2
+ * -> ffn.0; the rbhn_r64 readers): bf16((x - mean) * rsqrt(var + eps)), biased
+ * variance, summed in faq_layer_norm's order, so the same bits as faq_layer_norm then
+ * faq_hif4_quantize. Replaces WanLayerNorm (the reference's Wan checkout, elementwise_affine
+ * False) then HiF4Linear's input quantization (src/faquant/wan22_hif4.py:81-92). Same
+ * limits as faq_hif4_quantize_rms_norm.
+ */
+int faq_hif4_quantize_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps,
+                                 const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block,
+                                 int levels, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
 
 /*
  * faq_hif4_quantize of an activation's output, the activation fused into the load: `act`

@@ -132,7 +132,8 @@ def test_quantize_act_equals_activation_then_quantize(act: str, block: int, leve
 @pytest.mark.parametrize("k,block", [(1024, 1024), (4096, 1024), (5120, 1024), (5120, 64), (12288, 32), (16384, 1024)])
 def test_quantize_rms_norm_equals_norm_then_quantize(k: int, block: int) -> None:
     """faq_hif4_quantize_rms_norm (the decoder layer's RMSNorm inside K1) gives the bits of
-    faq_rms_norm followed by faq_hif4_quantize with the same HiSQ rotation: dequantized
+    faq_rms_norm followed by faq_hif4_quantize with the same HiSQ rotation, and
+    faq_hif4_quantize_layer_norm those of faq_layer_norm then faq_hif4_quantize: dequantized
     values and meta, ragged row counts, with and without input_scale, two level sets."""
     from faquant_b200 import ops
     from faquant_b200.hisq_rotation import derive_hisq_rotation
@@ -154,6 +155,14 @@ def test_quantize_rms_norm_equals_norm_then_quantize(k: int, block: int) -> None
                                          rot_block=block, want_codes=True)
         assert torch.equal(fused, qdq), (rows, levels)
         assert torch.equal(fmeta, meta), (rows, levels)
+        # the affine-free LayerNorm (norm_weight None), on values with an offset
+        xo = x + 0.75
+        fused, fmeta = ops.hif4_quantize_rms_norm(xo, None, 1e-6, levels=levels, input_scale=sc, signs=signs,
+                                                  permutation=perm, rot_block=block, want_meta=True)
+        qdq, _, meta = ops.hif4_quantize(ops.layer_norm(xo, 1e-6), levels=levels, input_scale=sc, signs=signs,
+                                         permutation=perm, rot_block=block, want_codes=True)
+        assert torch.equal(fused, qdq), ("layer", rows, levels)
+        assert torch.equal(fmeta, meta), ("layer", rows, levels)
     empty, _ = ops.hif4_quantize_rms_norm(torch.zeros(0, k, dtype=torch.bfloat16, device=DEV), w, 1e-6,
                                           signs=signs, permutation=perm, rot_block=block)
     assert empty.shape == (0, k)

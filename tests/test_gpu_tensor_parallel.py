@@ -189,11 +189,14 @@ def test_residual_adds_in_the_gemm_epilogue_are_the_same_bits() -> None:
         fused = model(ids)
         model.fuse_residual = False
         assert torch.equal(fused, model(ids)), cfg.hidden
-    block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
-    x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(DEV)
-    fused = block(x)
-    block.fuse_residual = False
-    assert torch.equal(fused, block(x))
+    # dim 1024 also takes the LayerNorms into the qkv / ffn.0 input quantization
+    for cfg in (_wan_cfg(), dataclasses.replace(_wan_cfg(), dim=1024, heads=8)):
+        block = WanBlockTP(cfg, TPGroup(), DEV)
+        x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(5))
+        x = x.to(torch.bfloat16).to(DEV)
+        fused = block(x)
+        block.fuse_residual = False
+        assert torch.equal(fused, block(x)), cfg.dim
 
 
 def test_wan_block_stages_match_the_oracle() -> None:
