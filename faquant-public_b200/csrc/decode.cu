@@ -634,26 +634,42 @@ extern "C" int faq_hif4_decode_attention(const void* q, const void* k, const voi
 // plans all of its memory at start-up and forbids allocations while it serves, or a host
 // hot path where cudaMalloc would synchronize the device. Instead of a caller workspace
 // the passes use one file-scope scratch array of FAQ_DECODE_STATIC_SCRATCH_BYTES
-// (16 MiB), which every GPU that loads this library holds until the process exits.
+// (16 MiB, include/faquant_b200.h), which every GPU that loads this library holds until
+// the process exits.
 //   - The kernels write every scratch word they read within the same call (scores and
 //     tile maxima in pass 1, partial results in pass 2), so nothing has to start at zero.
 //   - All calls on a device share the one array: calls that may overlap on that GPU
 //     (different streams without ordering between them) race; order them on one stream.
 //   - The array's device address is looked up (cudaGetSymbolAddress) on the first call on
 //     each device, with that device current, and cached; make that first call before
-//     any stream capture. No call allocates.
+//     any stream capture. The stream must belong to the current device (checked) and to
+//     its primary context, the one the runtime API uses. No call allocates through the
+//     library; under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default) the
+//     first call on a device is when the driver loads this module there, and that load
+//     is what places the array in device memory -- so make that first call at start-up.
 namespace faq {
 namespace dec {
-constexpr size_t STATIC_SCRATCH_BYTES = size_t(16) << 20;
+constexpr size_t STATIC_SCRATCH_BYTES = FAQ_DECODE_STATIC_SCRATCH_BYTES;
+static_assert(STATIC_SCRATCH_BYTES % 256 == 0, "the scratch array holds whole 256-byte units");
 static __device__ __align__(256) float g_static_scratch[STATIC_SCRATCH_BYTES / sizeof(float)];
 constexpr int MAX_DEVICES = 64;
 static float* g_static_scratch_ptr[MAX_DEVICES] = {};
 static std::mutex g_static_scratch_mutex;
 
-static int static_scratch(float** out) {
+static int static_scratch(void* stream, float** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+  if (stream != nullptr) {
+    // the cached address is this device's copy of the array: a stream of another device
+    // would run the kernels against memory that is not theirs
+    int stream_dev = -1;
+    err = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamGetDevice");
+    if (stream_dev != dev)
+      return fail(FAQ_ERR_ARG, "the stream belongs to device " + std::to_string(stream_dev) +
+                                   ", not to the current device " + std::to_string(dev));
+  }
   if (dev < 0 || dev >= MAX_DEVICES) return fail(FAQ_ERR_UNSUPPORTED, "device ordinal beyond 63");
   std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
   if (g_static_scratch_ptr[dev] == nullptr) {
@@ -685,7 +701,7 @@ extern "C" int faq_hif4_decode_attention_static(const void* q, const void* k, co
                                  " bytes of scratch, more than the 16 MiB static array of "
                                  "faq_hif4_decode_attention_static; use faq_hif4_decode_attention with a workspace");
   float* scratch = nullptr;
-  rc = dec::static_scratch(&scratch);
+  rc = dec::static_scratch(stream, &scratch);
   if (rc) return rc;
   return decode_launch(p, scratch, stream);
 }

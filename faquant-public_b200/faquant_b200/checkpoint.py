@@ -78,16 +78,18 @@ def check_receipt(checkpoint: str | Path, *, weight_levels: str = "123", act_lev
             raise ValueError(f"{checkpoint} has {artifact}; only step-0 initializations load without the QAT skeleton")
 
 
-def read_checkpoint(checkpoint: str | Path) -> tuple[dict[str, torch.Tensor], dict[str, dict[str, torch.Tensor]]]:
-    """``(state, metadata)``: every tensor of the shards listed by the index, with the HiF4
-    metadata leaves split off into ``metadata[module_name][field]``."""
+def iter_checkpoint_shards(checkpoint: str | Path, metadata: dict[str, dict[str, torch.Tensor]]):
+    """Yield the model tensors of one shard at a time (the shards listed by the index, in
+    order); the HiF4 metadata leaves are split off into ``metadata[module_name][field]``,
+    which the caller keeps across shards. Only one shard's tensors are alive at a time, as
+    in the reference's loader (qad_checkpoint.py:340-356), so the host peak is one shard
+    plus the small metadata, not the whole model."""
     from safetensors import safe_open
 
     checkpoint = Path(checkpoint)
     index = json.loads((checkpoint / "model.safetensors.index.json").read_text(encoding="utf-8"))
-    state: dict[str, torch.Tensor] = {}
-    metadata: dict[str, dict[str, torch.Tensor]] = {}
     for shard in sorted(set(index["weight_map"].values())):
+        state: dict[str, torch.Tensor] = {}
         with safe_open(str(checkpoint / shard), framework="pt", device="cpu") as tensors:
             for key in tensors.keys():
                 module_name, _, leaf = key.rpartition(".")
@@ -95,6 +97,18 @@ def read_checkpoint(checkpoint: str | Path) -> tuple[dict[str, torch.Tensor], di
                     metadata.setdefault(module_name, {})[HIF4_METADATA_LEAVES[leaf]] = tensors.get_tensor(key)
                 else:
                     state[key] = tensors.get_tensor(key)
+        yield state
+        del state
+
+
+def read_checkpoint(checkpoint: str | Path) -> tuple[dict[str, torch.Tensor], dict[str, dict[str, torch.Tensor]]]:
+    """``(state, metadata)``: every tensor of the shards listed by the index, with the HiF4
+    metadata leaves split off into ``metadata[module_name][field]`` (all shards at once;
+    the loader below goes shard by shard)."""
+    state: dict[str, torch.Tensor] = {}
+    metadata: dict[str, dict[str, torch.Tensor]] = {}
+    for shard_state in iter_checkpoint_shards(checkpoint, metadata):
+        state.update(shard_state)
     return state, metadata
 
 
@@ -110,12 +124,16 @@ def load_qad_inference_checkpoint(
     every weight against its metadata on the GPU (see the module docstring). With
     ``packed_out`` the packed weights are stored there by module name."""
     check_receipt(checkpoint, weight_levels=levels)
-    state, metadata = read_checkpoint(checkpoint)
     expected = set(model.state_dict())
-    result = model.load_state_dict(state, strict=False)
-    loaded = set(state)
-    unexpected = set(result.unexpected_keys)
-    del state
+    metadata: dict[str, dict[str, torch.Tensor]] = {}
+    loaded: set[str] = set()
+    unexpected: set[str] = set()
+    # one shard at a time: copy it into the model, then drop it before opening the next
+    for state in iter_checkpoint_shards(checkpoint, metadata):
+        result = model.load_state_dict(state, strict=False)
+        loaded.update(state)
+        unexpected.update(result.unexpected_keys)
+        del state, result
 
     max_abs, mismatches, linears = 0.0, 0, 0
     for name, module in model.named_modules():

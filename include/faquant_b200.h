@@ -301,12 +301,17 @@ int faq_hif4_decode_attention(const void* q, const void* k, const void* v, int64
  * allocate device memory (a runtime that plans all of its memory at start-up and forbids
  * allocations while serving; a host hot path where cudaMalloc would synchronize the
  * device). No counterpart in the reference: it is this library's allocation-free variant.
- * Its scratch is one 16 MiB file-scope device array that every GPU loading the library
- * holds until exit; problems whose faq_hif4_decode_workspace_bytes(...) exceeds 16 MiB
- * are rejected with FAQ_ERR_ARG. The array's address is looked up on the first call on
- * each device (make that call before any stream capture); nothing in it must start at
- * zero; calls that may overlap on one GPU share the array and race -- order them.
+ * Its scratch is one file-scope device array of FAQ_DECODE_STATIC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit; problems whose
+ * faq_hif4_decode_workspace_bytes(...) exceeds it are rejected with FAQ_ERR_ARG. The
+ * array's address is looked up on the first call on each device (make that call before
+ * any stream capture). Under lazy module loading (the CUDA default) that first call is
+ * also when the driver loads the library's module onto the device, which is what places
+ * the array in device memory: make it at start-up. `stream` must belong to the current
+ * device (FAQ_ERR_ARG otherwise) and to its primary context. Nothing in the array must
+ * start at zero; calls that may overlap on one GPU share the array and race -- order them.
  */
+#define FAQ_DECODE_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
 int faq_hif4_decode_attention_static(const void* q, const void* k, const void* v, int64_t batch,
                                      int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int d,
                                      int64_t qb, int64_t qh, int64_t qs, int64_t kb, int64_t kh,

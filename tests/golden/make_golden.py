@@ -42,7 +42,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF_SRC = Path(os.environ.get("FAQUANT_REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("FAQUANT_REFERENCE_SRC"):
+    raise SystemExit("set FAQUANT_REFERENCE_SRC to the reference checkout's src directory")
+REF_SRC = Path(os.environ["FAQUANT_REFERENCE_SRC"])
 sys.path.insert(0, str(REF_SRC))
 sys.path.insert(0, str(HERE))
 
