@@ -164,6 +164,10 @@ class FakeQuantLinear(nn.Module):
             self._gemm_weight = cached
         return cached
 
+    def dequantized_weight(self) -> torch.Tensor:
+        """The weight on the HiF4 grid as the GEMM sees it, in bf16 (exact)."""
+        return self._operand_weight()
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("faquant_b200.FakeQuantLinear runs on CUDA tensors only")

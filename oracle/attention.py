@@ -79,12 +79,22 @@ def attention(
     levels: dict[str, str] | None = None,
     return_f32: bool = False,
     operands_quantized: bool = False,
+    query_positions: np.ndarray | None = None,
+    full_queries: int | None = None,
 ) -> np.ndarray:
     """Tiled HiF4 attention; ``q [B,H,Sq,D]``, ``k/v [B,KV,Sk,D]`` -> ``[B,Sq,H,D]``.
 
     ``operands_quantized``: Q/K/V are already HiF4 operands (a kernel's K4 output) and
     are used as given (re-fitting HiF4 values is not idempotent); P is still quantized
-    when ``pv_quant``."""
+    when ``pv_quant``.
+
+    ``query_positions``: the position of each query row in the full query sequence of
+    ``n`` rows, whose causal offset is ``sk - n`` -- i.e. the key index of row i's
+    diagonal is ``query_positions[i] + sk - n``; pass ``n`` as ``full_queries``. Every
+    output row depends only on its own query and on all keys (the key tiling, the
+    running max and P's HiF4 groups are per row), so a subset of rows computed this way
+    equals those rows of the full computation; tests use it to check sampled rows of
+    sequences too long for the whole oracle."""
     if normalizer not in ("unquantized", "quantized_same"):
         raise ValueError(f"unsupported normalizer {normalizer!r}")
     lv = {"q": "123", "k": "123", "p": "123", "v": "123"}
@@ -104,7 +114,12 @@ def attention(
     ko = np.repeat(ko, rep, axis=1)
     vo = np.repeat(vo, rep, axis=1)
     out = np.zeros((b, h, sq, d), dtype=F32)
-    offset = sk - sq
+    if query_positions is None:
+        diag = np.arange(sq) + (sk - sq)
+    else:
+        diag = np.asarray(query_positions, dtype=np.int64) + (sk - full_queries)
+        if diag.shape != (sq,):
+            raise ValueError("query_positions needs one position per query row")
     for qs in range(0, sq, query_chunk):
         qe = min(qs + query_chunk, sq)
         rows = qe - qs
@@ -112,10 +127,10 @@ def attention(
         run_max = np.full((b, h, rows, 1), -np.inf, dtype=F32)
         denom = np.zeros((b, h, rows, 1), dtype=F32)
         acc = np.zeros((b, h, rows, d), dtype=F32)
-        qpos = np.arange(qs, qe) + offset
+        qpos = diag[qs:qe]
         for ks in range(0, sk, key_chunk):
             ke = min(ks + key_chunk, sk)
-            if causal and ks > qpos[-1]:
+            if causal and ks > qpos.max():
                 continue
             scores = (qt @ np.swapaxes(ko[:, :, ks:ke], -1, -2)).astype(F32) * scale
             if causal:

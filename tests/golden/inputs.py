@@ -76,3 +76,21 @@ def attention_inputs(b: int, h: int, kv: int, sq: int, sk: int, seed: int, d: in
     k = torch.randn(b, kv, sk, d, generator=g).to(torch.bfloat16)
     v = torch.randn(b, kv, sk, d, generator=g).to(torch.bfloat16)
     return q, k, v
+
+
+def config1_linear_inputs():
+    """BASELINE config 1's QuantLinear: X [2048, 4096] ~N(0,1) with 8 random channels x20
+    (bf16), W [4096, 4096] ~N(0, 0.02) (bf16), seeds 0 and 1."""
+    x = outlier_rows(2048, 4096, seed=0, outliers=8).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(1)
+    w = (torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    return x, w
+
+
+def c2_projection_inputs(tokens: int = 512):
+    """A config-2 projection (q_proj 4096 -> 4096): activations ~N(0,1) with 0.5 % outlier
+    channels x20 (20 of 4096), W ~N(0, 0.02), seeds 2 and 3."""
+    x = outlier_rows(tokens, 4096, seed=2, outliers=20).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(3)
+    w = (torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    return x, w

@@ -23,7 +23,23 @@ Fixtures (all ``.npz``):
   block 1024; three-level and, in a child process, two-level scales);
 - ``attention_*``: ``simulated_flash_attention_forward`` with HiF4 operands;
 - ``qk_prep``: the post-RoPE Q/K transform of ``qwen3._attention_forward``;
-- ``gptq``: a GPTQ HiF4 weight with its compact metadata.
+- ``gptq``: a GPTQ HiF4 weight with its compact metadata;
+- ``config1_attention``: BASELINE config 1's attention in full (B=1, 32/8 heads,
+  S=2048, causal, post-RoPE Hadamard, HiF4 Q/K/P/V, P-Reordering) through
+  ``simulated_flash_attention_forward``: sampled query rows of the output, the sum over
+  head_dim of every (query, head) and the simulator's geometry counters;
+- ``config1_linear`` (two-level, in a child process): BASELINE config 1's QuantLinear in
+  full (X [2048, 4096] with 8 outlier channels, W [4096, 4096], ``rbh_r64`` reader
+  rotation, RTN): the weight grid's SHA-256, sampled output rows and every row's sum;
+- ``c2_projection``: a config-2 projection (q_proj, HiSQ1024 seed 17, three-level) on
+  512 tokens, the same quantities.
+
+``wan_triton.npz`` comes from ``make_triton_golden.py`` instead: the reference's Triton
+kernel needs a GPU, so that script runs on a GPU box.
+
+Every sampled fixture stores rows picked at the start, the middle and the end of the
+tensor plus a regular stride, and a per-row sum of the whole tensor, so a test compares
+all rows through their sums and the sampled rows value by value.
 """
 
 from __future__ import annotations
@@ -52,6 +68,8 @@ from inputs import (  # noqa: E402
     ATTENTION_CASES,
     LINEAR_CASES,
     attention_inputs,
+    c2_projection_inputs,
+    config1_linear_inputs,
     linear_inputs,
     outlier_rows,
     sha,
@@ -259,9 +277,82 @@ def make_gptq() -> None:
          lv3=meta.scale_lv3_exponent.reshape(48, 4, 16).numpy())
 
 
+def sample_rows(n: int, edge: int, stride: int) -> np.ndarray:
+    """Rows at the start, the middle and the end of an n-row tensor plus every stride-th."""
+    mid = n // 2 - edge // 2
+    rows = set(range(edge)) | set(range(mid, mid + edge)) | set(range(n - edge, n)) | set(range(0, n, stride))
+    return np.array(sorted(rows), dtype=np.int64)
+
+
+def make_config1_attention() -> None:
+    from faquant.rotation import hadamard_transform
+    from faquant.simulated_flash_attention import simulated_flash_attention_forward
+
+    b, h, kv, s, d = 1, 32, 8, 2048, 128
+    q, k, v = attention_inputs(b, h, kv, s, s, seed=0)
+    # qwen3._attention_forward (qwen3.py:113-130): fp32 Hadamard over head_dim, one bf16 cast
+    qh = hadamard_transform(q.float()).to(torch.bfloat16)
+    kh = hadamard_transform(k.float()).to(torch.bfloat16)
+    module = _sim_module(True, "quantized_same", True, True)
+    with torch.no_grad():
+        out, _ = simulated_flash_attention_forward(module, qh, kh, v, None, scaling=d**-0.5)
+    rows = sample_rows(s, 64, 32)
+    save("config1_attention", in_sha=np.array(sha(q) + sha(k) + sha(v)), rows=rows,
+         out_rows=bits(out[0, rows]), head_sums=out[0].float().sum(dim=-1).numpy(),
+         stats=np.frombuffer(json.dumps(module.faquant_simulated_attention_stats).encode(), np.uint8))
+
+
+def _linear_fixture(name: str, x: torch.Tensor, w: torch.Tensor, rot, block: int, levels: str) -> None:
+    from faquant.hif4 import HIF4_ACT_SCALE_LEVELS, HIF4_SCALE_LEVELS
+    from faquant.quantization import FakeQuantLinear
+
+    assert HIF4_SCALE_LEVELS == levels and HIF4_ACT_SCALE_LEVELS == levels
+    lin = torch.nn.Linear(w.shape[1], w.shape[0], bias=False).to(torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    mod = FakeQuantLinear(lin, quant_format="hif4", bits=4, weight_group_size=64, activation_group_size=64,
+                          symmetric=True, clip_ratio=1.0, input_rotation_signs=rot.signs,
+                          input_rotation_permutation=rot.permutation, input_rotation_block_size=block)
+    with torch.no_grad():
+        y = mod(x)
+    rows = sample_rows(x.shape[0], 16, max(1, x.shape[0] // 32))
+    save(name, in_sha=np.array(sha(x) + sha(w)), rot_sha=np.array(sha(rot.signs) + sha(rot.permutation)),
+         wq_sha=np.array(sha(mod.weight.detach())), rows=rows, y_rows=bits(y[rows]),
+         row_sums=y.double().sum(dim=1).numpy(), levels=np.array(levels))
+
+
+def make_config1_linear(levels: str) -> None:
+    """Must run in a process whose FAQUANT_HIF4_SCALE_LEVELS equals ``levels`` (12)."""
+    from faquant.hisq_rotation import derive_hisq_rotation
+
+    x, w = config1_linear_inputs()
+    rot = derive_hisq_rotation("global_residual", 4096, seed=0, block_size=64)
+    _linear_fixture("config1_linear", x, w, rot, 64, levels)
+
+
+def make_c2_projection(levels: str) -> None:
+    from faquant.hisq_rotation import derive_hisq_rotation
+
+    x, w = c2_projection_inputs()
+    rot = derive_hisq_rotation("model.layers.0.self_attn.q_proj", 4096, seed=17, block_size=1024)
+    _linear_fixture("c2_projection", x, w, rot, 1024, levels)
+
+
 def main() -> None:
     if len(sys.argv) > 1 and sys.argv[1] == "--linear":
         make_linear(sys.argv[2])
+        return
+    if len(sys.argv) > 1 and sys.argv[1] == "--config1-linear":
+        make_config1_linear(sys.argv[2])
+        return
+    if len(sys.argv) > 1 and sys.argv[1] == "--baseline-sizes":
+        # the BASELINE-size fixtures alone (the others are unchanged by them)
+        torch.set_num_threads(min(8, os.cpu_count() or 1))
+        make_config1_attention()
+        make_c2_projection("123")
+        env = dict(os.environ, FAQUANT_HIF4_SCALE_LEVELS="12")
+        env.pop("FAQUANT_HIF4_ACT_SCALE_LEVELS", None)
+        subprocess.run([sys.executable, __file__, "--config1-linear", "12"], check=True, env=env)
         return
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     make_hif4_golden()
@@ -274,6 +365,11 @@ def main() -> None:
         env = dict(os.environ, FAQUANT_HIF4_SCALE_LEVELS=levels)
         env.pop("FAQUANT_HIF4_ACT_SCALE_LEVELS", None)
         subprocess.run([sys.executable, __file__, "--linear", levels], check=True, env=env)
+    make_config1_attention()
+    make_c2_projection("123")
+    env = dict(os.environ, FAQUANT_HIF4_SCALE_LEVELS="12")
+    env.pop("FAQUANT_HIF4_ACT_SCALE_LEVELS", None)
+    subprocess.run([sys.executable, __file__, "--config1-linear", "12"], check=True, env=env)
 
 
 if __name__ == "__main__":

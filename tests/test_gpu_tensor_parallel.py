@@ -53,6 +53,26 @@ def _wan_cfg():
     return WanBlockConfig(dim=512, heads=4, head_dim=128, ffn=1024, grid=(2, 6, 16))
 
 
+def _qwen_full_width_cfg():
+    """One Qwen3-32B layer at its full width (hidden 5120, 64/8 heads,
+    FFN 25600); one layer and a small vocabulary keep the oracle's host work in seconds."""
+    from faquant_b200.tensor_parallel import Qwen3TPConfig
+
+    return Qwen3TPConfig(layers=1, vocab=1000, bf16_layers=())
+
+
+def _wan_full_width_cfg():
+    """A Wan2.2-A14B block at its full width (dim 5120, 40 heads, FFN
+    13824) on a 1 x 4 x 64 latent grid (256 tokens)."""
+    from faquant_b200.tensor_parallel import WanBlockConfig
+
+    return WanBlockConfig(grid=(1, 4, 64))
+
+
+QWEN_CASES = [("small", _qwen_cfg, 2, 192), ("config5_full_width", _qwen_full_width_cfg, 1, 256)]
+WAN_CASES = [("small", _wan_cfg), ("config4_full_width", _wan_full_width_cfg)]
+
+
 def test_shards_reproduce_the_unsharded_projection() -> None:
     from faquant_b200.tensor_parallel import TPGroup, TPHiF4Linear, column_rotation, random_weight, row_rotation
 
@@ -130,18 +150,21 @@ def _mostly_equal(got: np.ndarray, ref: np.ndarray) -> None:
     assert np.mean(got == ref) >= 0.995 and _rel(got, ref) <= 2e-2
 
 
-def test_qwen3_prefill_stages_match_the_oracle() -> None:
-    """Every stage of a 2-layer prefill (one HiF4 layer, one bf16 layer) against the
-    reference's torch glue and the oracle, each applied to that stage's own GPU input:
-    the RMSNorms, the W4A4 projections (K1 + GEMM), the fused q/k norm + RoPE + Hadamard
-    + HiF4 (K4), the HiF4 attention (K5), SwiGLU and the logits."""
+@pytest.mark.parametrize("case", QWEN_CASES, ids=[c[0] for c in QWEN_CASES])
+def test_qwen3_prefill_stages_match_the_oracle(case) -> None:
+    """Every stage of a prefill against the reference's torch glue and the oracle, each
+    applied to that stage's own GPU input: the RMSNorms, the W4A4 projections (K1 +
+    GEMM), the fused q/k norm + RoPE + Hadamard + HiF4 (K4), the HiF4 attention (K5),
+    SwiGLU and the logits. Two shapes: a 2-layer model (one HiF4 layer, one bf16 layer)
+    at a small width, and one Qwen3-32B layer at its full width."""
     from faquant_b200.tensor_parallel import (Qwen3TPPrefill, TPGroup, apply_rope, default_input_ids, rms_norm,
                                               rope_tables)
 
-    model = Qwen3TPPrefill(_qwen_cfg(), TPGroup(), DEV)
+    _, make_cfg, batch, seq = case
+    model = Qwen3TPPrefill(make_cfg(), TPGroup(), DEV)
     cfg, d = model.cfg, model.cfg.head_dim
     tr = _traced(model)
-    ids = default_input_ids(2, 192, cfg.vocab, DEV, seed=3)
+    ids = default_input_ids(batch, seq, cfg.vocab, DEV, seed=3)
     logits = model(ids).cpu().numpy()
     b, s = ids.shape
     cos, sin = rope_tables(s, d, cfg.rope_theta, torch.device("cpu"))
@@ -172,7 +195,7 @@ def test_qwen3_prefill_stages_match_the_oracle() -> None:
         _close_linear(tr[("down", i)].numpy(), _oracle_linear(tr[("act", i)].numpy(), L.down, quant))
     final = bf(tr[("final", len(model.layers))])
     ref = torch.nn.functional.linear(rms_norm(final, model.final_norm.cpu(), cfg.eps), model.lm_head.cpu())
-    assert logits.shape == (2, cfg.vocab) and _rel(logits, ref.float().numpy()) <= 1e-2
+    assert logits.shape == (batch, cfg.vocab) and _rel(logits, ref.float().numpy()) <= 1e-2
 
 
 def test_residual_adds_in_the_gemm_epilogue_are_the_same_bits() -> None:
@@ -199,13 +222,15 @@ def test_residual_adds_in_the_gemm_epilogue_are_the_same_bits() -> None:
         assert torch.equal(fused, block(x)), cfg.dim
 
 
-def test_wan_block_stages_match_the_oracle() -> None:
+@pytest.mark.parametrize("case", WAN_CASES, ids=[c[0] for c in WAN_CASES])
+def test_wan_block_stages_match_the_oracle(case) -> None:
     """Every stage of a Wan2.2 block at TP 1 against the reference's torch glue and the
     oracle: the LayerNorms, the W4A4 projections, the fused q/k RMSNorm over all heads +
-    3-D RoPE (fp64) + Hadamard + HiF4 (K4), V's HiF4, the attention and the GELU."""
+    3-D RoPE (fp64) + Hadamard + HiF4 (K4), V's HiF4, the attention and the GELU; at a
+    small width and at the full Wan2.2-A14B width."""
     from faquant_b200.tensor_parallel import TPGroup, WanBlockTP, apply_rope3d, wan_qk_norm
 
-    block = WanBlockTP(_wan_cfg(), TPGroup(), DEV)
+    block = WanBlockTP(case[1](), TPGroup(), DEV)
     cfg, d, hl = block.cfg, block.cfg.head_dim, block.h_local
     tr = _traced(block)
     x = torch.randn(cfg.seq, cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
