@@ -10,9 +10,11 @@ copied out every step. The attention hot path (causal GQA
 32/8 heads, S = 32768) is measured in the same run and reported under
 ``attention``.
 
-``--impl reference`` times the reference algorithm on the host CPU instead: the
-numpy restatement in ``oracle/`` (the reference is PyTorch code that cannot be
-shipped to the GPU box), on a bounded sample of the same workload.
+``--impl reference`` times the reference's own CPU path on the host instead: its
+``FakeQuantLinear`` in CPU torch on all host threads when the reference is importable
+(an offline install under ``baseline/_ref``), else ``oracle/linear_torch.py``, a CPU-torch
+restatement with the same bits and cost; a step is 1024 of the 8192 tokens through all
+seven projections.
 
 Launch: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 under
 ``torch.distributed.run`` (one process per GPU, replicas: the linear set does not
@@ -58,6 +60,14 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 def linear_flops(tokens: int = T_TOKENS, out_frac: float = 1.0) -> float:
     return sum(2.0 * tokens * k * int(n * out_frac) for _, k, n in PROJECTIONS)
+
+
+def bench_config(world: int) -> dict:
+    """The workload both arms report (the reference arm times a bounded sample of it)."""
+    return {"workload": "qwen3-8b W4A4 linear set, T=8192 (BASELINE config 2)", "tokens": T_TOKENS,
+            "projections": [p for p, _, _ in PROJECTIONS], "rotation": "hisq1024 (seed 17)",
+            "levels": "123", "weights": "RTN HiF4 of N(0,0.02)", "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (512 MB activations + 436 MB weights per step)"}
 
 
 def peaks() -> tuple[dict, str]:
@@ -245,50 +255,107 @@ def flush_l2(buf):
     buf.add_(1.0)
 
 
-# ------------------------------------------------------------------ CPU legs (oracle)
-def cpu_linear_sample(tokens: int, out_frac: float, seed: int = 0):
-    """Inputs of the bounded CPU sample: `tokens` rows and a fraction of the output
-    channels of every projection; weights quantized by the oracle (setup)."""
-    import numpy as np
+# ------------------------------------------------------------------ CPU legs (reference path)
+REF_DIR = ROOT / "baseline" / "_ref"
 
-    from faquant_b200.hisq_rotation import derive_hisq_rotation
-    from oracle import hif4 as oh
 
-    rng = np.random.default_rng(seed)
-    sample = []
+def _import_reference():
+    """The reference's own modules from an offline install under baseline/_ref, or None."""
+    if not (REF_DIR / "faquant").is_dir():
+        return None
+    sys.path.insert(0, str(REF_DIR))
+    try:
+        import faquant.hisq_rotation as hr
+        import faquant.quantization as q
+    except Exception:  # noqa: BLE001 - an unusable install falls back to the port
+        return None
+    return hr, q
+
+
+def cpu_linear_set(tokens: int, seed: int = 0):
+    """The seven config-2 projections on `tokens` rows (full K and N) as CPU forwards.
+
+    With the reference importable, each forward is the reference's own
+    ``FakeQuantLinear`` (src/faquant/quantization.py:199-277) built as its module does
+    (RTN weight at construction, not timed); otherwise the CPU-torch restatement
+    ``oracle/linear_torch.py``, which gives the same bits and, measured against the
+    reference on 8 cores, 0.93-1.09x its time. Returns (kind, [(x, forward)]).
+    """
+    import torch
+
+    from oracle import linear_torch as lt
+
+    ref = _import_reference()
+    g = torch.Generator().manual_seed(seed)
+    out = []
     for path, k, n in PROJECTIONS:
-        x = rng.standard_normal((tokens, k), dtype=np.float32)
-        x[:, rng.choice(k, max(1, round(0.005 * k)), replace=False)] *= 20.0
-        x = oh.bf16_round(x)
-        ns = int(n * out_frac)
-        w = oh.bf16_round(rng.standard_normal((ns, k), dtype=np.float32) * np.float32(0.02))
-        wq = oh.fake_quantize(w, "123")
-        rot = derive_hisq_rotation(f"model.layers.0.{path}", k, seed=17, block_size=1024)
-        sample.append((x, wq, rot.signs.numpy(), rot.permutation.numpy()))
-    return sample
+        x = torch.randn(tokens, k, generator=g)
+        x[:, torch.randperm(k, generator=g)[: max(1, round(0.005 * k))]] *= 20.0
+        x = x.to(torch.bfloat16)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        name = f"model.layers.0.{path}"
+        if ref is not None:
+            hr, q = ref
+            rot = hr.derive_hisq_rotation(name, k, seed=17, block_size=1024)
+            lin = torch.nn.Linear(k, n, bias=False).to(torch.bfloat16)
+            with torch.no_grad():
+                lin.weight.copy_(w)
+            mod = q.FakeQuantLinear(lin, quant_format="hif4", bits=4, weight_group_size=64, activation_group_size=64,
+                                    symmetric=True, clip_ratio=1.0, input_rotation_signs=rot.signs,
+                                    input_rotation_permutation=rot.permutation, input_rotation_block_size=1024)
+            out.append((x, mod))
+        else:
+            from faquant_b200.hisq_rotation import derive_hisq_rotation
+
+            rot = derive_hisq_rotation(name, k, seed=17, block_size=1024)
+            wq = lt.hif4_fake_quantize(w, "123")
+
+            def fwd(xx, wq=wq, rot=rot):
+                return lt.fake_quant_linear(xx, wq, None, levels="123", signs=rot.signs, permutation=rot.permutation,
+                                            block=1024)
+
+            out.append((x, fwd))
+        del w
+    return ("reference" if ref is not None else "port"), out
 
 
-def cpu_linear_step(sample):
-    from oracle import linear as olin
+def cpu_linear_step(linears) -> None:
+    import torch
 
-    for x, wq, signs, perm in sample:
-        olin.fake_quant_linear(x, wq, None, levels="123", signs=signs, permutation=perm, block=1024)
+    with torch.no_grad():
+        for x, fwd in linears:
+            fwd(x)
 
 
-def cpu_baseline(tokens: int = 1024, out_frac: float = 0.25, steps: int = 2) -> dict:
-    sample = cpu_linear_sample(tokens, out_frac)
-    cpu_linear_step(sample)  # warm-up
+def cpu_threads() -> int:
+    import torch
+
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return n
+
+
+def cpu_sample_text(kind: str, tokens: int, threads: int, steps: int, warmup: int) -> str:
+    what = ("the reference's own FakeQuantLinear (src/faquant/quantization.py:199-277, imported from "
+            "baseline/_ref)" if kind == "reference" else
+            "oracle/linear_torch.py, the CPU-torch restatement of the reference's FakeQuantLinear (same bits; "
+            "0.93-1.09x the reference's time on 8 cores)")
+    return (f"{tokens} of the 8192 tokens through all 7 projections (full K and N): HiSQ1024 rotation, three-level "
+            f"HiF4 and the bf16 F.linear of {what}, CPU torch on {threads} threads, {steps} steps after {warmup} "
+            f"warm-up")
+
+
+def cpu_baseline(tokens: int = 1024, steps: int = 2) -> dict:
+    threads = cpu_threads()
+    kind, linears = cpu_linear_set(tokens)
+    cpu_linear_step(linears)  # warm-up
     t0 = time.perf_counter()
     for _ in range(steps):
-        cpu_linear_step(sample)
+        cpu_linear_step(linears)
     dt = (time.perf_counter() - t0) / steps
-    flops = linear_flops(tokens, out_frac)
     return {
-        "value": flops / dt / 1e12, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
-        "sample": f"{tokens} tokens x {int(out_frac * 100)}% of the output channels of each of the 7 projections "
-                  f"(full K), HiSQ1024 rotation + three-level HiF4 + fp32 GEMM in numpy (BLAS on all cores, "
-                  f"elementwise single-threaded), {steps} steps after 1 warm-up",
-        "seconds_per_step": dt,
+        "value": linear_flops(tokens) / dt / 1e12, "unit": "TFLOPS", "cores": threads, "kind": kind,
+        "sample": cpu_sample_text(kind, tokens, threads, steps, 1), "seconds_per_step": dt,
     }
 
 
@@ -296,25 +363,23 @@ def reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if world > 1 and rank != 0:
         return
-    import numpy as np  # noqa: F401
-
-    tokens, frac = 1024, 0.25
-    sample = cpu_linear_sample(tokens, frac)
+    tokens = 1024
+    threads = cpu_threads()
+    kind, linears = cpu_linear_set(tokens)
     for _ in range(args.warmup):
-        cpu_linear_step(sample)
+        cpu_linear_step(linears)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_linear_step(sample)
+        cpu_linear_step(linears)
     dt = (time.perf_counter() - t0) / args.steps
-    value = linear_flops(tokens, frac) / dt / 1e12
+    value = linear_flops(tokens) / dt / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "qwen3-8b linear set (BASELINE config 2), bounded CPU sample",
-                   "tokens": tokens, "out_channel_fraction": frac, "rotation": "hisq1024", "levels": "123"},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{tokens} tokens x {int(frac * 100)}% of each projection's output channels"},
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": bench_config(world),
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": kind,
+                         "sample": cpu_sample_text(kind, tokens, threads, args.steps, args.warmup)},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -407,6 +472,11 @@ def main_arm(args) -> None:
             "tokens_per_s": ATT["seq"] * ATT["batch"] / (a_ms * 1e-3),
             "gpu_launches_per_step": launches_att,
         }
+
+    # ---------------- the reference's own GPU kernel beside K5 (config 4 attention), rank 0
+    gpu_ref = None
+    if A is not None and rank == 0 and not args.no_gpu_reference:
+        gpu_ref = gpu_reference_attention(2)
 
     # ---------------- decode step (K6): one new token per sequence against a 32K-key cache
     dec = None
@@ -511,10 +581,7 @@ def main_arm(args) -> None:
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "qwen3-8b W4A4 linear set, T=8192 (BASELINE config 2)", "tokens": T_TOKENS,
-                       "projections": [p for p, _, _ in PROJECTIONS], "rotation": "hisq1024 (seed 17)",
-                       "levels": "123", "weights": "RTN HiF4 of N(0,0.02)", "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2 (512 MB activations + 436 MB weights per step)"},
+            "config": bench_config(world),
             "tokens_per_s": T_TOKENS * world / (ms_max * 1e-3),
             "roofline": {
                 "kernel": "gemm_bf16_tn_pair_kernel", "bound": "tensor", "achieved": gemm_tflops,
@@ -532,6 +599,7 @@ def main_arm(args) -> None:
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "attention": att,
+            "gpu_reference": gpu_ref,
             "decode": dec,
             **tp_lines,
             "e2e": e2e,
@@ -691,25 +759,27 @@ def kernel_case(name: str, reps: int) -> None:
     print(json.dumps({"kernel_case": name, "reps": reps, "ok": True}))
 
 
-def gpu_reference_attention(reps: int) -> None:
-    """The reference's own Triton attention (`wan22_attention.hif4_attention`, installed
-    under baseline/_ref by pip from the reference checkout) against K5 on BASELINE config 4
-    (Wan2.2: 75 600 tokens, 40 heads, non-causal, HiF4 P, P-Reordering), the same
-    HiF4-prepared operands for both, on this GPU. Prints one JSON line."""
+def gpu_reference_attention(reps: int) -> dict:
+    """The reference's own GPU kernel -- its Triton HiF4 attention
+    (`wan22_attention.hif4_attention`, src/faquant/wan22_attention.py:165-183) -- against K5
+    on BASELINE config 4 (Wan2.2: 75 600 tokens, 40 heads, non-causal, HiF4 P,
+    P-Reordering), the same HiF4-prepared operands for both, on this GPU. The reference is
+    imported from an offline install under baseline/_ref; without it the block says
+    `unavailable` and why."""
     import importlib
 
     import torch
 
-    ref_dir = Path(__file__).resolve().with_name("baseline") / "_ref"
     try:
-        sys.path.insert(0, str(ref_dir))
+        if not (REF_DIR / "faquant").is_dir():
+            raise ImportError(f"no reference install under {REF_DIR.relative_to(ROOT)}")
+        sys.path.insert(0, str(REF_DIR))
         ref = importlib.import_module("faquant.wan22_attention")
     except Exception as e:  # noqa: BLE001 - the install is optional
-        print(json.dumps({"gpu_reference": "unavailable", "why": f"{type(e).__name__}: {e}"[:200]}))
-        return
+        return {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     from faquant_b200 import ops
 
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", torch.cuda.current_device())
     seq, heads, d = 75600, 40, 128
     g = torch.Generator(device=dev).manual_seed(0)
     prep = [ops.qk_prep(torch.randn(1, heads, seq, d, device=dev, generator=g).to(torch.bfloat16), levels="123",
@@ -733,11 +803,14 @@ def gpu_reference_attention(reps: int) -> None:
                                                      quantized_normalizer=True))
     flops = 4.0 * d * heads * seq * seq
     a, b = o_our[0].float(), o_ref.float()
-    print(json.dumps({"gpu_reference": "triton hif4_attention (wan22_attention.py:165-183)",
-                      "workload": "BASELINE config 4 attention: 75600 tokens, 40 heads, d 128, non-causal",
-                      "reference_ms": ms_ref, "reference_tflops": flops / ms_ref / 1e9, "ours_ms": ms_our,
-                      "ours_tflops": flops / ms_our / 1e9, "speedup": ms_ref / ms_our,
-                      "rel_fro_diff": float((a - b).norm() / b.norm()), "reps": reps}))
+    result = {"kernel": "triton hif4_attention (wan22_attention.py:165-183)",
+              "workload": "BASELINE config 4 attention: 75600 tokens, 40 heads, d 128, non-causal",
+              "reference_ms": ms_ref, "reference_tflops": flops / ms_ref / 1e9, "ours_ms": ms_our,
+              "ours_tflops": flops / ms_our / 1e9, "speedup": ms_ref / ms_our,
+              "rel_fro_diff": float((a - b).norm() / b.norm()), "reps": reps}
+    del prep, views, o_ref, o_our, a, b
+    torch.cuda.empty_cache()
+    return result
 
 
 def main() -> None:
@@ -750,6 +823,8 @@ def main() -> None:
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true",
+                    help="skip timing the reference's Triton attention beside K5")
     ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
     ap.add_argument("--tp-steps", type=int, default=2)
     ap.add_argument("--qwen-layers", type=int, default=64)
@@ -760,7 +835,7 @@ def main() -> None:
                     help="time the reference's Triton attention (baseline/_ref) beside K5 on config 4 and exit")
     args = ap.parse_args()
     if args.gpu_reference:
-        gpu_reference_attention(args.reps)
+        print(json.dumps({"gpu_reference": gpu_reference_attention(args.reps)}))
         return
     if args.kernel_case:
         kernel_case(args.kernel_case, args.reps)
