@@ -128,6 +128,61 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
+// try_wait that lets the hardware suspend the thread for up to `suspend_ns` while the
+// phase is incomplete (it resumes when the phase completes): for warps that wait often and
+// long, so that their polling does not take issue slots from the warps doing work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return done != 0;
+}
+// Warp-uniform bounded wait (as mbar_wait_warp) built on mbar_try_wait_suspend.
+__device__ __forceinline__ bool mbar_wait_warp_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns, int site,
+                                                       int tile) {
+  bool ok = mbar_try_wait_suspend(bar, parity, suspend_ns);
+  if (!__all_sync(0xffffffffu, ok)) {
+    const uint64_t start = globaltimer();
+    while (!ok) {
+      ok = mbar_try_wait_suspend(bar, parity, suspend_ns);
+      if (!ok && globaltimer() - start > kWaitLimitNs) break;
+    }
+    if (!ok) report_timeout();
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && (threadIdx.x & 31) == 0) trace_timeout(site, tile);
+  }
+  return ok;
+}
+
+// try_wait with acquire at cluster scope: for phases completed by arrivals from the other
+// CTA of a pair (release.cluster), whose shared-memory writes the waiter then relies on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_site(uint32_t bar, uint32_t parity, int site, int tile) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (globaltimer() - start > kWaitLimitNs) {
+      report_timeout();
+      trace_timeout(site, tile);
+      return false;
+    }
+  }
+}
+
 // Wait for the phase of parity `parity` to complete, for at most `limit_ns`.
 // Returns false (and records FAQ_STATUS_TIMEOUT) when the limit runs out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,

@@ -1266,8 +1266,9 @@ static int launch_quantize(const void* x, int64_t rows, int64_t k, int64_t ldx, 
 #undef FAQ_ROTS_CASE
   }
   if constexpr (sizeof(T) == 2) {
-    const bool v4 = k % 1024 == 0 && k <= 16384 && x_vec && block >= 32 && block <= 1024 && o.qdq_vec &&
-                    (o.codes == nullptr || aligned16(o.codes)) && o.ldq % 8 == 0;
+    const bool v4 = k % 1024 == 0 && k <= 16384 && x_vec && block >= 32 && block <= 1024 &&
+                    (o.qdq == nullptr || (o.qdq_vec && o.ldq % 8 == 0)) &&
+                    (o.codes == nullptr || aligned16(o.codes));
     if (v4) {
       // one warp per 1024-chunk: barriers, map (2 B per channel), two row buffers, one
       // 32 x 34 float transpose scratch per warp

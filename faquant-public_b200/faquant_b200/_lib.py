@@ -42,6 +42,10 @@ SIGNATURES: dict[str, list] = {
                          _c_void_p],
     "faq_gemm_bf16_tn_residual": [_c_void_p, _i64, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p,
                                   _i64, _c_void_p, _i64, _c_void_p],
+    "faq_w4a4_gemm": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64,
+                      _c_void_p, _i64, _c_void_p],
+    "faq_w4a4_gemm_qdq_a": [_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64,
+                            _c_void_p, _i64, _c_void_p],
     "faq_qk_prep": [_c_void_p, _int, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _int,
                     _int, _int, _c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
     "faq_qk_norm_rope_prep": [_c_void_p, _int, _i64, _i64, _i64, _int, _i64, _i64, _i64, _c_void_p,

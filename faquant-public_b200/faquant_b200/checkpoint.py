@@ -119,10 +119,13 @@ def load_qad_inference_checkpoint(
     *,
     levels: str = "123",
     packed_out: dict[str, PackedHiF4Weight] | None = None,
+    pack: bool = False,
 ) -> QADInferenceLoadStats:
     """Load a step-0 QAD checkpoint into ``model``'s ``FakeQuantLinear`` modules and verify
     every weight against its metadata on the GPU (see the module docstring). With
-    ``packed_out`` the packed weights are stored there by module name."""
+    ``packed_out`` the packed weights are stored there by module name; with ``pack`` every
+    exactly packed weight replaces the module's bf16 weight (``FakeQuantLinear.use_packed``),
+    so the model keeps 4.5 bits per weight in HBM."""
     check_receipt(checkpoint, weight_levels=levels)
     expected = set(model.state_dict())
     metadata: dict[str, dict[str, torch.Tensor]] = {}
@@ -163,6 +166,8 @@ def load_qad_inference_checkpoint(
         linears += 1
         if packed_out is not None:
             packed_out[name] = PackedHiF4Weight(codes=codes, meta=meta, in_features=k)
+        if pack and bad == 0 and k % 256 == 0:
+            module.use_packed(codes, meta)
     if metadata:
         raise RuntimeError(f"HiF4 metadata for modules that are not quantized: {sorted(metadata)[:4]}")
     return QADInferenceLoadStats(linears=linears, requantized_max_abs=max_abs,

@@ -301,6 +301,58 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None
     return out
 
 
+def w4a4_gemm(a: torch.Tensor | tuple[torch.Tensor, torch.Tensor], b_codes: torch.Tensor, b_meta: torch.Tensor,
+              bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              residual: torch.Tensor | None = None) -> torch.Tensor:
+    """The W4A4 GEMM on a packed HiF4 weight ``(b_codes uint8 [n, k/2], b_meta int32
+    [n, k/64])``: ``deq(a) @ deq(b)^T (+ bias) (+ residual)`` in bf16, bit-identical to
+    ``gemm_bf16`` on the dequantized operands. ``a`` is the activation's packed form
+    ``(codes, meta)`` (``hif4_quantize(..., want_codes=True)``) or its bf16 QDQ ``[m, k]``.
+    ``k`` must be a multiple of 256 (``NotImplementedError`` otherwise)."""
+    device = _require_cuda(b_codes, b_meta, bias, residual)
+    if b_codes.dtype != torch.uint8 or b_meta.dtype not in (torch.int32, torch.uint32):
+        raise TypeError("packed weight: codes uint8 [n, k/2], meta int32 [n, k/64]")
+    n = b_codes.shape[0]
+    k = b_codes.shape[1] * 2
+    if b_meta.shape != (n, k // 64):
+        raise ValueError("packed weight: meta must be [n, k/64]")
+    b_codes, b_meta = b_codes.contiguous(), b_meta.contiguous()
+    packed_a = isinstance(a, tuple)
+    if packed_a:
+        a_codes, a_meta = (t.contiguous() for t in a)
+        _require_cuda(a_codes, a_meta)
+        m = a_codes.shape[0]
+        if a_codes.dtype != torch.uint8 or a_codes.shape[1] * 2 != k or a_meta.shape != (m, k // 64):
+            raise ValueError("packed activation: codes uint8 [m, k/2] and meta [m, k/64] with the weight's k")
+    else:
+        _require_cuda(a)
+        if a.dtype != torch.bfloat16 or a.shape[-1] != k:
+            raise ValueError("the QDQ activation must be bfloat16 [m, k] with the weight's k")
+        if a.stride(-1) != 1 or a.stride(0) % 8 or a.data_ptr() % 16:
+            a = a.contiguous()
+        m = a.shape[0]
+    if bias is not None:
+        bias = bias.to(device=device, dtype=torch.bfloat16).contiguous()
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+    ldr = 0
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or residual.shape != (m, n):
+            raise ValueError("residual must be bfloat16 [m, n]")
+        if residual.stride(-1) != 1:
+            residual = residual.contiguous()
+        ldr = residual.stride(0) if m > 1 else n
+    ldy = out.stride(0) if m > 1 else n
+    if packed_a:
+        _lib.call("faq_w4a4_gemm", a_codes.data_ptr(), a_meta.data_ptr(), b_codes.data_ptr(), b_meta.data_ptr(),
+                  m, n, k, _ptr(bias), _ptr(residual), ldr, out.data_ptr(), ldy, _stream(device))
+    else:
+        lda = a.stride(0) if m > 1 else k
+        _lib.call("faq_w4a4_gemm_qdq_a", a.data_ptr(), lda, b_codes.data_ptr(), b_meta.data_ptr(), m, n, k,
+                  _ptr(bias), _ptr(residual), ldr, out.data_ptr(), ldy, _stream(device))
+    return out
+
+
 def selftest_wait_timeout(limit_ns: int) -> None:
     device = torch.device("cuda", torch.cuda.current_device())
     _lib.call("faq_selftest_wait_timeout", int(limit_ns), _stream(device))

@@ -6,7 +6,12 @@ Mirrors ``src/faquant/quantization.py``: ``fake_quantize`` (:30-94),
 ``quantize_qwen3_linears`` (:378-408). The forward pass is two launches of the
 C-ABI library: K1 (input scale, HiSQ signs/permutation/block Hadamard, HiF4
 quantization, bit-exact with the reference) and K3 (tcgen05 GEMM on the
-exactly-dequantized bf16 operands). Only ``quant_format="hif4"`` is implemented;
+exactly-dequantized bf16 operands). With packed weights (``packed_weights=True``, or
+``FAQ_PACKED_WEIGHTS=1`` in the environment for modules built through the reference's
+installers) the module holds only the 4.5-bit packed weight, K1 writes the activation's
+packed codes and the GEMM expands both operands in shared memory
+(``faq_w4a4_gemm``): the same output bits, a quarter of the weight bytes in HBM.
+Only ``quant_format="hif4"`` is implemented;
 every other format, and the QAD-only clamp/companding knobs, raise
 ``NotImplementedError`` -- there is no CPU fallback.
 """
@@ -16,9 +21,15 @@ from __future__ import annotations
 import torch
 from torch import nn
 
+import os
+
 from . import ops
 
 HIF4_BLOCK_SIZE = 64
+
+
+def _packed_weights_default() -> bool:
+    return os.environ.get("FAQ_PACKED_WEIGHTS", "0") == "1"
 
 
 def _is_pow2(n: int) -> bool:
@@ -84,6 +95,7 @@ class FakeQuantLinear(nn.Module):
         activation_min: float | None = None,
         activation_max: float | None = None,
         activation_compand_log_scale: torch.Tensor | None = None,
+        packed_weights: bool | None = None,
     ) -> None:
         super().__init__()
         if quant_format != "hif4":
@@ -122,18 +134,113 @@ class FakeQuantLinear(nn.Module):
             None if activation_compand_log_scale is None else activation_compand_log_scale.detach().float().clone(),
         )
         weight = linear.weight.detach() if weight_override is None else weight_override.detach()
-        if quantize_weight:
-            weight = _quantize_weight_on_device(weight, ops.default_levels("weight"))
-        weight = weight.to(dtype=linear.weight.dtype)
-        with torch.inference_mode(False):
-            weight = weight.detach().clone()
-        self.weight = nn.Parameter(weight, requires_grad=False)
+        self._gemm_weight: torch.Tensor | None = None
+        # packed weight (non-persistent: the state_dict keeps the reference's bf16 `weight`)
+        self.register_buffer("weight_codes", None, persistent=False)
+        self.register_buffer("weight_meta", None, persistent=False)
+        packed = _packed_weights_default() if packed_weights is None else packed_weights
+        if packed and self._pack(weight, source=quantize_weight):
+            # only the packed form is kept; `weight` reads back as None
+            self.register_parameter("weight", None)
+        else:
+            if quantize_weight:
+                weight = _quantize_weight_on_device(weight, ops.default_levels("weight"))
+            weight = weight.to(dtype=linear.weight.dtype)
+            with torch.inference_mode(False):
+                weight = weight.detach().clone()
+            self.weight = nn.Parameter(weight, requires_grad=False)
         if linear.bias is None:
             self.register_parameter("bias", None)
         else:
             with torch.inference_mode(False):
                 self.bias = nn.Parameter(linear.bias.detach().clone(), requires_grad=False)
-        self._gemm_weight: torch.Tensor | None = None
+
+    # ---------------------------------------------------------------- packed weights
+    def _pack(self, weight: torch.Tensor, *, source: bool) -> bool:
+        """Store ``weight`` in the packed format (K2). ``source`` (RTN): ``weight`` is the
+        unquantized weight and the packed form is its RTN quantization, bit-identical to
+        the reference's (quantization.py:169-184). Otherwise ``weight`` is already on the
+        HiF4 grid without its metadata: it is refitted and kept packed only when the
+        packed form reproduces every value (RTN is not idempotent in general). False when
+        the weight stays in bf16 (k not a multiple of 256, or values not reproduced)."""
+        n, k = weight.shape
+        if k % 256:
+            return False
+        device = weight.device if weight.is_cuda else torch.device("cuda", torch.cuda.current_device())
+        codes, meta, changed = ops.hif4_pack_weight(weight.detach().to(device), levels=ops.default_levels("weight"))
+        if not source and changed:
+            return False
+        self.weight_codes, self.weight_meta = codes, meta
+        self._gemm_weight = None
+        return True
+
+    @property
+    def packed(self) -> bool:
+        return self.weight_codes is not None
+
+    def use_packed(self, codes: torch.Tensor, meta: torch.Tensor) -> None:
+        """Switch to packed storage with an exact packed form produced elsewhere (for
+        example K2 with a checkpoint's GPTQ metadata); the bf16 weight is released."""
+        if codes.shape != (self.out_features, self.in_features // 2) or meta.shape != (
+                self.out_features, self.in_features // 64):
+            raise ValueError("packed weight shape does not match the layer")
+        if self.in_features % 256:
+            raise NotImplementedError("the packed GEMM needs in_features % 256 == 0")
+        self.weight_codes, self.weight_meta = codes, meta
+        self._gemm_weight = None
+        self.register_parameter("weight", None)
+
+    def hif4_metadata(self) -> dict[str, torch.Tensor]:
+        """The packed weight's compact HiF4 metadata in the reference's checkpoint leaves
+        (qad_checkpoint.py:43-48, the fields of CompactHiF4Parameters, hif4.py:68-79):
+        scale and reciprocal fp32 [n, k/64], lv2 int8 [n, k/64, 8], lv3 int8 [n, k/64, 16]."""
+        meta = self.weight_meta.to(torch.int64) & 0xFFFFFFFF
+        code = meta & 0xFF
+        scale = (1.0 + (code & 3).double() / 4.0) * torch.exp2(((code >> 2) - 48).double())
+        scale = scale.float()
+        bits2 = torch.arange(8, device=meta.device)
+        bits3 = torch.arange(16, device=meta.device)
+        return {
+            "weight_hif4_scale": scale,
+            "weight_hif4_reciprocal": (1.0 / scale).to(torch.bfloat16).float(),
+            "weight_hif4_scale_lv2_exponent": ((meta[..., None] >> (8 + bits2)) & 1).to(torch.int8),
+            "weight_hif4_scale_lv3_exponent": ((meta[..., None] >> (16 + bits3)) & 1).to(torch.int8),
+        }
+
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        super()._save_to_state_dict(destination, prefix, keep_vars)
+        if self.packed:
+            # the reference's layout of a HiF4 checkpoint (qad_checkpoint.py:43-48): the
+            # weight on the HiF4 grid in bf16 plus its compact metadata, from which the
+            # packed form is rebuilt exactly on load
+            destination[prefix + "weight"] = self.dequantized_weight()
+            for leaf, value in self.hif4_metadata().items():
+                destination[prefix + leaf] = value
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        key = prefix + "weight"
+        leaves = ("weight_hif4_scale", "weight_hif4_reciprocal", "weight_hif4_scale_lv2_exponent",
+                  "weight_hif4_scale_lv3_exponent")
+        if self.packed and key in state_dict:
+            w = state_dict[key]
+            fields = [state_dict.get(prefix + leaf) for leaf in leaves]
+            if all(f is not None for f in fields):
+                n, k = w.shape
+                dev = self.weight_codes.device
+                codes, meta, bad = ops.hif4_pack_weight(
+                    w.to(dev), levels=ops.default_levels("weight"), scale=fields[0].reshape(n, k // 64).to(dev),
+                    lv2=fields[2].reshape(n, k // 64, 8), lv3=fields[3].reshape(n, k // 64, 16))
+                if bad:
+                    error_msgs.append(f"{key}: {bad} values are not on the grid of their HiF4 metadata")
+                else:
+                    self.weight_codes, self.weight_meta = codes, meta
+            elif not self._pack(w, source=False):
+                error_msgs.append(f"{key}: no HiF4 metadata, and a refit does not reproduce the weight; load it "
+                                  "into a module without packed weights")
+            state_dict = {k: v for k, v in state_dict.items() if k != key and k[len(prefix):] not in leaves}
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
 
     def _rotation(self) -> tuple[torch.Tensor | None, torch.Tensor | None, int]:
         if self.activation_min is not None or self.activation_max is not None:
@@ -149,11 +256,14 @@ class FakeQuantLinear(nn.Module):
             block = self.online_hadamard_block_size or self.in_features
             if not _is_pow2(block):
                 raise NotImplementedError("the 12*2^n generalized Hadamard is not implemented; use a power of two")
-            ones = torch.ones(self.in_features, dtype=torch.int8, device=self.weight.device)
+            device = self.weight_codes.device if self.packed else self.weight.device
+            ones = torch.ones(self.in_features, dtype=torch.int8, device=device)
             return ones, None, int(block)
         return None, None, 0
 
     def _operand_weight(self) -> torch.Tensor:
+        if self.packed:
+            return ops.hif4_dequantize(self.weight_codes, self.weight_meta, self.in_features)
         w = self.weight
         if w.dtype == torch.bfloat16:
             return w
@@ -181,6 +291,12 @@ class FakeQuantLinear(nn.Module):
         if scale is not None and scale.device != x.device:
             scale = scale.to(x.device)
         shape = x.shape
+        if self.packed and x.dtype == torch.bfloat16:
+            _, codes, meta = ops.hif4_quantize(x.reshape(-1, shape[-1]), levels=ops.default_levels("act"),
+                                               input_scale=scale, signs=signs, permutation=perm, rot_block=block,
+                                               want_qdq=False, want_codes=True)
+            y = ops.w4a4_gemm((codes, meta), self.weight_codes, self.weight_meta, self.bias)
+            return y.reshape(*shape[:-1], self.out_features)
         qdq, _, _ = ops.hif4_quantize(
             x.reshape(-1, shape[-1]),
             levels=ops.default_levels("act"),

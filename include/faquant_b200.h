@@ -178,6 +178,34 @@ int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void* b, int64_t
                               void* y, int64_t ldy, void* stream);
 
 /*
+ * K3p -- the W4A4 GEMM on packed HiF4 operands: y [m, n] = deq(a) . deq(b)^T (+ bias [n])
+ * (+ residual [m, n], ldr), bf16 output, where a [m, k] and b [n, k] are in the packed
+ * format above (codes uint8 [rows, k/2] and meta uint32 [rows, k/64], rows contiguous)
+ * -- K1's `codes`/`meta` for the activations, K2's
+ * for the weights. The tensor cores read bf16 tiles expanded from the packed bytes in
+ * shared memory, so HBM holds and moves 4.5 bits per operand value; the result is
+ * bit-identical to faq_gemm_bf16_tn(_residual) on the dequantized operands, which is
+ * F.linear on the reference's fake-quantized tensors (src/faquant/quantization.py:277 with
+ * hif4.py:254-271 for both operands). k must be a multiple of 256 (the meta rows are
+ * loaded by TMA, which needs 16-byte rows; FAQ_ERR_UNSUPPORTED otherwise), codes and meta
+ * 16-byte aligned. Replaces, with
+ * faq_hif4_quantize writing codes, FakeQuantLinear.forward's quantize-then-F.linear
+ * (quantization.py:267-277).
+ */
+int faq_w4a4_gemm(const uint8_t* a_codes, const uint32_t* a_meta, const uint8_t* b_codes,
+                  const uint32_t* b_meta, int64_t m, int64_t n, int64_t k, const void* bias,
+                  const void* residual, int64_t ldr, void* y, int64_t ldy, void* stream);
+/*
+ * faq_w4a4_gemm with the activation operand given as its exact bf16 dequantization
+ * a [m, lda] (faq_hif4_quantize's `qdq` output; lda >= k, a multiple of 8, 16-byte aligned)
+ * and the weight packed: for callers that keep the QDQ activation (the same bits as
+ * faq_w4a4_gemm on the activation's codes).
+ */
+int faq_w4a4_gemm_qdq_a(const void* a, int64_t lda, const uint8_t* b_codes, const uint32_t* b_meta,
+                        int64_t m, int64_t n, int64_t k, const void* bias, const void* residual,
+                        int64_t ldr, void* y, int64_t ldy, void* stream);
+
+/*
  * K4 -- attention operand preparation for one of Q, K or V.
  * x is [batch, heads, seq, d] with element strides (sb, sh, ss) and d contiguous,
  * bf16 or fp32. Replaces the post-RoPE block of qwen3._attention_forward
