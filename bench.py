@@ -194,8 +194,9 @@ def build_linear_set(device, seed: int = 0):
         x = x.to(torch.bfloat16)
         w = (torch.randn(n, k, device=device, generator=g) * 0.02).to(torch.bfloat16)
         wq, _, _ = ops.hif4_quantize(w, levels="123")  # RTN onto the HiF4 grid
+        wc, wm, _ = ops.hif4_pack_weight(w, levels="123")  # the same grid, 4.5-bit packed
         rot = derive_hisq_rotation(f"model.layers.0.{path}", k, seed=17, block_size=1024)
-        layers.append(dict(path=path, k=k, n=n, x=x, w=wq, signs=rot.signs.to(device),
+        layers.append(dict(path=path, k=k, n=n, x=x, w=wq, wc=wc, wm=wm, signs=rot.signs.to(device),
                            perm=rot.permutation.to(device), y=torch.empty(T_TOKENS, n, device=device,
                                                                            dtype=torch.bfloat16)))
         del w
@@ -217,6 +218,22 @@ def run_linear_step(layers, timers=None):
             timers["g1"].append(timers["ev"]())
         launches += 2
     return launches
+
+
+def run_packed_step(layers, timers=None):
+    """The same step with the weights packed: K1 writes the activation's codes, the W4A4
+    GEMM expands both operands tile by tile (faq_w4a4_gemm)."""
+    from faquant_b200 import ops
+
+    for L in layers:
+        _, codes, meta = ops.hif4_quantize(L["x"], levels="123", signs=L["signs"], permutation=L["perm"],
+                                           rot_block=1024, want_qdq=False, want_codes=True)
+        if timers is not None:
+            timers["g0"].append(timers["ev"]())
+        ops.w4a4_gemm((codes, meta), L["wc"], L["wm"], out=L["y"])
+        if timers is not None:
+            timers["g1"].append(timers["ev"]())
+    return 2 * len(layers)
 
 
 def build_attention(device, seed: int = 1):
@@ -444,6 +461,40 @@ def main_arm(args) -> None:
     }
     quant_gbs = quant_bytes * args.steps / (quant_ms * 1e-3) / 1e9
 
+    # ---------------- the same step with packed weights (faq_w4a4_gemm)
+    packed = None
+    if not args.no_packed:
+        run_linear_step(layers)
+        ref_out = [L["y"].clone() for L in layers]
+        run_packed_step(layers)
+        same = all(torch.equal(a.view(torch.int16), L["y"].view(torch.int16)) for a, L in zip(ref_out, layers))
+        del ref_out
+        for _ in range(args.warmup):
+            run_packed_step(layers)
+        ptimers = {"g0": [], "g1": [], "ev": ev}
+        barrier()
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for _ in range(args.steps):
+            run_packed_step(layers, ptimers)
+        p1.record()
+        torch.cuda.synchronize()
+        barrier()
+        p_ms = p0.elapsed_time(p1) / args.steps
+        p_gemm_ms = sum(a.elapsed_time(b) for a, b in zip(ptimers["g0"], ptimers["g1"])) / args.steps
+        packed = {
+            "workload": "the config-2 step with 4.5-bit packed weights: K1 writes codes, faq_w4a4_gemm expands "
+                        "both operands in shared memory",
+            "ms_per_step": p_ms, "tflops": linear_flops() / (p_ms * 1e-3) / 1e12,
+            "gemm_ms_per_step": p_gemm_ms, "gemm_tflops": linear_flops() / (p_gemm_ms * 1e-3) / 1e12,
+            "gemm_frac_of_bf16_peak": linear_flops() / (p_gemm_ms * 1e-3) / 1e12 / pk["bf16_tflops"],
+            "weight_bytes_packed": sum(L["wc"].numel() + 4 * L["wm"].numel() for L in layers),
+            "weight_bytes_bf16": sum(2 * L["w"].numel() for L in layers),
+            "bit_identical_to_bf16_path": same,
+            "gpu_launches_per_step": 2 * len(layers),
+        }
+
     # ---------------- attention (config 3), device-resident
     att = None
     if A is not None:
@@ -598,6 +649,7 @@ def main_arm(args) -> None:
             "per_projection_ms": per_proj,
             "clocks": clocks.summary(),
             "gpu_launches": launches,
+            "packed_linear_set": packed,
             "attention": att,
             "gpu_reference": gpu_ref,
             "decode": dec,
@@ -823,6 +875,7 @@ def main() -> None:
     ap.add_argument("--no-attention", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-packed", action="store_true", help="skip the packed-weight step")
     ap.add_argument("--no-gpu-reference", action="store_true",
                     help="skip timing the reference's Triton attention beside K5")
     ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
