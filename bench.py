@@ -117,6 +117,11 @@ def init_dist(world: int, backend: str):
         if backend == "nccl":  # one GPU per rank, named, so NCCL does not guess the mapping
             import torch
 
+            # NCCL's communicator lines (rank, nranks, transport) in the log, as evidence of
+            # the ranks the collectives ran on
+            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+
             kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     return dist if world > 1 else None
@@ -710,6 +715,28 @@ def run_decode(args, device, pk: dict, barrier, dist) -> dict:
             "gpu_launches_per_step": 3, "steps": 20}
 
 
+def _allreduce_share(tp, step, step_ms: float, world: int, barrier) -> dict | None:
+    """One more step with the all-reduces timed by CUDA events on the streams they run on:
+    their summed device time and bytes against the timed step (an untimed extra step, so
+    the events cannot perturb the measurement above). Overlapped chunks (side stream) count
+    in full, so `share` bounds the exposed communication from above."""
+    import torch
+
+    if world == 1:
+        return None
+    tp.timer = []
+    barrier()
+    step()
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b, _ in tp.timer)
+    nbytes = sum(n for _, _, n in tp.timer)
+    calls = len(tp.timer)
+    tp.timer = None
+    busbw = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9 if ms > 0 else None
+    return {"calls_per_step": calls, "bytes_per_step": nbytes, "ms_per_step": ms, "share_of_step": ms / step_ms,
+            "bus_gbs": busbw, "collective": "NCCL all_reduce(sum, bf16) over NVLink"}
+
+
 def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dist) -> dict:
     """BASELINE configs 4 (Wan2.2 block, heads sharded) and 5 (Qwen3-32B TP prefill)."""
     import torch
@@ -724,6 +751,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
     g = torch.Generator(device=device).manual_seed(7)
     x = torch.randn(wcfg.seq, wcfg.dim, generator=g, device=device).to(torch.bfloat16)
     w_ms = _timed(lambda: block(x), args.tp_steps, 1, barrier, dist, device)
+    w_comm = _allreduce_share(tp, lambda: block(x), w_ms, world, barrier)
     wf = wcfg.flops()
     out["wan22_block"] = {
         "workload": "Wan2.2-A14B DiT block, S=75600 (21x45x80), 40 heads, self-attention + FFN (BASELINE config 4)",
@@ -732,6 +760,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         wf["total"] / (w_ms * 1e-3) / 1e12 / (pk["bf16_tflops"] * world),
         "tokens_per_s": wcfg.seq / (w_ms * 1e-3), "flops": wf, "steps": args.tp_steps,
         "rotation": "rbhn_r64 readers (column-parallel), signs r64 (row-parallel)", "levels": wcfg.levels,
+        "allreduce": w_comm,
     }
     del block, x
     torch.cuda.empty_cache()
@@ -739,6 +768,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
     model = Qwen3TPPrefill(qcfg, tp, device)
     ids = default_input_ids(4, 8192, qcfg.vocab, device)
     q_ms = _timed(lambda: model(ids), args.tp_steps, 1, barrier, dist, device)
+    q_comm = _allreduce_share(tp, lambda: model(ids), q_ms, world, barrier)
     qf = qcfg.flops(4, 8192)
     out["qwen3_32b_prefill"] = {
         "workload": f"Qwen3-32B prefill, {qcfg.layers} layers, batch 4 x 8192 tokens (BASELINE config 5)",
@@ -748,6 +778,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         "flops": qf, "steps": args.tp_steps, "bf16_layers": list(qcfg.bf16_layers),
         "rotation": "hisq1024 per norm (column-parallel), signs r64 (row-parallel)",
         "logits": "last position of each sequence", "weights": "RTN HiF4 of N(0,0.02)",
+        "allreduce": q_comm,
     }
     del model
     torch.cuda.empty_cache()

@@ -40,6 +40,9 @@ class TPGroup:
     rank: int = 0
     world: int = 1
     group: object | None = None
+    # when a list: every all-reduce appends (start event, end event, bytes), recorded on the
+    # stream it runs on -- the measurement of the collectives' share of a step
+    timer: list | None = None
 
     def shard(self, n: int, unit: int) -> tuple[int, int]:
         """(start, size) of this rank's even share of ``n`` items in whole ``unit``s."""
@@ -52,7 +55,14 @@ class TPGroup:
         if self.world > 1:
             import torch.distributed as dist
 
-            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            if self.timer is None:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            else:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+                e1.record()
+                self.timer.append((e0, e1, t.numel() * t.element_size()))
         return t
 
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
