@@ -821,6 +821,14 @@ def kernel_case(name: str, reps: int) -> None:
         v = torch.randn(1, 8, 32768, 128, device=dev, generator=g).to(torch.bfloat16)
         for _ in range(reps):
             ops.hif4_decode_attention(q, k, v)
+    elif name == "w4a4":  # the packed GEMM, 2048 x 4096 x 4096: both operands packed, then A as bf16 QDQ
+        x = torch.randn(2048, 4096, device=dev, generator=g).to(torch.bfloat16)
+        xq, ac, am = ops.hif4_quantize(x, levels="123", want_codes=True)
+        w = (torch.randn(4096, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        bc, bm, _ = ops.hif4_pack_weight(w, levels="123")
+        for _ in range(reps):
+            ops.w4a4_gemm((ac, am), bc, bm)
+            ops.w4a4_gemm(xq, bc, bm)
     elif name == "wan_operands":  # K4 on a Wan qkv output: 16800 tokens x 40 heads (config-4 heads)
         from faquant_b200.tensor_parallel import rope3d_tables
 
@@ -912,7 +920,7 @@ def main() -> None:
     ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
     ap.add_argument("--tp-steps", type=int, default=2)
     ap.add_argument("--qwen-layers", type=int, default=64)
-    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention", "decode", "wan_operands"],
+    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention", "decode", "wan_operands", "w4a4"],
                     help="run one kernel on a profiling-sized case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--gpu-reference", action="store_true",
