@@ -100,6 +100,7 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
 #include "attention_sm100.cu"
 #include "glue.cu"
 #include "decode.cu"
+#include "gptq.cu"
 
 extern "C" int faq_version(void) { return 100; }
 

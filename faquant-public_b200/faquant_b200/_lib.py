@@ -68,6 +68,8 @@ SIGNATURES: dict[str, list] = {
     "faq_hif4_decode_attention_static": [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
                                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_float,
                                          _int, _int, _c_void_p, _i64, _i64, _i64, _c_void_p],
+    "faq_gptq_hif4_block": [_c_void_p, _i64, _i64, _int, _i64, _c_void_p, _i64, _i64, _int, _c_void_p, _i64,
+                            _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_selftest_wait_timeout": [_i64, _c_void_p],
     "faq_selftest_ex2_monotone": [ctypes.POINTER(ctypes.c_uint64), _c_void_p],
     "faq_device_trace": [ctypes.POINTER(ctypes.c_uint), _int, _int],

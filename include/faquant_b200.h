@@ -347,6 +347,27 @@ int faq_hif4_decode_attention_static(const void* q, const void* k, const void* v
                                      int p_levels, int normalizer_quantized, void* out, int64_t ob,
                                      int64_t os, int64_t oh, void* stream);
 
+/*
+ * GPTQ with HiF4 grids (offline weight production): the per-column loop of one block of
+ * `cols` (64 or 128) columns for every row of w, as GPTQ.quantize does it
+ * (src/faquant/gptq.py:417-548; block-diagonal form :197-298). w [rows, ldw] fp32 holds
+ * the block's current values at column b * cols for block b < nblocks (nblocks > 1: the
+ * independent groups of the block-diagonal form); hinv: block b's [cols x cols] upper
+ * inverse Cholesky factor at hinv + b * hinv_stride, row stride ldh. At each 64-column
+ * group start the HiF4 metadata is fitted from the group's current values
+ * (fit_hif4_compact_parameters, `levels`) and written to scale/rec ([rows,
+ * groups_per_row] fp32, the block's first group at column b * cols / 64), lv2 ([.., 8]) and
+ * lv3 ([.., 16]) int8; then per column: q = the HiF4 value, e = (w - q) / hinv[c][c],
+ * w[j] -= e * hinv[c][j] for j >= c, each step one fp32 rounding as in the reference.
+ * Writes the quantized values to q and the errors to err (same layout as w); w is not
+ * modified. The caller applies the lazy update of later columns, w[:, stop:] -= err @
+ * H^-1[block, stop:], with any fp32 GEMM.
+ */
+int faq_gptq_hif4_block(const float* w, int64_t ldw, int64_t rows, int cols, int64_t nblocks,
+                        const float* hinv, int64_t ldh, int64_t hinv_stride, int levels, float* q,
+                        int64_t ldq, float* err, int64_t lde, float* scale, float* rec, int8_t* lv2,
+                        int8_t* lv3, int64_t groups_per_row, void* stream);
+
 /* Diagnostics: copy up to max_records records of the waits that gave up (3 words
  * each: site | tile << 8, blockIdx.x | blockIdx.y << 16, blockIdx.z) into `records`
  * (host memory); returns the number of timeouts recorded (>= 0) or -FAQ_ERR_*.

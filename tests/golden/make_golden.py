@@ -23,7 +23,8 @@ Fixtures (all ``.npz``):
   block 1024; three-level and, in a child process, two-level scales);
 - ``attention_*``: ``simulated_flash_attention_forward`` with HiF4 operands;
 - ``qk_prep``: the post-RoPE Q/K transform of ``qwen3._attention_forward``;
-- ``gptq``: a GPTQ HiF4 weight with its compact metadata;
+- ``gptq``: a GPTQ HiF4 weight with its compact metadata; ``gptq_cases``: two larger
+  layers at the deployed GPTQ settings (full Hessian, and block-diagonal);
 - ``config1_attention``: BASELINE config 1's attention in full (B=1, 32/8 heads,
   S=2048, causal, post-RoPE Hadamard, HiF4 Q/K/P/V, P-Reordering) through
   ``simulated_flash_attention_forward``: sampled query rows of the output, the sum over
@@ -338,12 +339,42 @@ def make_c2_projection(levels: str) -> None:
     _linear_fixture("c2_projection", x, w, rot, 1024, levels)
 
 
+def make_gptq_cases() -> None:
+    """GPTQ at the deployed settings (gptq.py:324-593, GPTQ_SETTINGS of
+    workflows/wan22_gptq.py:58) on two larger layers: the full-Hessian solver (256 x 1024,
+    block 128, 4096 calibration rows with 1 % outlier channels) and the block-diagonal
+    one (128 x 512, 64-column Hessian blocks). Stores the bf16 result and the metadata."""
+    from faquant.gptq import GPTQ
+
+    arrays = {}
+    for tag, n, k, hblock, seed in (("full", 256, 1024, None, 61), ("blockdiag", 128, 512, 64, 62)):
+        torch.manual_seed(seed)
+        lin = torch.nn.Linear(k, n, bias=False)
+        with torch.no_grad():
+            lin.weight.normal_(0.0, 0.02)
+        gp = GPTQ(lin, hessian_block_size=hblock)
+        gp.add_batch(outlier_rows(4096, k, seed=seed + 1, outliers=max(1, k // 100)))
+        gp.quantize(quant_format="hif4", bits=4, group_size=64, damp=0.01, block_size=128,
+                    capture_hif4_metadata=True)
+        meta = lin.faquant_hif4_qat_parameters
+        g = k // 64
+        arrays[f"{tag}_w"] = bits(lin.weight.detach().to(torch.bfloat16))
+        arrays[f"{tag}_scale"] = meta.scale.reshape(n, g).numpy()
+        arrays[f"{tag}_lv2"] = meta.scale_lv2_exponent.reshape(n, g, 8).numpy()
+        arrays[f"{tag}_lv3"] = meta.scale_lv3_exponent.reshape(n, g, 16).numpy()
+    save("gptq_cases", **arrays)
+
+
 def main() -> None:
     if len(sys.argv) > 1 and sys.argv[1] == "--linear":
         make_linear(sys.argv[2])
         return
     if len(sys.argv) > 1 and sys.argv[1] == "--config1-linear":
         make_config1_linear(sys.argv[2])
+        return
+    if len(sys.argv) > 1 and sys.argv[1] == "--gptq":
+        torch.set_num_threads(min(8, os.cpu_count() or 1))
+        make_gptq_cases()
         return
     if len(sys.argv) > 1 and sys.argv[1] == "--baseline-sizes":
         # the BASELINE-size fixtures alone (the others are unchanged by them)
@@ -361,6 +392,7 @@ def main() -> None:
     make_attention()
     make_qk_prep()
     make_gptq()
+    make_gptq_cases()
     for levels in ("123", "12"):
         env = dict(os.environ, FAQUANT_HIF4_SCALE_LEVELS=levels)
         env.pop("FAQUANT_HIF4_ACT_SCALE_LEVELS", None)
