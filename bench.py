@@ -119,8 +119,8 @@ def init_dist(world: int, backend: str):
 
             # NCCL's communicator lines (rank, nranks, transport) in the log, as evidence of
             # the ranks the collectives ran on
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
 
             kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)

@@ -462,6 +462,16 @@ __device__ __forceinline__ void tc_mma_f16_lo(uint32_t d_tmem, uint32_t a_lo, ui
       "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(SW128_DESC_HI)
       : "memory");
 }
+// tcgen05.mma.cta_group::2 form taking the low descriptor words (see tc_mma_f16_lo)
+__device__ __forceinline__ void tc_mma_f16_pair_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                                   uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; .reg .b64 ad, bd; setp.ne.b32 p, %4, 0;\n"
+      "mov.b64 ad, {%1, %5}; mov.b64 bd, {%2, %5};\n"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], ad, bd, %3, p; }" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(SW128_DESC_HI)
+      : "memory");
+}
 __device__ __forceinline__ void tc_mma_f16_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
                                                  uint32_t accumulate) {
   asm volatile(

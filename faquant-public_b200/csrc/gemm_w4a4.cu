@@ -58,10 +58,22 @@ constexpr int P_OPERAND = P_CODES + P_META;
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = 512;
 constexpr int TRANSFORM_WARPS = 8;
-constexpr int FIRST_TRANSFORM_WARP = 6;
-constexpr int FORWARD_WARP = FIRST_TRANSFORM_WARP + TRANSFORM_WARPS;  // 14
-constexpr int A_WARP = FORWARD_WARP + 1;                              // 15
-constexpr int THREADS = (A_WARP + 1) * 32;                            // 512
+// Warp roles. A warp runs on sub-partition (SMSP) warp % 4. The MMA issuer is a single
+// thread whose few instructions per K block must not wait behind the integer-heavy
+// expansion, so its sub-partition (1) holds no transform warp: only the issuer, one
+// epilogue warp and the two single-lane roles. The eight transform warps share the other
+// three sub-partitions (3, 3, 2).
+constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, FORWARD_WARP = 9, A_WARP = 13;
+constexpr int FIRST_EPILOGUE_WARP = 4;  // warps 4..7: TMEM lane quarter = warp % 4
+constexpr int THREADS = 16 * 32;        // 512
+// transform warp index (0..7) of each warp, -1 for the other roles
+__device__ __forceinline__ int transform_index(int warp) {
+  // warps 2, 3, 8, 10, 11, 12, 14, 15
+  constexpr unsigned long long kMap = 0x76F543F2FFFF10FFull;  // nibble w: index or F
+  const int v = static_cast<int>((kMap >> (4 * warp)) & 0xF);
+  return v == 0xF ? -1 : v;
+}
+constexpr int DRAINER_WARP = 2;  // transform index 0
 constexpr uint32_t IDESC = idesc_bf16_f32(256, 256, false, false);
 // Ring sizes per mode. Both operands packed: 4 operand stages and 8 staging slots of A and
 // B (12 KB). Activation as bf16 by TMA, only the weight staged: 6 operand stages and 4
@@ -215,7 +227,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&maps.b_codes);
     tma_prefetch_desc(&maps.b_meta);
   }
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     tmem_alloc_pair(smem_addr(tmem_slot), TMEM_COLS);
     tmem_relinquish_pair();
   }
@@ -228,7 +240,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t tempty_at_leader = mapa_shared(smem_addr(&tempty[0]), 0);
   const int my_rows = 128 * static_cast<int>(rank);
 
-  if (warp == 0) {
+  const int tw = transform_index(warp);
+  if (warp == PRODUCER_WARP) {
     if (lane == 0) {
       int ps = 0;
       uint32_t pphase = 0;
@@ -285,8 +298,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == MMA_WARP) {
     int it = 0;
+    const uint32_t desc_a0 = sw128_desc_lo(smem_addr(sA), 16), desc_b0 = sw128_desc_lo(smem_addr(sB), 16);
     if (leader && lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
@@ -300,11 +314,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           // transform warps of the peer CTA released their stores at cluster scope
           if (!mbar_wait_cluster_site(smem_addr(&full[stage]), phase, 63, kb)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a0 = smem_addr(sA + stage * TILE_BYTES), b0 = smem_addr(sB + stage * TILE_BYTES);
+          // descriptor low words (start address >> 4 | leading byte offset 16 >> 4 << 16);
+          // a K=16 step advances the start by 32 bytes
+          const uint32_t a_lo = desc_a0 + static_cast<uint32_t>(stage) * (TILE_BYTES >> 4);
+          const uint32_t b_lo = desc_b0 + static_cast<uint32_t>(stage) * (TILE_BYTES >> 4);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc_mma_f16_pair(d_tmem, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), IDESC,
-                            (kb | kk) != 0);
+            tc_mma_f16_pair_lo(d_tmem, a_lo + 2 * kk, b_lo + 2 * kk, IDESC, (kb | kk) != 0);
           tc_commit_pair(smem_addr(&empty[stage]), 0x3);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -333,7 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp < FIRST_TRANSFORM_WARP) {
+  } else if (tw < 0) {  // epilogue warps 4..7
     const int quarter = warp & 3;
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += pairs, ++it) {
@@ -361,9 +377,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
   } else {
     // transform warps
-    const int t = threadIdx.x - FIRST_TRANSFORM_WARP * 32;
+    const int t = tw * 32 + lane;
     const int row = t >> 1, half = t & 1;
-    const bool drainer = warp == FIRST_TRANSFORM_WARP;
+    const bool drainer = warp == DRAINER_WARP;
     int stage = 0, ps = 0, n = 0;
     uint32_t phase = 0, pphase = 0;
     bool ok = true;
@@ -435,7 +451,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == MMA_WARP) {
     if (lane == 0) {
       if (!leader) {
         mbar_arrive_cluster(mapa_shared(smem_addr(token), 0));
