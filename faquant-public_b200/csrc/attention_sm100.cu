@@ -155,6 +155,33 @@ __device__ __forceinline__ float quantize_p64(float* f) {
   return __fadd_rn(s.x, s.y);
 }
 
+// 2^(lv2 + lv3) of the two quarters of an 8-key sub-block of P, as floats, from the
+// products r = (fl(m3a * rec), fl(m3b * rec)) of the quarter maxima with the group's
+// reciprocal: hif4_level_shifts' comparisons for products that are finite, non-negative
+// and below 8 (levels 123) or 4 (12, 13). P is in [0, 1], so the E6M2 scale of its group
+// is not clamped from above, and m3 * rec <= max / s <= 1.125 * 7.0137 * (1 + 2^-9) < 7.91
+// for the divisor 7 (tie-to-even E6M2 rounding lowers s by at most a factor 1.125; 1/7 and
+// 1/s are bf16-rounded), half that for the divisor 3.5: the exponent comparisons reduce to
+// maxima of powers of two, without the upper clamps. 2^floor(log2 r) is r's exponent field
+// (0 for r = 0), lv2 (123) is [max(r) >= 4], so 2^lv2 = max(2^floor(log2 max(r)) / 2, 1) and
+// 2^(lv2 + lv3) = max(2^floor(log2 r), 2^lv2). A NaN product (a quarter of NaN scores) gives
+// other shifts, but its row's output is NaN whatever they are.
+template <int LEVELS>
+__device__ __forceinline__ float2 p_shift_pow2(float2 r) {
+  const float pa = __uint_as_float(__float_as_uint(r.x) & 0x7F800000u);
+  const float pb = __uint_as_float(__float_as_uint(r.y) & 0x7F800000u);
+  if constexpr (LEVELS == 123) {
+    const float2 h = __fmul2_rn(make_float2(pa, pb), make_float2(0.5f, 0.5f));
+    const float lv = fmax3(h.x, h.y, 1.0f);
+    return make_float2(fmaxf(pa, lv), fmaxf(pb, lv));
+  } else if constexpr (LEVELS == 12) {
+    const float e = fmax3(pa, pb, 1.0f);
+    return make_float2(e, e);
+  } else {
+    return make_float2(fmaxf(pa, 1.0f), fmaxf(pb, 1.0f));
+  }
+}
+
 // exp2 and HiF4 quantization of one 64-key group (this thread's half row, f[0..63] the
 // masked scores), sub-block by sub-block so that the exp2 of one sub-block overlaps the
 // quantization of the previous one. p = ex2(fma(s, c, -m)) as in the unfused form; the
@@ -166,9 +193,12 @@ template <int LEVELS, bool RAW>
 __device__ __forceinline__ float exp_quantize_p64(float* f, float2 c2, float2 mneg, float s_max, float* raw) {
   const float m1 = ex2(__fmaf_rn(s_max, c2.x, mneg.x));
   const Hif4Scale sc = hif4_scale(m1, LEVELS);
-  // 4 qm = rec * 2^(2 - sh), ds / 4 = s * 2^(sh - 2) and -2^23 ds / 4 by exponent moves
-  const uint32_t rec_q = __float_as_uint(sc.rec) + (2u << 23), s_d = __float_as_uint(sc.s) - (2u << 23);
   const float2 rec2 = make_float2(sc.rec, sc.rec);
+  // with w = 2^sh: 4 qm = rec * 2^(2 - sh) by an exponent move (bits(w) = (127 + sh) << 23),
+  // ds / 4 = (s / 4) * w and -2^23 ds / 4 = (-2^23 s / 4) * w, exact products
+  const uint32_t rec_w = __float_as_uint(sc.rec) + (2u << 23) + 0x3F800000u;
+  const float s_q = __uint_as_float(__float_as_uint(sc.s) - (2u << 23));
+  const float2 sq2 = make_float2(s_q, s_q), so2 = make_float2(-8388608.0f * s_q, -8388608.0f * s_q);
   float2 part[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float2 rp[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -184,11 +214,10 @@ __device__ __forceinline__ float exp_quantize_p64(float* f, float2 c2, float2 mn
     const float m3a = fmaxf(fmax3(e[0].x, e[0].y, e[1].x), e[1].y);
     const float m3b = fmaxf(fmax3(e[2].x, e[2].y, e[3].x), e[3].y);
     const float2 rab = __fmul2_rn(make_float2(m3a, m3b), rec2);
-    uint32_t ea, eb;
-    hif4_level_shifts(rab.x, rab.y, LEVELS, ea, eb);
-    const float qa = __uint_as_float(rec_q - ea), qb = __uint_as_float(rec_q - eb);
-    const float da = __uint_as_float(s_d + ea), db = __uint_as_float(s_d + eb);
-    const float oa = __uint_as_float(s_d + ea + 0x8B800000u), ob = __uint_as_float(s_d + eb + 0x8B800000u);
+    const float2 w = p_shift_pow2<LEVELS>(rab);
+    const float qa = __uint_as_float(rec_w - __float_as_uint(w.x)), qb = __uint_as_float(rec_w - __float_as_uint(w.y));
+    const float2 dd = __fmul2_rn(w, sq2), oo = __fmul2_rn(w, so2);
+    const float da = dd.x, db = dd.y, oa = oo.x, ob = oo.y;
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const float qm = t < 2 ? qa : qb, ds = t < 2 ? da : db, off = t < 2 ? oa : ob;
