@@ -225,20 +225,38 @@ def run_linear_step(layers, timers=None):
     return launches
 
 
-def run_packed_step(layers, timers=None):
-    """The same step with the weights packed: K1 writes the activation's codes, the W4A4
-    GEMM expands both operands tile by tile (faq_w4a4_gemm)."""
+def run_packed_step(layers, timers=None, kernel=False):
+    """The same step with the weights held packed, as FakeQuantLinear(packed_weights=True)
+    runs it: from PACKED_EXPAND_MIN_ROWS input rows (all of config 2) K1 writes the bf16
+    QDQ, the weight is expanded to bf16 (faq_hif4_dequantize) and K3 runs; with `kernel`
+    (or fewer rows) K1 writes the activation's codes and the W4A4 GEMM expands both
+    operands tile by tile (faq_w4a4_gemm)."""
     from faquant_b200 import ops
+    from faquant_b200.quantization import PACKED_EXPAND_MIN_ROWS
 
+    launches = 0
     for L in layers:
-        _, codes, meta = ops.hif4_quantize(L["x"], levels="123", signs=L["signs"], permutation=L["perm"],
-                                           rot_block=1024, want_qdq=False, want_codes=True)
-        if timers is not None:
-            timers["g0"].append(timers["ev"]())
-        ops.w4a4_gemm((codes, meta), L["wc"], L["wm"], out=L["y"])
+        if not kernel and L["x"].shape[0] >= PACKED_EXPAND_MIN_ROWS:
+            launches += 3
+            xq, _, _ = ops.hif4_quantize(L["x"], levels="123", signs=L["signs"], permutation=L["perm"],
+                                         rot_block=1024)
+            if timers is not None:
+                timers["x0"].append(timers["ev"]())
+            w = ops.hif4_dequantize(L["wc"], L["wm"], L["k"])
+            if timers is not None:
+                timers["g0"].append(timers["ev"]())
+            ops.gemm_bf16(xq, w, out=L["y"])
+        else:
+            launches += 2
+            _, codes, meta = ops.hif4_quantize(L["x"], levels="123", signs=L["signs"], permutation=L["perm"],
+                                               rot_block=1024, want_qdq=False, want_codes=True)
+            if timers is not None:
+                timers["x0"].append(timers["ev"]())
+                timers["g0"].append(timers["x0"][-1])
+            ops.w4a4_gemm((codes, meta), L["wc"], L["wm"], out=L["y"])
         if timers is not None:
             timers["g1"].append(timers["ev"]())
-    return 2 * len(layers)
+    return launches
 
 
 def build_attention(device, seed: int = 1):
@@ -466,38 +484,54 @@ def main_arm(args) -> None:
     }
     quant_gbs = quant_bytes * args.steps / (quant_ms * 1e-3) / 1e9
 
-    # ---------------- the same step with packed weights (faq_w4a4_gemm)
+    # ---------------- the same step with packed weights (FakeQuantLinear(packed_weights=True))
     packed = None
     if not args.no_packed:
-        run_linear_step(layers)
-        ref_out = [L["y"].clone() for L in layers]
-        run_packed_step(layers)
-        same = all(torch.equal(a.view(torch.int16), L["y"].view(torch.int16)) for a, L in zip(ref_out, layers))
-        del ref_out
-        for _ in range(args.warmup):
-            run_packed_step(layers)
-        ptimers = {"g0": [], "g1": [], "ev": ev}
-        barrier()
-        torch.cuda.synchronize()
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record()
-        for _ in range(args.steps):
-            run_packed_step(layers, ptimers)
-        p1.record()
-        torch.cuda.synchronize()
-        barrier()
-        p_ms = p0.elapsed_time(p1) / args.steps
-        p_gemm_ms = sum(a.elapsed_time(b) for a, b in zip(ptimers["g0"], ptimers["g1"])) / args.steps
+        def timed_packed(kernel):
+            run_linear_step(layers)
+            ref_out = [L["y"].clone() for L in layers]
+            run_packed_step(layers, kernel=kernel)
+            same = all(torch.equal(a.view(torch.int16), L["y"].view(torch.int16)) for a, L in zip(ref_out, layers))
+            del ref_out
+            for _ in range(args.warmup):
+                run_packed_step(layers, kernel=kernel)
+            ptimers = {"x0": [], "g0": [], "g1": [], "ev": ev}
+            barrier()
+            torch.cuda.synchronize()
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record()
+            for _ in range(args.steps):
+                launches = run_packed_step(layers, ptimers, kernel=kernel)
+            p1.record()
+            torch.cuda.synchronize()
+            barrier()
+            p_ms = p0.elapsed_time(p1) / args.steps
+            g_ms = sum(a.elapsed_time(b) for a, b in zip(ptimers["g0"], ptimers["g1"])) / args.steps
+            x_ms = sum(a.elapsed_time(b) for a, b in zip(ptimers["x0"], ptimers["g0"])) / args.steps
+            return p_ms, g_ms, x_ms, same, launches
+
+        p_ms, p_gemm_ms, p_x_ms, same, launches = timed_packed(False)
+        k_ms, k_gemm_ms, _, k_same, k_launches = timed_packed(True)
+        w_vals = sum(L["wc"].numel() * 2 for L in layers)
         packed = {
-            "workload": "the config-2 step with 4.5-bit packed weights: K1 writes codes, faq_w4a4_gemm expands "
-                        "both operands in shared memory",
+            "workload": "the config-2 step with 4.5-bit packed weights as FakeQuantLinear(packed_weights=True) runs "
+                        "it at 8192 rows: K1 bf16 QDQ, the weight expanded to bf16 (faq_hif4_dequantize), K3",
             "ms_per_step": p_ms, "tflops": linear_flops() / (p_ms * 1e-3) / 1e12,
+            "expand_ms_per_step": p_x_ms,
+            "expand_gbs": w_vals * (0.5625 + 2.0) / (p_x_ms * 1e-3) / 1e9 if p_x_ms > 0 else None,
             "gemm_ms_per_step": p_gemm_ms, "gemm_tflops": linear_flops() / (p_gemm_ms * 1e-3) / 1e12,
-            "gemm_frac_of_bf16_peak": linear_flops() / (p_gemm_ms * 1e-3) / 1e12 / pk["bf16_tflops"],
             "weight_bytes_packed": sum(L["wc"].numel() + 4 * L["wm"].numel() for L in layers),
             "weight_bytes_bf16": sum(2 * L["w"].numel() for L in layers),
             "bit_identical_to_bf16_path": same,
-            "gpu_launches_per_step": 2 * len(layers),
+            "gpu_launches_per_step": launches,
+            "packed_gemm_kernel": {
+                "workload": "the same step on faq_w4a4_gemm (K1 writes codes, both operands expanded in shared "
+                            "memory tile by tile; what the module runs below PACKED_EXPAND_MIN_ROWS rows)",
+                "ms_per_step": k_ms, "gemm_ms_per_step": k_gemm_ms,
+                "gemm_tflops": linear_flops() / (k_gemm_ms * 1e-3) / 1e12,
+                "gemm_frac_of_bf16_peak": linear_flops() / (k_gemm_ms * 1e-3) / 1e12 / pk["bf16_tflops"],
+                "bit_identical_to_bf16_path": k_same, "gpu_launches_per_step": k_launches,
+            },
         }
 
     # ---------------- attention (config 3), device-resident

@@ -40,6 +40,7 @@
 // for a negative zero code as the packed format's own decoder gives. Four integer ops
 // and one FMA per pair, plus the scale words per 4-value lv3 group.
 #include "common.cuh"
+#include "hif4.cuh"
 #include "tma.h"
 
 namespace faq {
@@ -118,11 +119,6 @@ __device__ __forceinline__ Slice read_slice(uint32_t operand, int row, int half,
   s.meta = lds_u32(operand + P_CODES + static_cast<uint32_t>(row * 16 + (kb & 3) * 4));
   return s;
 }
-__device__ __forceinline__ uint32_t hfma2_bf16(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -130,40 +126,14 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, ui
 // Expand one thread's 32 values (half `half` of a 64-value block) into row `row` of a
 // 128-byte-swizzled K-major bf16 tile at `tile` (shared address, 1024-byte aligned).
 __device__ __forceinline__ void expand_half(const Slice& s, int half, uint32_t tile, int row) {
-  const uint32_t code = s.meta & 0xFFu;
-  // bf16 bits of c0 = scale * 2^-2 and of -128 c0, duplicated in both halves; a micro
-  // exponent e adds e to both exponents (e <= 2 stays far from the field's ends: the
-  // scale's exponent lies in [-48, 15])
-  const uint32_t sb = code << 5;  // (e + 48) << 7 | t << 5: the scale's bf16 bits minus 79 << 7
-  const uint32_t base_c = (sb + (77u << 7)) * 0x00010001u;
-  const uint32_t base_n = ((sb + (84u << 7)) | 0x8000u) * 0x00010001u;
-  const uint32_t l2 = s.meta >> (8 + 4 * half);   // bit i: lv2 of code word i
-  const uint32_t l3 = s.meta >> (16 + 8 * half);  // bits 2i, 2i + 1: lv3 of word i's two groups
-  const uint32_t words[4] = {s.codes.x, s.codes.y, s.codes.z, s.codes.w};
+  uint32_t out[16];
+  hif4_expand32_bf16(s.codes, s.meta, half, out);  // hif4.cuh: three ALU ops and one bf16x2 FMA per pair
   const uint32_t row_addr = tile + static_cast<uint32_t>(row) * 128u;
   const uint32_t swz = static_cast<uint32_t>(row & 7);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t w = words[i];
-    const uint32_t r = __funnelshift_l(w, w, 4);
-    const uint32_t e2 = (l2 >> i) & 1u;
-    const uint32_t ea = (e2 + ((l3 >> (2 * i)) & 1u)) * 0x00800080u;
-    const uint32_t eb = (e2 + ((l3 >> (2 * i + 1)) & 1u)) * 0x00800080u;
-    const uint32_t ca = base_c + ea, na = base_n + ea;
-    const uint32_t cb = base_c + eb, nb = base_n + eb;
-    uint32_t out[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      // bytes: [w.j (m0), r.j (s0 in bit 7), r.(j+1) (m1), w.j (s1 in bit 7)]
-      const uint32_t sel = static_cast<uint32_t>(j) | (static_cast<uint32_t>(4 + j) << 4) |
-                           (static_cast<uint32_t>(4 + ((j + 1) & 3)) << 8) | (static_cast<uint32_t>(j) << 12);
-      const uint32_t x = __byte_perm(w, r, sel);
-      const uint32_t magic = (x & 0x00070007u) | 0x43004300u;  // (128 + m0, 128 + m1)
-      const uint32_t v = hfma2_bf16(magic, j < 2 ? ca : cb, j < 2 ? na : nb);
-      out[j] = v ^ (x & 0x80008000u);
-    }
     const uint32_t chunk = static_cast<uint32_t>(4 * half + i) ^ swz;
-    sts_v4(row_addr + (chunk << 4), out[0], out[1], out[2], out[3]);
+    sts_v4(row_addr + (chunk << 4), out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
   }
 }
 

@@ -214,6 +214,53 @@ __device__ __forceinline__ uint4 hif4_quant8_bits(const uint32_t (&w)[4], int le
   return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
+// Packed HiF4 -> bf16 for 32 consecutive values (half `half` of a 64-value block): `codes`
+// their 16 code bytes (two sign-magnitude nibbles per byte, value 2i in the low nibble of
+// byte i), `meta` the block's word (E6M2 code | lv2 bits << 8 | lv3 bits << 16). out[q]
+// receives values 2q (low half) and 2q + 1 as bf16 bits, exactly hif4_decode's values
+// (-0.0 for a negative zero code). Per pair of values: one byte permute gathers
+// [m0 | s0 at bit 15 | m1 | s1 at bit 31] from the code word and its 4-bit rotation, the
+// bf16 pair (128 + m0, 128 + m1) = (x & 0x00070007) | 0x43004300 is exact, one
+// fma.rn.bf16x2 with (c, -128 c), c = scale * 2^(lv2 + lv3 - 2) (exact, by exponent
+// arithmetic on the E6M2 code), gives m * c exactly, and an xor restores the sign.
+__device__ __forceinline__ uint32_t hfma2_bf16(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ void hif4_expand32_bf16(const uint4& codes, uint32_t meta, int half, uint32_t (&out)[16]) {
+  const uint32_t code = meta & 0xFFu;
+  // bf16 bits of c0 = scale * 2^-2 and of -128 c0, duplicated in both halves; a micro
+  // exponent e adds e to both exponents (e <= 2 stays far from the field's ends: the
+  // scale's exponent lies in [-48, 15])
+  const uint32_t sb = code << 5;  // (e + 48) << 7 | t << 5: the scale's bf16 bits minus 79 << 7
+  const uint32_t base_c = (sb + (77u << 7)) * 0x00010001u;
+  const uint32_t base_n = ((sb + (84u << 7)) | 0x8000u) * 0x00010001u;
+  const uint32_t l2 = meta >> (8 + 4 * half);   // bit i: lv2 of code word i
+  const uint32_t l3 = meta >> (16 + 8 * half);  // bits 2i, 2i + 1: lv3 of word i's two groups
+  const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w = words[i];
+    const uint32_t r = __funnelshift_l(w, w, 4);
+    const uint32_t e2 = (l2 >> i) & 1u;
+    const uint32_t ea = (e2 + ((l3 >> (2 * i)) & 1u)) * 0x00800080u;
+    const uint32_t eb = (e2 + ((l3 >> (2 * i + 1)) & 1u)) * 0x00800080u;
+    const uint32_t ca = base_c + ea, na = base_n + ea;
+    const uint32_t cb = base_c + eb, nb = base_n + eb;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // bytes: [w.j (m0), r.j (s0 in bit 7), r.(j+1) (m1), w.j (s1 in bit 7)]
+      const uint32_t sel = static_cast<uint32_t>(j) | (static_cast<uint32_t>(4 + j) << 4) |
+                           (static_cast<uint32_t>(4 + ((j + 1) & 3)) << 8) | (static_cast<uint32_t>(j) << 12);
+      const uint32_t x = __byte_perm(w, r, sel);
+      const uint32_t magic = (x & 0x00070007u) | 0x43004300u;  // (128 + m0, 128 + m1)
+      const uint32_t v = hfma2_bf16(magic, j < 2 ? ca : cb, j < 2 ? na : nb);
+      out[4 * i + j] = v ^ (x & 0x80008000u);
+    }
+  }
+}
+
 // Decode one packed nibble with its block's meta word (inverse of the packing).
 __device__ __forceinline__ float hif4_decode(uint32_t nibble, uint32_t meta, int index_in_block) {
   const uint32_t code = meta & 0xFFu;

@@ -8,9 +8,12 @@ C-ABI library: K1 (input scale, HiSQ signs/permutation/block Hadamard, HiF4
 quantization, bit-exact with the reference) and K3 (tcgen05 GEMM on the
 exactly-dequantized bf16 operands). With packed weights (``packed_weights=True``, or
 ``FAQ_PACKED_WEIGHTS=1`` in the environment for modules built through the reference's
-installers) the module holds only the 4.5-bit packed weight, K1 writes the activation's
-packed codes and the GEMM expands both operands in shared memory
-(``faq_w4a4_gemm``): the same output bits, a quarter of the weight bytes in HBM.
+installers) the module holds only the 4.5-bit packed weight: below
+``PACKED_EXPAND_MIN_ROWS`` input rows (decode, small batches: weight bytes bound the call)
+K1 writes the activation's packed codes and the GEMM expands both operands in shared
+memory (``faq_w4a4_gemm``); from there on (prefill: the tensor cores bound the call) the
+weight is expanded to bf16 in a transient buffer at HBM speed (``faq_hif4_dequantize``)
+and K3 runs on it. Either way the same output bits, a quarter of the weight bytes held.
 Only ``quant_format="hif4"`` is implemented;
 every other format, and the QAD-only clamp/companding knobs, raise
 ``NotImplementedError`` -- there is no CPU fallback.
@@ -26,6 +29,12 @@ import os
 from . import ops
 
 HIF4_BLOCK_SIZE = 64
+# Input rows from which a packed module expands its weight to bf16 and runs the bf16 GEMM
+# instead of the packed GEMM: the expansion reads 0.5625 and writes 2 bytes per weight
+# value (a few microseconds per projection), then K3 runs near the bf16 tensor peak,
+# about twice the packed GEMM's rate; below this many rows the packed GEMM's smaller
+# weight reads win.
+PACKED_EXPAND_MIN_ROWS = 512
 
 
 def _packed_weights_default() -> bool:
@@ -291,7 +300,7 @@ class FakeQuantLinear(nn.Module):
         if scale is not None and scale.device != x.device:
             scale = scale.to(x.device)
         shape = x.shape
-        if self.packed and x.dtype == torch.bfloat16:
+        if self.packed and x.dtype == torch.bfloat16 and x.numel() // shape[-1] < PACKED_EXPAND_MIN_ROWS:
             _, codes, meta = ops.hif4_quantize(x.reshape(-1, shape[-1]), levels=ops.default_levels("act"),
                                                input_scale=scale, signs=signs, permutation=perm, rot_block=block,
                                                want_qdq=False, want_codes=True)

@@ -165,9 +165,14 @@ def test_fake_quant_linear_with_packed_weights() -> None:
     plain, packed = FakeQuantLinear(lin, **kw), FakeQuantLinear(lin, packed_weights=True, **kw)
     assert packed.packed and packed.weight is None and not plain.packed
     assert torch.equal(packed.dequantized_weight(), plain.weight)
-    x = torch.randn(3, 700, k, device=DEV, generator=g).to(torch.bfloat16)
+    x = torch.randn(3, 700, k, device=DEV, generator=g).to(torch.bfloat16)  # weight expanded, bf16 GEMM
+    xs = torch.randn(2, 100, k, device=DEV, generator=g).to(torch.bfloat16)  # the packed GEMM
+    from faquant_b200.quantization import PACKED_EXPAND_MIN_ROWS
+
+    assert 200 < PACKED_EXPAND_MIN_ROWS <= 2100
     with torch.no_grad():
         assert np.array_equal(_bits(packed(x)), _bits(plain(x)))
+        assert np.array_equal(_bits(packed(xs)), _bits(plain(xs)))
     sd = packed.state_dict()
     assert torch.equal(sd["weight"], plain.weight) and "weight_codes" not in sd
     # the saved metadata is the reference's RTN fit of the source weight (hif4.py:142-219)
@@ -190,3 +195,22 @@ def test_fake_quant_linear_with_packed_weights() -> None:
         assert torch.equal(other.dequantized_weight(), plain.weight)
     except RuntimeError as e:
         assert "refit" in str(e)
+
+
+@pytest.mark.parametrize("rows,k", [(1000, 4096), (37, 192), (4096, 12288)])
+def test_fast_bf16_expansion_matches_the_decoder(rows: int, k: int) -> None:
+    """faq_hif4_dequantize's bf16 path for whole blocks (hif4_expand32_bf16, the packed
+    GEMM's expansion) against its generic per-value decoder (fp32 output, exact in bf16):
+    the same bits, negative zero codes included, over random codes and meta words spanning
+    the E6M2 code range and every lv2/lv3 pattern."""
+    from faquant_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(rows + k)
+    codes = torch.randint(0, 256, (rows, k // 2), device=DEV, generator=g, dtype=torch.int32).to(torch.uint8)
+    scale = torch.randint(0, 256, (rows, k // 64), device=DEV, generator=g, dtype=torch.int64)  # every E6M2 code
+    bits = torch.randint(0, 1 << 24, (rows, k // 64), device=DEV, generator=g, dtype=torch.int64) << 8
+    word = bits | scale  # < 2^32: as int32 with the same bits
+    meta = (word - ((word >> 31) << 32)).to(torch.int32)
+    fast = ops.hif4_dequantize(codes, meta, k, dtype=torch.bfloat16)
+    ref = ops.hif4_dequantize(codes, meta, k, dtype=torch.float32).to(torch.bfloat16)
+    assert np.array_equal(_bits(fast), _bits(ref))
