@@ -227,7 +227,7 @@ def run_linear_step(layers, timers=None):
 
 def run_packed_step(layers, timers=None, kernel=False):
     """The same step with the weights held packed, as FakeQuantLinear(packed_weights=True)
-    runs it: from PACKED_EXPAND_MIN_ROWS input rows (all of config 2) K1 writes the bf16
+    runs it: from PACKED_EXPAND_MIN_ROWS input rows (by default every call) K1 writes the bf16
     QDQ, the weight is expanded to bf16 (faq_hif4_dequantize) and K3 runs; with `kernel`
     (or fewer rows) K1 writes the activation's codes and the W4A4 GEMM expands both
     operands tile by tile (faq_w4a4_gemm)."""
@@ -526,7 +526,7 @@ def main_arm(args) -> None:
             "gpu_launches_per_step": launches,
             "packed_gemm_kernel": {
                 "workload": "the same step on faq_w4a4_gemm (K1 writes codes, both operands expanded in shared "
-                            "memory tile by tile; what the module runs below PACKED_EXPAND_MIN_ROWS rows)",
+                            "memory tile by tile; the module's path below PACKED_EXPAND_MIN_ROWS rows)",
                 "ms_per_step": k_ms, "gemm_ms_per_step": k_gemm_ms,
                 "gemm_tflops": linear_flops() / (k_gemm_ms * 1e-3) / 1e12,
                 "gemm_frac_of_bf16_peak": linear_flops() / (k_gemm_ms * 1e-3) / 1e12 / pk["bf16_tflops"],

@@ -8,12 +8,12 @@ C-ABI library: K1 (input scale, HiSQ signs/permutation/block Hadamard, HiF4
 quantization, bit-exact with the reference) and K3 (tcgen05 GEMM on the
 exactly-dequantized bf16 operands). With packed weights (``packed_weights=True``, or
 ``FAQ_PACKED_WEIGHTS=1`` in the environment for modules built through the reference's
-installers) the module holds only the 4.5-bit packed weight: below
-``PACKED_EXPAND_MIN_ROWS`` input rows (decode, small batches: weight bytes bound the call)
-K1 writes the activation's packed codes and the GEMM expands both operands in shared
-memory (``faq_w4a4_gemm``); from there on (prefill: the tensor cores bound the call) the
-weight is expanded to bf16 in a transient buffer at HBM speed (``faq_hif4_dequantize``)
-and K3 runs on it. Either way the same output bits, a quarter of the weight bytes held.
+installers) the module holds only the 4.5-bit packed weight: from
+``PACKED_EXPAND_MIN_ROWS`` input rows (by default every call) the weight is expanded to
+bf16 in a transient buffer at HBM speed (``faq_hif4_dequantize``) and K3 runs on it;
+below it K1 writes the activation's packed codes and the GEMM expands both operands in
+shared memory (``faq_w4a4_gemm``). Either way the same output bits, a quarter of the
+weight bytes held.
 Only ``quant_format="hif4"`` is implemented;
 every other format, and the QAD-only clamp/companding knobs, raise
 ``NotImplementedError`` -- there is no CPU fallback.
@@ -30,11 +30,13 @@ from . import ops
 
 HIF4_BLOCK_SIZE = 64
 # Input rows from which a packed module expands its weight to bf16 and runs the bf16 GEMM
-# instead of the packed GEMM: the expansion reads 0.5625 and writes 2 bytes per weight
-# value (a few microseconds per projection), then K3 runs near the bf16 tensor peak,
-# about twice the packed GEMM's rate; below this many rows the packed GEMM's smaller
-# weight reads win.
-PACKED_EXPAND_MIN_ROWS = 512
+# instead of the packed GEMM (faq_w4a4_gemm). The expansion reads 0.5625 and writes 2
+# bytes per weight value, then K3 runs near the bf16 tensor peak, about twice the packed
+# GEMM's rate at prefill sizes; at small row counts the packed GEMM's 256 x 256 tiles
+# leave most SMs idle. Measured through the module on the config-2 projection shapes at
+# 64 .. 2048 rows, expansion was never slower (down_proj at 64 rows: 124 us against 196),
+# so every call expands; raise it to route small calls to the packed GEMM.
+PACKED_EXPAND_MIN_ROWS = 0
 
 
 def _packed_weights_default() -> bool:

@@ -145,7 +145,7 @@ def test_bad_arguments_are_rejected() -> None:
         ops.w4a4_gemm((codes, meta), codes, meta)
 
 
-def test_fake_quant_linear_with_packed_weights() -> None:
+def test_fake_quant_linear_with_packed_weights(monkeypatch) -> None:
     """``FakeQuantLinear`` holding only the packed weight gives the bits of the bf16-weight
     module (config-2 q_proj shape, HiSQ1024 rotation, bias); its state_dict carries the
     reference's bf16 ``weight``; a packed module loaded from it reproduces the weight."""
@@ -165,14 +165,16 @@ def test_fake_quant_linear_with_packed_weights() -> None:
     plain, packed = FakeQuantLinear(lin, **kw), FakeQuantLinear(lin, packed_weights=True, **kw)
     assert packed.packed and packed.weight is None and not plain.packed
     assert torch.equal(packed.dequantized_weight(), plain.weight)
-    x = torch.randn(3, 700, k, device=DEV, generator=g).to(torch.bfloat16)  # weight expanded, bf16 GEMM
-    xs = torch.randn(2, 100, k, device=DEV, generator=g).to(torch.bfloat16)  # the packed GEMM
-    from faquant_b200.quantization import PACKED_EXPAND_MIN_ROWS
+    x = torch.randn(3, 700, k, device=DEV, generator=g).to(torch.bfloat16)
+    xs = torch.randn(2, 100, k, device=DEV, generator=g).to(torch.bfloat16)
+    import faquant_b200.quantization as fq
 
-    assert 200 < PACKED_EXPAND_MIN_ROWS <= 2100
     with torch.no_grad():
-        assert np.array_equal(_bits(packed(x)), _bits(plain(x)))
-        assert np.array_equal(_bits(packed(xs)), _bits(plain(xs)))
+        for rows in (0, 1 << 30):  # weight expanded + bf16 GEMM, then the packed GEMM
+            monkeypatch.setattr(fq, "PACKED_EXPAND_MIN_ROWS", rows)
+            assert np.array_equal(_bits(packed(x)), _bits(plain(x)))
+            assert np.array_equal(_bits(packed(xs)), _bits(plain(xs)))
+    monkeypatch.undo()
     sd = packed.state_dict()
     assert torch.equal(sd["weight"], plain.weight) and "weight_codes" not in sd
     # the saved metadata is the reference's RTN fit of the source weight (hif4.py:142-219)
