@@ -286,6 +286,90 @@ def run_attention_step(A, timers=None):
     return 4
 
 
+def attention_e2e(A, args, device, barrier, dist):
+    """Config-3 attention through the public calls a model makes, from pinned host buffers:
+    Q/K/V go up (one side stream, the next step's while this one computes), the model-side
+    transform of qwen3._attention_forward (faq_qk_prep: Smooth-QK and the Hadamard, one bf16
+    cast) and the HF attention backend (simulated_flash_attention_forward: Q/K/V HiF4, then
+    K5), the output comes down on another stream. Every byte crosses PCIe inside the timed
+    region; time on the device, max over ranks."""
+    import torch
+
+    from faquant_b200 import ops
+    from faquant_b200.attention import new_simulated_attention_stats, simulated_flash_attention_forward
+
+    module = torch.nn.Module()
+    module.is_causal = True
+    module.faquant_attention_query_chunk_size = 128
+    module.faquant_attention_key_chunk_size = 128
+    module.faquant_qk_matmul_quant = True
+    module.faquant_pv_matmul_quant = True
+    module.faquant_pv_normalizer_mode = "quantized_same"
+    module.faquant_matmul_quant_kwargs = {"quant_format": "hif4", "bits": 4, "group_size": 64, "symmetric": True,
+                                          "clip_ratio": 1.0}
+    module.faquant_simulated_attention_stats = new_simulated_attention_stats()
+    host = {n: A[n].cpu().pin_memory() for n in ("q", "k", "v")}
+    out_shape = A["out"].shape
+    host_out = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+    host_out.zero_()
+    main = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+
+    def upload():
+        with torch.cuda.stream(s_in):
+            dev_in = {n: host[n].to(device, non_blocking=True) for n in host}
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        return dev_in, ev
+
+    def step(dev_in, ev):
+        main.wait_event(ev)
+        for t in dev_in.values():
+            t.record_stream(main)
+        qh = ops.qk_prep(dev_in["q"], levels=None, rotate=True, smooth_scale=A["smooth"], smooth_mode="mul")[0]
+        kh = ops.qk_prep(dev_in["k"], levels=None, rotate=True, smooth_scale=A["smooth"], smooth_mode="div")[0]
+        out, _ = simulated_flash_attention_forward(module, qh, kh, dev_in["v"], None, scaling=128**-0.5)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            host_out.copy_(out, non_blocking=True)
+        out.record_stream(s_out)
+
+    nxt = upload()
+    for _ in range(2):
+        cur, nxt = nxt, upload()
+        step(*cur)
+    torch.cuda.synchronize()
+    steps = max(2, args.att_steps)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    nxt = upload()
+    for i in range(steps):
+        cur = nxt
+        if i + 1 < steps:
+            nxt = upload()
+        step(*cur)
+    main.wait_stream(s_out)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = torch.tensor([e0.elapsed_time(e1) / steps], device=device)
+    if dist is not None:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    world = dist.get_world_size() if dist is not None else 1
+    return {"value": attention_flops() * world / (float(e_ms.item()) * 1e-3) / 1e12, "unit": "TFLOPS",
+            "ms_per_step": float(e_ms.item()),
+            "h2d_bytes_per_step": sum(h.numel() * 2 for h in host.values()),
+            "d2h_bytes_per_step": host_out.numel() * 2,
+            "path": "pinned host Q/K/V -> faq_qk_prep (model transform) -> simulated_flash_attention_forward "
+                    "(HF backend: Q/K/V HiF4 + K5) -> pinned host output"}
+
+
 def attention_flops() -> float:
     s = ATT["seq"]
     return 4.0 * ATT["d"] * ATT["hq"] * ATT["batch"] * s * (s + 1) / 2.0
@@ -562,6 +646,10 @@ def main_arm(args) -> None:
             "tokens_per_s": ATT["seq"] * ATT["batch"] / (a_ms * 1e-3),
             "gpu_launches_per_step": launches_att,
         }
+
+    # ---------------- the same attention end to end through the public API, host buffers
+    if att is not None and not args.no_e2e:
+        att["e2e"] = attention_e2e(A, args, device, barrier, dist)
 
     # ---------------- the reference's own GPU kernel beside K5 (config 4 attention), rank 0
     gpu_ref = None
