@@ -100,6 +100,17 @@ __device__ __forceinline__ int exponent_of(float x) {  // floor(log2 x), x posit
   return static_cast<int>((__float_as_uint(x) >> 23) & 0xFF) - 127;
 }
 
+// ---------------------------------------------------------------- register-fragment MMA
+// mma.sync m16n8k16, bf16 operands, fp32 accumulate in place: for products too small for a
+// tcgen05 tile (decode rows, a few query rows per KV head).
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // ---------------------------------------------------------------- smem / mbarrier
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

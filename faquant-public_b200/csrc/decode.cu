@@ -92,13 +92,6 @@ __device__ __forceinline__ const unsigned char* sw_unit(const unsigned char* til
 // is bound by reading the cache; the products are a small part of its time, so the
 // register-fragment MMA serves without tensor memory.
 constexpr int MBLK = MAX_ROWS / 16;  // m-blocks of 16 rows
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 // q fragments of m-block mb for the kv head (b, hk): row g = lane / 4 and g + 8, channels
 // 16 ks + 2 (lane % 4) (+1) and + 8 (the m16n8k16 A layout)
 __device__ __forceinline__ void load_q_frags(const Params& p, int b, int hk, int mb, int lane, uint32_t (&qa)[8][4]) {

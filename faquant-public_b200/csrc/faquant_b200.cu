@@ -95,6 +95,7 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns) {
 
 #include "quantize.cu"
 #include "gemm_sm100.cu"
+#include "gemm_w4_small.cu"
 #include "gemm_w4a4.cu"
 #include "qk_prep.cu"
 #include "attention_sm100.cu"

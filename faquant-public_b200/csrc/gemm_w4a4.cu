@@ -535,6 +535,12 @@ extern "C" int faq_w4a4_gemm_qdq_a(const void* a, int64_t lda, const uint8_t* b_
   FAQ_CHECK_ARG(a != nullptr && aligned16(a), "a must be a 16-byte aligned device pointer");
   FAQ_CHECK_ARG(lda >= k && lda % 8 == 0, "lda must be >= k and a multiple of 8");
   if (m == 0 || n == 0) return FAQ_OK;
+  if (w4s::small_m_fits(m, k)) {  // a few rows: the weight streams packed into register-fragment MMAs
+    const w4s::Params sp{static_cast<const __nv_bfloat16*>(a), lda, b_codes, b_meta, static_cast<int>(m),
+                         static_cast<int>(n), static_cast<int>(k), static_cast<const __nv_bfloat16*>(bias),
+                         static_cast<const __nv_bfloat16*>(residual), ldr, static_cast<__nv_bfloat16*>(y), ldy};
+    return w4s::launch_small_m(sp, stream);
+  }
   const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
   const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
   const uint32_t box[2] = {w4a4::BK, 128};

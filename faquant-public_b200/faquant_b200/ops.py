@@ -307,8 +307,10 @@ def w4a4_gemm(a: torch.Tensor | tuple[torch.Tensor, torch.Tensor], b_codes: torc
     """The W4A4 GEMM on a packed HiF4 weight ``(b_codes uint8 [n, k/2], b_meta int32
     [n, k/64])``: ``deq(a) @ deq(b)^T (+ bias) (+ residual)`` in bf16, bit-identical to
     ``gemm_bf16`` on the dequantized operands. ``a`` is the activation's packed form
-    ``(codes, meta)`` (``hif4_quantize(..., want_codes=True)``) or its bf16 QDQ ``[m, k]``.
-    ``k`` must be a multiple of 256 (``NotImplementedError`` otherwise)."""
+    ``(codes, meta)`` (``hif4_quantize(..., want_codes=True)``) or its bf16 QDQ ``[m, k]``;
+    a bf16 ``a`` of at most 16 rows runs the small-row kernel, whose sums run in another
+    order (the same values up to fp32 rounding of the accumulation). ``k`` must be a
+    multiple of 256 (``NotImplementedError`` otherwise)."""
     device = _require_cuda(b_codes, b_meta, bias, residual)
     if b_codes.dtype != torch.uint8 or b_meta.dtype not in (torch.int32, torch.uint32):
         raise TypeError("packed weight: codes uint8 [n, k/2], meta int32 [n, k/64]")

@@ -8,12 +8,13 @@ C-ABI library: K1 (input scale, HiSQ signs/permutation/block Hadamard, HiF4
 quantization, bit-exact with the reference) and K3 (tcgen05 GEMM on the
 exactly-dequantized bf16 operands). With packed weights (``packed_weights=True``, or
 ``FAQ_PACKED_WEIGHTS=1`` in the environment for modules built through the reference's
-installers) the module holds only the 4.5-bit packed weight: from
-``PACKED_EXPAND_MIN_ROWS`` input rows (by default every call) the weight is expanded to
-bf16 in a transient buffer at HBM speed (``faq_hif4_dequantize``) and K3 runs on it;
-below it K1 writes the activation's packed codes and the GEMM expands both operands in
-shared memory (``faq_w4a4_gemm``). Either way the same output bits, a quarter of the
-weight bytes held.
+installers) the module holds only the 4.5-bit packed weight: up to
+``PACKED_SMALL_ROWS`` input rows (decode) the small-row kernel streams it packed into
+register-fragment MMAs (``faq_w4a4_gemm_qdq_a``); from ``PACKED_EXPAND_MIN_ROWS`` rows
+(by default every larger call) the weight is expanded to bf16 in a transient buffer at HBM
+speed (``faq_hif4_dequantize``) and K3 runs on it, with the output bits of the bf16 path;
+in between K1 writes the activation's packed codes and the GEMM expands both operands in
+shared memory (``faq_w4a4_gemm``, the same bits too). A quarter of the weight bytes held.
 Only ``quant_format="hif4"`` is implemented;
 every other format, and the QAD-only clamp/companding knobs, raise
 ``NotImplementedError`` -- there is no CPU fallback.
@@ -37,6 +38,12 @@ HIF4_BLOCK_SIZE = 64
 # 64 .. 2048 rows, expansion was never slower (down_proj at 64 rows: 124 us against 196),
 # so every call expands; raise it to route small calls to the packed GEMM.
 PACKED_EXPAND_MIN_ROWS = 0
+# Up to this many input rows a packed module runs the small-row kernel (faq_w4a4_gemm_qdq_a
+# with m <= 16): the weight is read in its 4.5-bit form and expanded in registers, so a
+# decode step reads 0.5625 bytes per weight value instead of 2 (bf16 weights) or 4.5
+# (expansion to bf16 and back). Its sums run in another order than the bf16 GEMM's: the
+# same values up to fp32 rounding of the accumulation, not bit for bit.
+PACKED_SMALL_ROWS = 16
 
 
 def _packed_weights_default() -> bool:
@@ -302,7 +309,14 @@ class FakeQuantLinear(nn.Module):
         if scale is not None and scale.device != x.device:
             scale = scale.to(x.device)
         shape = x.shape
-        if self.packed and x.dtype == torch.bfloat16 and x.numel() // shape[-1] < PACKED_EXPAND_MIN_ROWS:
+        rows = x.numel() // shape[-1]
+        if self.packed and x.dtype == torch.bfloat16 and 0 < rows <= PACKED_SMALL_ROWS:
+            # a few rows (decode): the weight streams packed into the small-row kernel
+            qdq, _, _ = ops.hif4_quantize(x.reshape(-1, shape[-1]), levels=ops.default_levels("act"),
+                                          input_scale=scale, signs=signs, permutation=perm, rot_block=block)
+            y = ops.w4a4_gemm(qdq, self.weight_codes, self.weight_meta, self.bias)
+            return y.reshape(*shape[:-1], self.out_features)
+        if self.packed and x.dtype == torch.bfloat16 and rows < PACKED_EXPAND_MIN_ROWS:
             _, codes, meta = ops.hif4_quantize(x.reshape(-1, shape[-1]), levels=ops.default_levels("act"),
                                                input_scale=scale, signs=signs, permutation=perm, rot_block=block,
                                                want_qdq=False, want_codes=True)

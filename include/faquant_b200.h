@@ -199,7 +199,10 @@ int faq_w4a4_gemm(const uint8_t* a_codes, const uint32_t* a_meta, const uint8_t*
  * faq_w4a4_gemm with the activation operand given as its exact bf16 dequantization
  * a [m, lda] (faq_hif4_quantize's `qdq` output; lda >= k, a multiple of 8, 16-byte aligned)
  * and the weight packed: for callers that keep the QDQ activation (the same bits as
- * faq_w4a4_gemm on the activation's codes).
+ * faq_w4a4_gemm on the activation's codes). For m <= 16 (decode) it runs a small-row kernel
+ * that streams the packed weight into register-fragment MMAs, split over K inside each
+ * CTA and summed in a fixed order: deterministic, equal to the tiled GEMM up to fp32
+ * rounding of the sums (another summation order), not bit for bit.
  */
 int faq_w4a4_gemm_qdq_a(const void* a, int64_t lda, const uint8_t* b_codes, const uint32_t* b_meta,
                         int64_t m, int64_t n, int64_t k, const void* bias, const void* residual,

@@ -216,3 +216,54 @@ def test_fast_bf16_expansion_matches_the_decoder(rows: int, k: int) -> None:
     fast = ops.hif4_dequantize(codes, meta, k, dtype=torch.bfloat16)
     ref = ops.hif4_dequantize(codes, meta, k, dtype=torch.float32).to(torch.bfloat16)
     assert np.array_equal(_bits(fast), _bits(ref))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (3, 1000, 4096), (8, 1024, 12288), (9, 2304, 4096),
+                                   (16, 5120, 25600), (16, 17, 256)])
+def test_small_row_kernel_matches_fp64(m: int, n: int, k: int) -> None:
+    """faq_w4a4_gemm_qdq_a with m <= 16 (the small-row kernel: the weight streamed packed
+    into mma.sync fragments, K split over eight warps, a fixed-order sum) against the product
+    of the dequantized operands in fp64, with bias and residual; the same bits on a second
+    run; within bf16 output rounding of the tiled bf16 GEMM on the same operands."""
+    from faquant_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    a, _, _ = ops.hif4_quantize(x, levels="123")
+    w = (torch.randn(n, k, device=DEV, generator=g) * 0.02).to(torch.bfloat16)
+    bc, bm, _ = ops.hif4_pack_weight(w, levels="123")
+    wd = ops.hif4_dequantize(bc, bm, k)
+    bias = (torch.randn(n, device=DEV, generator=g) * 0.1).to(torch.bfloat16)
+    res = torch.randn(m, n, device=DEV, generator=g).to(torch.bfloat16)
+    y = ops.w4a4_gemm(a, bc, bm, bias=bias, residual=res)
+    y2 = ops.w4a4_gemm(a, bc, bm, bias=bias, residual=res)
+    assert np.array_equal(_bits(y), _bits(y2))
+    pre = a.double() @ wd.double().T + bias.double()
+    ref = pre + res.double()
+    # the output is bf16(bf16(sum + bias) + residual): the first rounding may land one ulp
+    # away from the exact sum's (fp32 sums in another order), the second is half an ulp
+    scale = pre.abs() + res.double().abs() + 1e-30
+    assert bool(((y.double() - ref).abs() <= 2.0 ** -7 * scale).all())
+    tiled = ops.gemm_bf16(a, wd, bias=bias, residual=res)
+    assert bool(((y.double() - tiled.double()).abs() <= 2.0 ** -6 * scale).all())
+
+
+def test_packed_module_few_rows_streams_the_packed_weight() -> None:
+    """A packed FakeQuantLinear called with at most PACKED_SMALL_ROWS rows (decode) runs the
+    small-row kernel; it agrees with the bf16-weight module within bf16 output rounding."""
+    from faquant_b200.quantization import PACKED_SMALL_ROWS, FakeQuantLinear
+
+    k, n = 4096, 4096
+    g = torch.Generator(device=DEV).manual_seed(5)
+    lin = torch.nn.Linear(k, n, bias=True, device=DEV, dtype=torch.bfloat16)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(n, k, device=DEV, generator=g) * 0.02)
+        lin.bias.copy_(torch.randn(n, device=DEV, generator=g) * 0.1)
+    kw = dict(quant_format="hif4", bits=4, weight_group_size=64, activation_group_size=64, symmetric=True,
+              clip_ratio=1.0)
+    plain, packed = FakeQuantLinear(lin, **kw), FakeQuantLinear(lin, packed_weights=True, **kw)
+    for rows in (1, 4, PACKED_SMALL_ROWS):
+        x = torch.randn(rows, k, device=DEV, generator=g).to(torch.bfloat16)
+        with torch.no_grad():
+            yp, yb = packed(x).double(), plain(x).double()
+        assert bool(((yp - yb).abs() <= 2.0 ** -7 * yb.abs() + 1e-30).all())  # one bf16 ulp at most
