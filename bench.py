@@ -259,6 +259,73 @@ def run_packed_step(layers, timers=None, kernel=False):
     return launches
 
 
+def run_decode_linear(layers, device, pk):
+    """The config-2 projections at decode sizes (1 and 16 rows): FakeQuantLinear modules with
+    bf16 weights (K1 + K3) against the same modules holding packed weights (K1 + the
+    small-row kernel, faq_w4a4_gemm_qdq_a), the seven calls of a step captured in one CUDA
+    graph as a decode loop captures them (host work out of the timing). Weight bytes bound
+    these calls: 386 MB of bf16 weights against 109 MB packed per step."""
+    import torch
+
+    from faquant_b200.quantization import FakeQuantLinear
+
+    kw = dict(quant_format="hif4", bits=4, weight_group_size=64, activation_group_size=64, symmetric=True,
+              clip_ratio=1.0, quantize_weight=False, input_rotation_block_size=1024)
+    plain, packed = [], []
+    for L in layers:
+        lin = torch.nn.Linear(L["k"], L["n"], bias=False, device="meta")
+        lin.weight = torch.nn.Parameter(L["w"], requires_grad=False)
+        rot = dict(input_rotation_signs=L["signs"], input_rotation_permutation=L["perm"])
+        plain.append(FakeQuantLinear(lin, **kw, **rot))
+        pm = FakeQuantLinear(lin, **kw, **rot, packed_weights=False)
+        pm.use_packed(L["wc"], L["wm"])
+        packed.append(pm)
+    w_bf16 = sum(2 * L["w"].numel() for L in layers)
+    w_packed = sum(L["wc"].numel() + 4 * L["wm"].numel() for L in layers)
+
+    def graph_us(mods, xs, reps=20):
+        s = torch.cuda.Stream(device=device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.no_grad(), torch.cuda.stream(s):
+            for _ in range(2):
+                for m, x in zip(mods, xs):
+                    m(x)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(g):
+            for _ in range(reps):
+                for m, x in zip(mods, xs):
+                    m(x)
+        g.replay()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            us = a.elapsed_time(b) * 1000 / reps
+            best = us if best is None else min(best, us)
+        del g
+        return best
+
+    out = {"workload": "the seven config-2 projections per decode step, FakeQuantLinear, CUDA-graph replay",
+           "weight_bytes_bf16": w_bf16, "weight_bytes_packed": w_packed}
+    for rows in (1, 16):
+        xs = [L["x"][:rows].contiguous() for L in layers]
+        us_b = graph_us(plain, xs)
+        us_p = graph_us(packed, xs)
+        out[f"rows_{rows}"] = {
+            "bf16_weights_us_per_step": us_b, "packed_us_per_step": us_p, "speedup": us_b / us_p,
+            "packed_weight_gbs": w_packed / (us_p * 1e-6) / 1e9,
+            "packed_frac_of_hbm": w_packed / (us_p * 1e-6) / 1e9 / pk["hbm_gbs"],
+            "bf16_weight_gbs": w_bf16 / (us_b * 1e-6) / 1e9,
+        }
+    return out
+
+
 def build_attention(device, seed: int = 1):
     import torch
 
@@ -618,6 +685,11 @@ def main_arm(args) -> None:
             },
         }
 
+    # ---------------- the projections at decode sizes: packed weights streamed by the small-row kernel
+    dec_lin = None
+    if not args.no_packed:
+        dec_lin = run_decode_linear(layers, device, pk)
+
     # ---------------- attention (config 3), device-resident
     att = None
     if A is not None:
@@ -777,6 +849,7 @@ def main_arm(args) -> None:
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "packed_linear_set": packed,
+            "decode_linear_set": dec_lin,
             "attention": att,
             "gpu_reference": gpu_ref,
             "decode": dec,
