@@ -1024,6 +1024,16 @@ def kernel_case(name: str, reps: int) -> None:
         for _ in range(reps):
             ops.w4a4_gemm((ac, am), bc, bm)
             ops.w4a4_gemm(xq, bc, bm)
+    elif name == "decode_linear":  # K3s on down_proj at one row, then the bf16 expansion of the gate weight
+        w = (torch.randn(4096, 12288, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        bc, bm, _ = ops.hif4_pack_weight(w, levels="123")
+        a, _, _ = ops.hif4_quantize(torch.randn(1, 12288, device=dev, generator=g).to(torch.bfloat16), levels="123")
+        for _ in range(reps):
+            ops.w4a4_gemm(a, bc, bm)
+        wg = (torch.randn(12288, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        gc, gm, _ = ops.hif4_pack_weight(wg, levels="123")
+        for _ in range(reps):
+            ops.hif4_dequantize(gc, gm, 4096)
     elif name == "wan_operands":  # K4 on a Wan qkv output: 16800 tokens x 40 heads (config-4 heads)
         from faquant_b200.tensor_parallel import rope3d_tables
 
@@ -1115,7 +1125,8 @@ def main() -> None:
     ap.add_argument("--no-tp", action="store_true", help="skip the sharded workloads (configs 4 and 5)")
     ap.add_argument("--tp-steps", type=int, default=2)
     ap.add_argument("--qwen-layers", type=int, default=64)
-    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention", "decode", "wan_operands", "w4a4"],
+    ap.add_argument("--kernel-case", choices=["gemm", "quantize", "attention", "decode", "wan_operands", "w4a4",
+                                              "decode_linear"],
                     help="run one kernel on a profiling-sized case (for ncu) and exit")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--gpu-reference", action="store_true",
