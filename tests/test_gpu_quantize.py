@@ -115,6 +115,26 @@ def test_rotation_wide_rows_bit_exact(k: int, block: int) -> None:
     assert np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
 
 
+@pytest.mark.parametrize("k,block,rows", [(4096, 1024, 1), (4096, 64, 5), (12288, 1024, 3), (5120, 512, 16)])
+def test_rotation_few_rows_bit_exact(k: int, block: int, rows: int) -> None:
+    """A few rows (a decode step's activations: fewer rows than CTAs, each CTA building
+    the whole permutation map for a row or two) give the bits of the oracle, codes and meta
+    included."""
+    ops = _ops()
+    rng = np.random.default_rng(7 * k + rows)
+    x = torch.from_numpy(rng.standard_normal((rows, k)).astype(np.float32) * 2).to(torch.bfloat16)
+    x[:, rng.integers(0, k, 3)] *= 30
+    signs = torch.from_numpy(rng.choice([-1, 1], k).astype(np.int8))
+    perm = torch.from_numpy(rng.permutation(k).astype(np.int64))
+    qdq, codes, meta = ops.hif4_quantize(x.to(DEV), levels="123", signs=signs.to(DEV), permutation=perm.to(DEV),
+                                         rot_block=block, want_codes=True)
+    rotated = olin.rotate_input(x.float().numpy(), signs.numpy(), perm.numpy(), block, "bf16")
+    assert np.array_equal(_bits(qdq), oh.f32_to_bf16_bits(oh.fake_quantize(rotated, "123")))
+    ocodes, ometa = oh.hif4_encode(rotated, "123")
+    assert np.array_equal(codes.cpu().numpy(), ocodes)
+    assert np.array_equal(meta.cpu().numpy().view(np.uint32), ometa)
+
+
 @pytest.mark.parametrize("block", [8, 16, 32, 64, 128, 256])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_signs_only_rotation_streaming_bit_exact(block: int, dtype: torch.dtype) -> None:
