@@ -1103,7 +1103,9 @@ def gpu_reference_attention(reps: int) -> dict:
               "workload": "BASELINE config 4 attention: 75600 tokens, 40 heads, d 128, non-causal",
               "reference_ms": ms_ref, "reference_tflops": flops / ms_ref / 1e9, "ours_ms": ms_our,
               "ours_tflops": flops / ms_our / 1e9, "speedup": ms_ref / ms_our,
-              "rel_fro_diff": float((a - b).norm() / b.norm()), "reps": reps}
+              "rel_fro_diff": float((a - b).double().norm() / b.double().norm()),
+              "values_differing": int((a != b).sum()), "values": a.numel(),
+              "max_abs_diff": float((a - b).abs().max()), "reps": reps}
     del prep, views, o_ref, o_our, a, b
     torch.cuda.empty_cache()
     return result
