@@ -932,6 +932,63 @@ def _allreduce_share(tp, step, step_ms: float, world: int, barrier) -> dict | No
             "bus_gbs": busbw, "collective": "NCCL all_reduce(sum, bf16) over NVLink"}
 
 
+def _e2e_timed(fn, host_in, steps: int, device, barrier, dist) -> dict:
+    """A sharded workload end to end from pinned host memory: every step uploads its input
+    (one side stream; the next step's while this one computes), runs `fn` on it through the
+    workload's public module, and downloads the output on another stream; the timed region
+    ends when the last output is on the host. Device time, max over ranks; bytes per rank."""
+    import torch
+
+    main = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+    outs = {}
+
+    def upload():
+        with torch.cuda.stream(s_in):
+            x = host_in.to(device, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(s_in)
+        return x, ev
+
+    def step(x, ev):
+        main.wait_event(ev)
+        x.record_stream(main)
+        y = fn(x)
+        if "host" not in outs:
+            outs["host"] = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            outs["host"].copy_(y, non_blocking=True)
+        y.record_stream(s_out)
+
+    step(*upload())  # warm-up, allocates the pinned output
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    nxt = upload()
+    for i in range(steps):
+        cur = nxt
+        if i + 1 < steps:
+            nxt = upload()
+        step(*cur)
+    main.wait_stream(s_out)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = torch.tensor([e0.elapsed_time(e1) / steps], device=device)
+    if dist is not None:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    out_bytes = outs["host"].numel() * outs["host"].element_size()
+    del outs
+    return {"ms_per_step": float(e_ms.item()), "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+            "d2h_bytes_per_step": out_bytes}
+
+
 def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dist) -> dict:
     """BASELINE configs 4 (Wan2.2 block, heads sharded) and 5 (Qwen3-32B TP prefill)."""
     import torch
@@ -957,6 +1014,12 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         "rotation": "rbhn_r64 readers (column-parallel), signs r64 (row-parallel)", "levels": wcfg.levels,
         "allreduce": w_comm,
     }
+    if not args.no_e2e:
+        e2e = _e2e_timed(block, x.cpu().pin_memory(), args.tp_steps, device, barrier, dist)
+        e2e.update({"value": wf["total"] / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TFLOPS",
+                    "path": "pinned host hidden states -> WanBlockTP (every rank its replicated input) -> "
+                            "pinned host output"})
+        out["wan22_block"]["e2e"] = e2e
     del block, x
     torch.cuda.empty_cache()
     qcfg = Qwen3TPConfig(layers=args.qwen_layers)
@@ -965,6 +1028,11 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
     q_ms = _timed(lambda: model(ids), args.tp_steps, 1, barrier, dist, device)
     q_comm = _allreduce_share(tp, lambda: model(ids), q_ms, world, barrier)
     qf = qcfg.flops(4, 8192)
+    q_e2e = None
+    if not args.no_e2e:
+        q_e2e = _e2e_timed(model, ids.cpu().pin_memory(), args.tp_steps, device, barrier, dist)
+        q_e2e.update({"value": 4 * 8192 / (q_e2e["ms_per_step"] * 1e-3), "unit": "tokens/s",
+                      "path": "pinned host token ids -> Qwen3TPPrefill -> pinned host logits"})
     out["qwen3_32b_prefill"] = {
         "workload": f"Qwen3-32B prefill, {qcfg.layers} layers, batch 4 x 8192 tokens (BASELINE config 5)",
         "parallelism": f"tensor-parallel x{world}", "scaling": "strong", "ms_per_forward": q_ms,
@@ -973,7 +1041,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         "flops": qf, "steps": args.tp_steps, "bf16_layers": list(qcfg.bf16_layers),
         "rotation": "hisq1024 per norm (column-parallel), signs r64 (row-parallel)",
         "logits": "last position of each sequence", "weights": "RTN HiF4 of N(0,0.02)",
-        "allreduce": q_comm,
+        "allreduce": q_comm, "e2e": q_e2e,
     }
     del model
     torch.cuda.empty_cache()
