@@ -66,7 +66,9 @@ def bench_config(world: int) -> dict:
     """The workload both arms report (the reference arm times a bounded sample of it)."""
     return {"workload": "qwen3-8b W4A4 linear set, T=8192 (BASELINE config 2)", "tokens": T_TOKENS,
             "projections": [p for p, _, _ in PROJECTIONS], "rotation": "hisq1024 (seed 17)",
-            "levels": "123", "weights": "RTN HiF4 of N(0,0.02)", "parallelism": f"replicas x{world}",
+            "levels": "123", "weights": "GPTQ HiF4 of N(0,0.02) (damp 0.01, group 64, block 128, H from "
+            "the rotated step activations; the CPU arm's time does not depend on the weight values and "
+            "it quantizes them by RTN)", "parallelism": f"replicas x{world}",
             "l2": "inputs larger than L2 (512 MB activations + 436 MB weights per step)"}
 
 
@@ -184,7 +186,51 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ GPU workload
-def build_linear_set(device, seed: int = 0):
+def _rotated_fp32(x, signs, perm, block: int):
+    """The reader rotation in fp32 (``x * signs``, gather, block Hadamard, ``/sqrt(block)``)
+    by a Hadamard matrix product: GPTQ's calibration input, where the last bits of the
+    Hessian do not matter."""
+    import torch
+
+    h = torch.ones(1, 1, device=x.device)
+    while h.shape[0] < block:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    r = (x.float() * signs.float())[:, perm]
+    return (r.view(r.shape[0], -1, block) @ h).view_as(r) / float(block) ** 0.5
+
+
+def gptq_weight(w, x_rot):
+    """GPTQ with HiF4 grids (this library's GPU solver, ``faquant_b200.gptq``) at the deployed
+    settings -- damp 0.01, groups of 64, block 128 -- with the Hessian from the rotated
+    activations. Returns the bf16 grid weight and its packed form (metadata from the solver)."""
+    import torch
+
+    from faquant_b200 import ops
+    from faquant_b200.gptq import GPTQ
+
+    n, k = w.shape
+    lin = torch.nn.Linear(k, n, bias=False, device=w.device, dtype=torch.float32)
+    with torch.no_grad():
+        lin.weight.copy_(w.float())
+    gp = GPTQ(lin)
+    gp.add_batch(x_rot)
+    gp.quantize(quant_format="hif4", bits=4, group_size=64, damp=0.01, block_size=128,
+                capture_hif4_metadata=True)
+    meta = lin.faquant_hif4_qat_parameters
+    wq = lin.weight.detach().to(torch.bfloat16)
+    wc, wm, bad = ops.hif4_pack_weight(wq, scale=meta.scale.reshape(n, k // 64),
+                                       lv2=meta.scale_lv2_exponent.reshape(n, k // 64, 8),
+                                       lv3=meta.scale_lv3_exponent.reshape(n, k // 64, 16))
+    if bad:
+        raise RuntimeError(f"GPTQ weight does not pack onto its own metadata ({bad} values)")
+    del gp, lin
+    return wq, wc, wm
+
+
+def build_linear_set(device, seed: int = 0, weights: str = "gptq"):
+    """Config 2's seven projections: activations N(0,1) with 0.5 % outlier channels x20 (bf16),
+    weights N(0,0.02) quantized onto the HiF4 grid by GPTQ (``weights="gptq"``, Hessian from
+    the step's own rotated activations, as the configuration states) or by RTN."""
     import torch
 
     from faquant_b200 import ops
@@ -198,13 +244,17 @@ def build_linear_set(device, seed: int = 0):
         x[:, outliers] *= 20.0
         x = x.to(torch.bfloat16)
         w = (torch.randn(n, k, device=device, generator=g) * 0.02).to(torch.bfloat16)
-        wq, _, _ = ops.hif4_quantize(w, levels="123")  # RTN onto the HiF4 grid
-        wc, wm, _ = ops.hif4_pack_weight(w, levels="123")  # the same grid, 4.5-bit packed
         rot = derive_hisq_rotation(f"model.layers.0.{path}", k, seed=17, block_size=1024)
-        layers.append(dict(path=path, k=k, n=n, x=x, w=wq, wc=wc, wm=wm, signs=rot.signs.to(device),
-                           perm=rot.permutation.to(device), y=torch.empty(T_TOKENS, n, device=device,
-                                                                           dtype=torch.bfloat16)))
+        signs, perm = rot.signs.to(device), rot.permutation.to(device)
+        if weights == "gptq":
+            wq, wc, wm = gptq_weight(w, _rotated_fp32(x, signs, perm, 1024))
+        else:
+            wq, _, _ = ops.hif4_quantize(w, levels="123")  # RTN onto the HiF4 grid
+            wc, wm, _ = ops.hif4_pack_weight(w, levels="123")  # the same grid, 4.5-bit packed
+        layers.append(dict(path=path, k=k, n=n, x=x, w=wq, wc=wc, wm=wm, signs=signs, perm=perm,
+                           y=torch.empty(T_TOKENS, n, device=device, dtype=torch.bfloat16)))
         del w
+        torch.cuda.empty_cache()
     return layers
 
 
