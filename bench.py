@@ -961,10 +961,13 @@ def run_decode(args, device, pk: dict, barrier, dist) -> dict:
 
 
 def _allreduce_share(tp, step, step_ms: float, world: int, barrier) -> dict | None:
-    """One more step with the all-reduces timed by CUDA events on the streams they run on:
-    their summed device time and bytes against the timed step (an untimed extra step, so
-    the events cannot perturb the measurement above). Overlapped chunks (side stream) count
-    in full, so `share` bounds the exposed communication from above."""
+    """One more step with the collectives (all-reduces; with sequence parallelism the
+    reduce-scatters and all-gathers) timed by CUDA events on the streams they run on: their
+    summed device time and bytes against the timed step (an untimed extra step, so the
+    events cannot perturb the measurement above). Overlapped chunks (side stream) count in
+    full, so `share` bounds the exposed communication from above. Bus bytes per rank: an
+    all-reduce moves 2 (n - 1) / n of its tensor, a reduce-scatter or all-gather (n - 1) / n
+    of the full tensor."""
     import torch
 
     if world == 1:
@@ -973,13 +976,26 @@ def _allreduce_share(tp, step, step_ms: float, world: int, barrier) -> dict | No
     barrier()
     step()
     torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b) for a, b, _ in tp.timer)
-    nbytes = sum(n for _, _, n in tp.timer)
-    calls = len(tp.timer)
+    kinds = {}
+    for a, b, n, kind in tp.timer:
+        k = kinds.setdefault(kind, {"calls_per_step": 0, "bytes_per_step": 0, "ms_per_step": 0.0})
+        k["calls_per_step"] += 1
+        k["bytes_per_step"] += n
+        k["ms_per_step"] += a.elapsed_time(b)
     tp.timer = None
-    busbw = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9 if ms > 0 else None
-    return {"calls_per_step": calls, "bytes_per_step": nbytes, "ms_per_step": ms, "share_of_step": ms / step_ms,
-            "bus_gbs": busbw, "collective": "NCCL all_reduce(sum, bf16) over NVLink"}
+    bus = 0.0
+    for kind, k in kinds.items():
+        f = 2 * (world - 1) / world if kind == "all_reduce" else (world - 1) / world
+        bus += k["bytes_per_step"] * f
+        k["bus_gbs"] = k["bytes_per_step"] * f / (k["ms_per_step"] * 1e-3) / 1e9 if k["ms_per_step"] > 0 else None
+    ms = sum(k["ms_per_step"] for k in kinds.values())
+    return {"calls_per_step": sum(k["calls_per_step"] for k in kinds.values()),
+            "bytes_per_step": sum(k["bytes_per_step"] for k in kinds.values()), "bus_bytes_per_step": bus,
+            "ms_per_step": ms, "share_of_step": ms / step_ms, "bus_gbs": bus / (ms * 1e-3) / 1e9 if ms > 0 else None,
+            "by_kind": kinds,
+            "collective": "NCCL over NVLink: all_reduce(sum, bf16) of row-parallel outputs, or with sequence "
+                          "parallelism reduce_scatter(sum, bf16) of them and all_gather of the packed HiF4 codes "
+                          "and meta (bf16 in the bf16 layers); all_gather of Wan's per-head sums of squares"}
 
 
 def _e2e_timed(fn, host_in, steps: int, device, barrier, dist) -> dict:
@@ -1052,8 +1068,16 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
     block = WanBlockTP(wcfg, tp, device)
     g = torch.Generator(device=device).manual_seed(7)
     x = torch.randn(wcfg.seq, wcfg.dim, generator=g, device=device).to(torch.bfloat16)
-    w_ms = _timed(lambda: block(x), args.tp_steps, 1, barrier, dist, device)
-    w_comm = _allreduce_share(tp, lambda: block(x), w_ms, world, barrier)
+    lay = block.seq_layout(wcfg.seq)
+    if lay is not None:  # sequence parallel: a block of a DiT takes and passes on its rank's token rows
+        x = x[lay.owned(device)].contiguous()
+        run_block = lambda: block.forward_shard(x, lay)  # noqa: E731
+        w_io = f"this rank's {lay.shard_rows} token rows in and out (sequence parallel, {lay.chunks} chunks)"
+    else:
+        run_block = lambda: block(x)  # noqa: E731
+        w_io = "all 75600 token rows in and out"
+    w_ms = _timed(run_block, args.tp_steps, 1, barrier, dist, device)
+    w_comm = _allreduce_share(tp, run_block, w_ms, world, barrier)
     wf = wcfg.flops()
     out["wan22_block"] = {
         "workload": "Wan2.2-A14B DiT block, S=75600 (21x45x80), 40 heads, self-attention + FFN (BASELINE config 4)",
@@ -1062,10 +1086,11 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         wf["total"] / (w_ms * 1e-3) / 1e12 / (pk["bf16_tflops"] * world),
         "tokens_per_s": wcfg.seq / (w_ms * 1e-3), "flops": wf, "steps": args.tp_steps,
         "rotation": "rbhn_r64 readers (column-parallel), signs r64 (row-parallel)", "levels": wcfg.levels,
-        "allreduce": w_comm,
+        "io": w_io, "collectives": w_comm,
     }
     if not args.no_e2e:
-        e2e = _e2e_timed(block, x.cpu().pin_memory(), args.tp_steps, device, barrier, dist)
+        e2e = _e2e_timed((lambda xs: block.forward_shard(xs, lay)) if lay is not None else block,
+                         x.cpu().pin_memory(), args.tp_steps, device, barrier, dist)
         e2e.update({"value": wf["total"] / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TFLOPS",
                     "path": "pinned host hidden states -> WanBlockTP (every rank its replicated input) -> "
                             "pinned host output"})
@@ -1091,7 +1116,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         "flops": qf, "steps": args.tp_steps, "bf16_layers": list(qcfg.bf16_layers),
         "rotation": "hisq1024 per norm (column-parallel), signs r64 (row-parallel)",
         "logits": "last position of each sequence", "weights": "RTN HiF4 of N(0,0.02)",
-        "allreduce": q_comm, "e2e": q_e2e,
+        "collectives": q_comm, "e2e": q_e2e,
     }
     del model
     torch.cuda.empty_cache()

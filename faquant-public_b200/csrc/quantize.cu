@@ -1439,16 +1439,17 @@ namespace faq {
 template <int NORM>
 int quantize_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight, float eps,
                   const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block, int levels,
-                  uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
+                  uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
   FAQ_CHECK_ARG(rows >= 0 && k > 0, "need rows >= 0 and k > 0");
   FAQ_CHECK_ARG(x != nullptr || rows == 0, "x is null");
   FAQ_CHECK_ARG(NORM != kNormRms || (norm_weight != nullptr && aligned16(norm_weight)),
                 "norm_weight must be non-null and 16-byte aligned");
   FAQ_CHECK_ARG(eps >= 0.0f, "eps must be non-negative");
   FAQ_CHECK_ARG(valid_levels(levels), "levels must be 123, 12 or 13");
-  FAQ_CHECK_ARG(qdq != nullptr || rows == 0, "the fused norm writes the QDQ operand: qdq is required");
-  FAQ_CHECK_ARG(ldq >= k && ldq % 8 == 0 && (qdq == nullptr || aligned16(qdq)),
+  FAQ_CHECK_ARG(qdq != nullptr || codes != nullptr || rows == 0, "qdq and codes are both null");
+  FAQ_CHECK_ARG(qdq == nullptr || (ldq >= k && ldq % 8 == 0 && aligned16(qdq)),
                 "qdq must be 16-byte aligned with ldq >= k, a multiple of 8");
+  FAQ_CHECK_ARG(codes == nullptr || aligned16(codes), "codes must be 16-byte aligned");
   FAQ_CHECK_ARG(!meta || (reinterpret_cast<uintptr_t>(meta) & 3) == 0, "meta must be 4-byte aligned");
   FAQ_CHECK_ARG(signs != nullptr, "the fused norm feeds a rotation: signs are required");
   FAQ_CHECK_ARG((x == nullptr || aligned16(x)) && ldx >= k && ldx % 8 == 0 &&
@@ -1463,7 +1464,7 @@ int quantize_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const voi
   if (smem > 200 * 1024) return fail(FAQ_ERR_UNSUPPORTED, "row too long for the fused norm's shared memory");
   int log2b = 0;
   while ((1 << log2b) < rot_block) ++log2b;
-  QuantOut o{nullptr, meta, qdq, ldq, true};
+  QuantOut o{codes, meta, qdq, ldq, true};
   const int W = static_cast<int>(k / 1024);
   const int per_sm = std::max(1, std::min(16, static_cast<int>((227 * 1024) / (smem + 1024))));
   const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * per_sm);
@@ -1471,7 +1472,7 @@ int quantize_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const voi
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define FAQ_ROTN_LAUNCH(L, MW)                                                                                       \
   {                                                                                                                \
-    auto kern = hif4_rotate_v4_kernel<L, false, MW, NORM>;                                                          \
+    auto kern = codes ? hif4_rotate_v4_kernel<L, true, MW, NORM> : hif4_rotate_v4_kernel<L, false, MW, NORM>;       \
     FAQ_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));    \
     kern<<<static_cast<unsigned>(grid), W * 32, smem, st>>>(                                                       \
         static_cast<const __nv_bfloat16*>(x), rows, static_cast<int>(k), ldx,                                       \
@@ -1503,18 +1504,18 @@ int quantize_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const voi
 
 extern "C" int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
                                           float eps, const void* input_scale, const int8_t* signs,
-                                          const int64_t* perm, int rot_block, int levels, uint32_t* meta, void* qdq,
-                                          int64_t ldq, void* stream) {
+                                          const int64_t* perm, int rot_block, int levels, uint8_t* codes,
+                                          uint32_t* meta, void* qdq, int64_t ldq, void* stream) {
   return faq::quantize_norm<faq::kNormRms>(x, rows, k, ldx, norm_weight, eps, input_scale, signs, perm, rot_block,
-                                           levels, meta, qdq, ldq, stream);
+                                           levels, codes, meta, qdq, ldq, stream);
 }
 
 extern "C" int faq_hif4_quantize_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps,
                                             const void* input_scale, const int8_t* signs, const int64_t* perm,
-                                            int rot_block, int levels, uint32_t* meta, void* qdq, int64_t ldq,
-                                            void* stream) {
+                                            int rot_block, int levels, uint8_t* codes, uint32_t* meta, void* qdq,
+                                            int64_t ldq, void* stream) {
   return faq::quantize_norm<faq::kNormLayer>(x, rows, k, ldx, nullptr, eps, input_scale, signs, perm, rot_block,
-                                             levels, meta, qdq, ldq, stream);
+                                             levels, codes, meta, qdq, ldq, stream);
 }
 
 extern "C" int faq_hif4_quantize_act(const void* x, int act, int64_t rows, int64_t k, int64_t ldx,

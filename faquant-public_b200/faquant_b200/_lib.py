@@ -30,9 +30,9 @@ SIGNATURES: dict[str, list] = {
     "faq_hif4_quantize": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int, _int,
                           _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_hif4_quantize_rms_norm": [_c_void_p, _i64, _i64, _i64, _c_void_p, ctypes.c_float, _c_void_p, _c_void_p,
-                                   _c_void_p, _int, _int, _c_void_p, _c_void_p, _i64, _c_void_p],
+                                   _c_void_p, _int, _int, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_hif4_quantize_layer_norm": [_c_void_p, _i64, _i64, _i64, ctypes.c_float, _c_void_p, _c_void_p, _c_void_p,
-                                     _int, _int, _c_void_p, _c_void_p, _i64, _c_void_p],
+                                     _int, _int, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_hif4_quantize_act": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _int, _int, _c_void_p,
                               _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_hif4_dequantize": [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _int, _i64, _c_void_p],

@@ -193,14 +193,17 @@ def hif4_quantize_rms_norm(
     permutation: torch.Tensor | None = None,
     rot_block: int,
     want_meta: bool = False,
-) -> tuple[torch.Tensor, torch.Tensor | None]:
+    want_qdq: bool = True,
+    codes_out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor | None, torch.Tensor | None]:
     """:func:`hif4_quantize` of ``rms_norm(x, norm_weight, eps)`` in one pass
     (``faq_hif4_quantize_rms_norm``): the same bits as :func:`rms_norm` followed by
     :func:`hif4_quantize`, without the normalized tensor in memory. bf16 ``x [rows, k]``
-    with ``rms_norm_quantize_supported(k, rot_block)``; returns ``(qdq, meta)``.
-    ``norm_weight=None`` takes the affine-free LayerNorm instead
-    (``faq_hif4_quantize_layer_norm``, the bits of :func:`layer_norm` then
-    :func:`hif4_quantize`)."""
+    with ``rms_norm_quantize_supported(k, rot_block)``; returns ``(qdq, meta)``
+    (``qdq`` None with ``want_qdq=False``). ``codes_out`` (``uint8 [rows, k/2]``,
+    contiguous) receives the packed codes as well. ``norm_weight=None`` takes the
+    affine-free LayerNorm instead (``faq_hif4_quantize_layer_norm``, the bits of
+    :func:`layer_norm` then :func:`hif4_quantize`)."""
     device = _require_cuda(x, norm_weight, input_scale, signs, permutation)
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise TypeError("hif4_quantize_rms_norm takes a rank-2 bfloat16 tensor")
@@ -208,15 +211,21 @@ def hif4_quantize_rms_norm(
     if x.stride(-1) != 1 or (rows > 1 and x.stride(0) % 8) or x.data_ptr() % 16:
         x = x.contiguous()
     ldx = x.stride(0) if rows > 1 else k
-    qdq = torch.empty((rows, k), dtype=torch.bfloat16, device=device)
+    qdq = torch.empty((rows, k), dtype=torch.bfloat16, device=device) if want_qdq else None
     meta = torch.empty((rows, k // 64), dtype=torch.int32, device=device) if want_meta else None
+    if codes_out is not None:
+        if (codes_out.dtype != torch.uint8 or tuple(codes_out.shape) != (rows, k // 2)
+                or not codes_out.is_contiguous() or codes_out.device != device):
+            raise ValueError("codes_out must be a contiguous uint8 [rows, k/2] tensor on x's device")
+    elif not want_qdq:
+        raise ValueError("nothing to write: want_qdq=False without codes_out")
     if input_scale is not None:
         input_scale = input_scale.to(device=device, dtype=torch.bfloat16).contiguous()
     signs = signs.to(device=device, dtype=torch.int8).contiguous()
     if permutation is not None:
         permutation = permutation.to(device=device, dtype=torch.int64).contiguous()
-    tail = (_ptr(input_scale), signs.data_ptr(), _ptr(permutation), int(rot_block), levels_code(levels), _ptr(meta),
-            qdq.data_ptr(), k, _stream(device))
+    tail = (_ptr(input_scale), signs.data_ptr(), _ptr(permutation), int(rot_block), levels_code(levels),
+            _ptr(codes_out), _ptr(meta), _ptr(qdq), k, _stream(device))
     if norm_weight is None:
         _lib.call("faq_hif4_quantize_layer_norm", x.data_ptr(), rows, k, ldx, float(eps), *tail)
     else:
@@ -225,12 +234,19 @@ def hif4_quantize_rms_norm(
     return qdq, meta
 
 
-def hif4_dequantize(codes: torch.Tensor, meta: torch.Tensor, k: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-    device = _require_cuda(codes, meta)
+def hif4_dequantize(codes: torch.Tensor, meta: torch.Tensor, k: int, dtype: torch.dtype = torch.bfloat16,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Packed HiF4 ``codes [rows, k64/2]`` / ``meta [rows, k64/64]`` -> values ``[rows, k]``
+    (into ``out`` when given: any row stride, unit column stride)."""
+    device = _require_cuda(codes, meta, out)
     rows = codes.shape[0]
-    out = torch.empty((rows, k), dtype=dtype, device=device)
+    if out is None:
+        out = torch.empty((rows, k), dtype=dtype, device=device)
+    elif out.shape != (rows, k) or out.stride(-1) != 1 or out.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out must be a bf16/fp32 [rows, k] tensor with unit column stride")
+    ldo = out.stride(0) if rows > 1 else k
     _lib.call("faq_hif4_dequantize", codes.contiguous().data_ptr(), meta.contiguous().data_ptr(), rows, k,
-              out.data_ptr(), _dtype_code(out), k, _stream(device))
+              out.data_ptr(), _dtype_code(out), ldo, _stream(device))
     return out
 
 

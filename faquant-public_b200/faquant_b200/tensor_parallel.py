@@ -17,6 +17,14 @@ Megatron-style sharding, one process per GPU (``torch.distributed``, backend ``n
 
 Only the GEMM accumulation order depends on the number of ranks (partial sums meet in
 the all-reduce); every quantized activation and weight code is the same at any TP size.
+
+With more than one rank the models run sequence-parallel by default (``SeqLayout``): the
+residual stream between projections is sharded by rows, so the norms and the readers'
+quantization run on 1/N of the rows instead of on every rank in full; the column-parallel
+inputs are all-gathered as packed HiF4 codes (0.5625 bytes per value instead of bf16's
+2) and the row-parallel outputs are reduce-scattered instead of all-reduced, one chunk of
+rows at a time so each collective overlaps the next chunk's GEMM. Per row the arithmetic
+is the all-reduce path's; at two ranks the outputs are the same bits.
 """
 
 from __future__ import annotations
@@ -40,8 +48,8 @@ class TPGroup:
     rank: int = 0
     world: int = 1
     group: object | None = None
-    # when a list: every all-reduce appends (start event, end event, bytes), recorded on the
-    # stream it runs on -- the measurement of the collectives' share of a step
+    # when a list: every collective appends (start event, end event, bytes, kind), recorded
+    # on the stream it runs on -- the measurement of the collectives' share of a step
     timer: list | None = None
 
     def shard(self, n: int, unit: int) -> tuple[int, int]:
@@ -55,24 +63,52 @@ class TPGroup:
         if self.world > 1:
             import torch.distributed as dist
 
-            if self.timer is None:
-                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
-            else:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
-                e1.record()
-                self.timer.append((e0, e1, t.numel() * t.element_size()))
+            self._timed(lambda: dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group),
+                        t.numel() * t.element_size(), "all_reduce")
         return t
 
     def all_gather(self, t: torch.Tensor) -> torch.Tensor:
         """``[world, *t.shape]``: every rank's ``t`` in rank order."""
         if self.world == 1:
             return t.unsqueeze(0)
+        out = torch.empty((self.world, *t.shape), dtype=t.dtype, device=t.device)
+        self.all_gather_into(out.view(-1, *t.shape[1:]) if t.dim() else out, t)
+        return out
+
+    def _timed(self, call, nbytes: int, kind: str) -> None:
+        if self.timer is None or not torch.cuda.is_available():
+            call()
+            return
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        self.timer.append((e0, e1, nbytes, kind))
+
+    def all_gather_into(self, out: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """``out [world * n, ...]`` <- every rank's ``t [n, ...]`` in rank order (NCCL
+        all-gather; ``out`` must be contiguous)."""
+        if self.world == 1:
+            out.copy_(t)
+            return out
         import torch.distributed as dist
 
-        out = torch.empty((self.world, *t.shape), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        t = t.contiguous()
+        self._timed(lambda: dist.all_gather_into_tensor(out, t, group=self.group), out.numel() * out.element_size(),
+                    "all_gather")
+        return out
+
+    def reduce_scatter(self, out: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """``out [n, ...]`` <- rows ``rank * n .. rank * n + n - 1`` of the sum over ranks of
+        ``t [world * n, ...]`` (NCCL reduce-scatter, sum)."""
+        if self.world == 1:
+            out.copy_(t)
+            return out
+        import torch.distributed as dist
+
+        t = t.contiguous()
+        self._timed(lambda: dist.reduce_scatter_tensor(out, t, op=dist.ReduceOp.SUM, group=self.group),
+                    t.numel() * t.element_size(), "reduce_scatter")
         return out
 
     def comm_stream(self, device: torch.device) -> torch.cuda.Stream:
@@ -82,6 +118,91 @@ class TPGroup:
         if key not in cache:
             cache[key] = torch.cuda.Stream(device=device)
         return cache[key]
+
+
+@dataclass(frozen=True)
+class SeqLayout:
+    """Sequence-parallel row layout of a ``[rows, hidden]`` activation: the rows are cut
+    into ``chunks`` equal chunks and every chunk into ``world`` equal pieces; rank ``r``
+    holds piece ``r`` of every chunk, in chunk order (its shard, ``[chunks * piece,
+    hidden]``). A reduce-scatter of chunk ``c`` of a row-parallel output lands in piece
+    ``c`` of each rank's shard, and an all-gather of piece ``c`` rebuilds chunk ``c`` in
+    row order, so the collectives of one chunk can overlap the GEMM of the next."""
+
+    rows: int
+    world: int
+    rank: int
+    chunks: int
+
+    @property
+    def chunk_rows(self) -> int:
+        return self.rows // self.chunks
+
+    @property
+    def piece(self) -> int:
+        return self.rows // (self.chunks * self.world)
+
+    @property
+    def shard_rows(self) -> int:
+        return self.chunks * self.piece
+
+    def chunk(self, c: int) -> slice:
+        return slice(c * self.chunk_rows, (c + 1) * self.chunk_rows)
+
+    def piece_of_shard(self, c: int) -> slice:
+        return slice(c * self.piece, (c + 1) * self.piece)
+
+    def owned(self, device: torch.device | str = "cpu") -> torch.Tensor:
+        """Row indices of this rank's shard, in shard order."""
+        base = torch.arange(self.chunks, device=device) * self.chunk_rows + self.rank * self.piece
+        return (base[:, None] + torch.arange(self.piece, device=device)[None, :]).reshape(-1)
+
+    def locate(self, row: int) -> tuple[int, int]:
+        """(rank, index in that rank's shard) of ``row``."""
+        c, within = divmod(row, self.chunk_rows)
+        r, i = divmod(within, self.piece)
+        return r, c * self.piece + i
+
+
+def seq_layout(rows: int, tp: TPGroup, max_chunks: int = 4) -> SeqLayout | None:
+    """The layout with the most chunks (at most ``max_chunks``) that splits ``rows`` evenly,
+    or None when ``rows`` does not divide by the TP size (the replicated path then runs)."""
+    for chunks in range(max_chunks, 0, -1):
+        if rows % (chunks * tp.world) == 0:
+            return SeqLayout(rows, tp.world, tp.rank, chunks)
+    return None
+
+
+def _stream_ctx(stream):
+    import contextlib
+
+    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+
+def sp_gather_rows(tp: TPGroup, lay: SeqLayout, shard: torch.Tensor, out: torch.Tensor | None = None,
+                   comm=None, on_chunk=None) -> torch.Tensor:
+    """All-gather of a sequence-parallel shard back to ``[rows, ...]`` in row order, one
+    collective per chunk (on ``comm`` when given). ``on_chunk(c)``, called after chunk
+    ``c``'s collective was issued, lets the caller consume it while later chunks move."""
+    if out is None:
+        out = torch.empty((lay.rows, *shard.shape[1:]), dtype=shard.dtype, device=shard.device)
+    for c in range(lay.chunks):
+        with _stream_ctx(comm):
+            tp.all_gather_into(out[lay.chunk(c)], shard[lay.piece_of_shard(c)])
+        if on_chunk is not None:
+            on_chunk(c)
+    return out
+
+
+def sp_reduce_scatter_rows(tp: TPGroup, lay: SeqLayout, full: torch.Tensor,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Reduce-scatter of a row-parallel ``[rows, ...]`` partial into this rank's shard,
+    one collective per chunk."""
+    if out is None:
+        out = torch.empty((lay.shard_rows, *full.shape[1:]), dtype=full.dtype, device=full.device)
+    for c in range(lay.chunks):
+        tp.reduce_scatter(out[lay.piece_of_shard(c)], full[lay.chunk(c)])
+    return out
 
 
 def _seed(*parts: object) -> int:
@@ -192,6 +313,86 @@ class TPHiF4Linear(nn.Module):
             return ops.gemm_bf16(xq, self.weight, self.bias, residual=residual)
         y = self._row_parallel(xq)
         return y if residual is None else residual + y
+
+    # ------------------------------------------------ sequence-parallel forms
+    def sp_column(self, x_shard: torch.Tensor, lay: SeqLayout, tp: TPGroup,
+                  norm: tuple[torch.Tensor | None, float] | None = None) -> torch.Tensor:
+        """Column-parallel projection of a sequence-parallel input: ``x_shard`` holds this
+        rank's rows (``lay``); the norm (``norm = (weight, eps)``, ``weight=None``: the
+        affine-free LayerNorm) and the input quantization run on the shard only, the
+        quantized rows are all-gathered -- as packed HiF4 codes and meta words (0.5625
+        bytes per value) when the norm is fused into K1 -- expanded back to the bf16
+        operand (the same values K1 would have written) and multiplied, chunk by chunk, so
+        chunk ``c + 1`` moves over NVLink while chunk ``c`` is expanded and multiplied.
+        Returns the ``[rows, n_local]`` output."""
+        dev = x_shard.device
+        k = x_shard.shape[1]
+        r = self.rotation
+        packed = (self.quantize and norm is not None and r.signs is not None
+                  and ops.rms_norm_quantize_supported(k, r.block))
+        if packed:
+            codes = torch.empty((x_shard.shape[0], k // 2), dtype=torch.uint8, device=dev)
+            _, meta = ops.hif4_quantize_rms_norm(x_shard, norm[0], norm[1], levels=self.levels, signs=r.signs,
+                                                 permutation=r.permutation, rot_block=r.block, want_meta=True,
+                                                 want_qdq=False, codes_out=codes)
+            shards = [codes, meta]
+        elif norm is not None:
+            h = ops.layer_norm(x_shard, norm[1]) if norm[0] is None else ops.rms_norm(x_shard, norm[0], norm[1])
+            shards = [self.quantize_input(h)]
+        else:
+            shards = [self.quantize_input(x_shard)]
+        fulls = [torch.empty((lay.rows, *t.shape[1:]), dtype=t.dtype, device=dev) for t in shards]
+        y = torch.empty((lay.rows, self.weight.shape[0]), dtype=torch.bfloat16, device=dev)
+        compute = torch.cuda.current_stream(dev)
+        comm = tp.comm_stream(dev)
+        comm.wait_stream(compute)  # the shard's quantized rows are written
+        for t in shards + fulls:
+            t.record_stream(comm)
+
+        def consume(c: int) -> None:
+            ev = torch.cuda.Event()
+            ev.record(comm)
+            compute.wait_event(ev)
+            rows = lay.chunk(c)
+            if packed:
+                a = torch.empty((lay.chunk_rows, k), dtype=torch.bfloat16, device=dev)
+                ops.hif4_dequantize(fulls[0][rows], fulls[1][rows], k, out=a)
+            else:
+                a = fulls[0][rows]
+            ops.gemm_bf16(a, self.weight, self.bias, out=y[rows])
+
+        for c in range(lay.chunks):
+            with torch.cuda.stream(comm):
+                for src, dst in zip(shards, fulls):
+                    tp.all_gather_into(dst[lay.chunk(c)], src[lay.piece_of_shard(c)])
+            consume(c)
+        return y
+
+    def sp_row(self, xq: torch.Tensor, residual: torch.Tensor, lay: SeqLayout, tp: TPGroup) -> torch.Tensor:
+        """Row-parallel projection into a sequence-parallel residual stream: the GEMM of
+        the quantized input ``xq [rows, k_local]`` chunk by chunk, each chunk's partial
+        output reduce-scattered (NCCL, sum in bf16) while the next chunk multiplies, and
+        added to this rank's residual rows. Returns the new ``[shard_rows, hidden]``
+        residual (the same sums and bf16 adds as the all-reduce path's rows)."""
+        dev = xq.device
+        n = self.weight.shape[0]
+        out = torch.empty_like(residual)
+        compute = torch.cuda.current_stream(dev)
+        comm = tp.comm_stream(dev)
+        residual.record_stream(comm)
+        out.record_stream(comm)
+        for c in range(lay.chunks):
+            part = torch.empty((lay.chunk_rows, n), dtype=torch.bfloat16, device=dev)
+            ops.gemm_bf16(xq[lay.chunk(c)], self.weight, self.bias, out=part)
+            comm.wait_stream(compute)
+            part.record_stream(comm)
+            with torch.cuda.stream(comm):
+                red = torch.empty((lay.piece, n), dtype=torch.bfloat16, device=dev)
+                tp.reduce_scatter(red, part)
+                p = lay.piece_of_shard(c)
+                torch.add(residual[p], red, out=out[p])
+        compute.wait_stream(comm)
+        return out
 
     def _row_parallel(self, xq: torch.Tensor) -> torch.Tensor:
         tp = self.reduce
@@ -321,6 +522,9 @@ class Qwen3TPPrefill(nn.Module):
         # the residual adds in the o_proj / down_proj GEMM epilogues (off while a trace hook
         # needs the projections' own outputs)
         self.fuse_residual = True
+        # with more than one rank: the residual stream sharded by rows, reduce-scatter and
+        # all-gather of packed codes instead of all-reduces (off while a trace hook is set)
+        self.sequence_parallel = True
         d = cfg.head_dim
         sl = qwen3_shard_slices(cfg, tp)
         hq, hkv = cfg.heads // tp.world, cfg.kv_heads // tp.world
@@ -373,11 +577,18 @@ class Qwen3TPPrefill(nn.Module):
                    norm: tuple[torch.Tensor, float] | None = None) -> torch.Tensor:
         """``h`` is the normalized input, or with ``norm`` the raw one (the norm is then
         fused into the qkv input quantization)."""
-        cfg, d = self.cfg, self.cfg.head_dim
         if norm is None:
             qkv = self._t("qkv", index, layer.qkv(self._t("input_norm", index, h)))  # [T, (hq + 2 hkv) d]
         else:
             qkv = self._t("qkv", index, layer.qkv(h, norm=norm))
+        out = self._attend(layer, qkv, batch, seq, cos, sin, index)
+        return self._t("o", index, layer.o(out, residual=residual))
+
+    def _attend(self, layer: _Qwen3Layer, qkv: torch.Tensor, batch: int, seq: int, cos, sin,
+                index: int = 0) -> torch.Tensor:
+        """The attention of the rank's heads from the qkv projection's output ``[T, (hq + 2
+        hkv) d]``; returns ``[T, hq d]`` (the o_proj input)."""
+        cfg, d = self.cfg, self.cfg.head_dim
         nq, nk = layer.heads * d, layer.kv_heads * d
         # q_norm/k_norm, RoPE, Hadamard and HiF4 in one K4 pass per operand
         q = qkv[:, :nq].view(batch, seq, layer.heads, d).transpose(1, 2)
@@ -390,12 +601,47 @@ class Qwen3TPPrefill(nn.Module):
         vd = self._t("vd", index, ops.qk_prep(v, levels=cfg.levels, rotate=False)[0])
         out = ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=True, p_levels=cfg.levels,
                                  quantized_normalizer=True)  # [B, S, hq, d]
-        return self._t("o", index, layer.o(self._t("attention", index, out).view(batch * seq, nq), residual=residual))
+        return self._t("attention", index, out).view(batch * seq, nq)
+
+    def seq_layout(self, batch: int, seq: int) -> SeqLayout | None:
+        """The sequence-parallel layout the forward uses (None: the replicated path)."""
+        if not self.sequence_parallel or self.tp.world == 1 or self.trace is not None:
+            return None
+        return seq_layout(batch * seq, self.tp)
+
+    def _forward_sp(self, input_ids: torch.Tensor, lay: SeqLayout) -> torch.Tensor:
+        """Sequence-parallel forward: the residual stream is sharded by rows (``lay``), the
+        norms and the column-parallel inputs' quantization run on the shard and the packed
+        codes are all-gathered (:meth:`TPHiF4Linear.sp_column`); the row-parallel outputs
+        are reduce-scattered into the shard (:meth:`TPHiF4Linear.sp_row`). The same
+        per-row arithmetic as the all-reduce path: at two ranks the logits are the same
+        bits."""
+        cfg, tp = self.cfg, self.tp
+        batch, seq = input_ids.shape
+        cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
+        x = torch.nn.functional.embedding(input_ids.reshape(-1)[lay.owned(self.device)], self.embed)
+        for layer in self.layers:
+            qkv = layer.qkv.sp_column(x, lay, tp, norm=(layer.input_norm, cfg.eps))
+            att = self._attend(layer, qkv, batch, seq, cos, sin)
+            x = layer.o.sp_row(layer.o.quantize_input(att), x, lay, tp)
+            gu = layer.gate_up.sp_column(x, lay, tp, norm=(layer.post_norm, cfg.eps))
+            x = layer.down.sp_row(layer.down.activate_and_quantize(gu, "swiglu"), x, lay, tp)
+        # the last position of each sequence, from the rank that holds it (the others add zeros)
+        last = torch.zeros((batch, cfg.hidden), dtype=torch.bfloat16, device=self.device)
+        for b in range(batch):
+            owner, i = lay.locate(b * seq + seq - 1)
+            if owner == tp.rank:
+                last[b] = x[i]
+        tp.all_reduce_(last)
+        return torch.nn.functional.linear(rms_norm(last, self.final_norm, cfg.eps), self.lm_head).float()
 
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
         batch, seq = input_ids.shape
+        lay = self.seq_layout(batch, seq)
+        if lay is not None:
+            return self._forward_sp(input_ids, lay)
         cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
         x = torch.nn.functional.embedding(input_ids.reshape(-1), self.embed)  # [T, hidden]
         fuse = self.fuse_residual and self.trace is None
@@ -509,6 +755,7 @@ class WanBlockTP(nn.Module):
         self.cfg, self.tp, self.device = cfg, tp, device
         self.trace = None  # trace(stage, 0, tensor) at each stage boundary, as in Qwen3TPPrefill
         self.fuse_residual = True
+        self.sequence_parallel = True  # as in Qwen3TPPrefill (off while a trace hook is set)
         if cfg.heads % tp.world:
             raise ValueError("heads must divide by the TP size")
         d = cfg.head_dim
@@ -544,17 +791,17 @@ class WanBlockTP(nn.Module):
         self.norm_k = torch.ones(cfg.dim, dtype=torch.float32, device=device)[rows].contiguous()
         self.cos, self.sin = rope3d_tables(cfg.grid, d, cfg.rope_theta, device)
 
-    @torch.no_grad()
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """``x [L, dim]`` bf16 (batch 1) -> ``[L, dim]``."""
+    def seq_layout(self, seq: int) -> SeqLayout | None:
+        """The sequence-parallel layout of ``seq`` tokens (None: the replicated path)."""
+        if not self.sequence_parallel or self.tp.world == 1 or self.trace is not None:
+            return None
+        return seq_layout(seq, self.tp)
+
+    def _attend(self, qkv: torch.Tensor, seq: int, tr) -> torch.Tensor:
+        """The rank's heads of the self-attention from the qkv output ``[L, 3 hl d]``: Wan's
+        q/k RMSNorm over all heads (per-head sums of squares all-gathered), the 3-D RoPE, the
+        Hadamard and HiF4 operands (K4), the HiF4 attention (K5); returns ``[L, hl d]``."""
         cfg, d, hl = self.cfg, self.cfg.head_dim, self.h_local
-        seq = x.shape[0]
-        tr = (lambda stage, t: (self.trace(stage, 0, t), t)[1]) if self.trace is not None else (lambda stage, t: t)
-        fuse = self.fuse_residual and self.trace is None  # norms in the readers' K1, residual adds in epilogues
-        if fuse:
-            qkv = self.qkv(x, norm=(None, cfg.eps))
-        else:
-            qkv = tr("qkv", self.qkv(tr("norm1", ops.layer_norm(x, cfg.eps))))
         n = hl * d
         # per-head sums of squares of q and k: [world, L, 2 hl] after the gather
         head_ss = self.tp.all_gather(ops.row_sumsq(qkv[:, :2 * n], segments=2 * hl))
@@ -566,7 +813,42 @@ class WanBlockTP(nn.Module):
         vd = tr("vd", ops.qk_prep(heads(2 * n), levels=cfg.levels, rotate=False)[0])
         att = tr("attention", ops.hif4_attention(qd, kd, vd, scale=d ** -0.5, causal=False, p_levels=cfg.levels,
                                                  quantized_normalizer=True))  # [1, L, hl, d]
-        x = tr("x_mid", self.o(att.view(seq, n), residual=x) if fuse else x + tr("o", self.o(att.view(seq, n))))
+        return att.view(seq, n)
+
+    @torch.no_grad()
+    def forward_shard(self, x_shard: torch.Tensor, lay: SeqLayout) -> torch.Tensor:
+        """Sequence-parallel block: ``x_shard`` holds this rank's token rows of the residual
+        stream (``lay``, the form consecutive blocks pass on); returns the same rows of the
+        block's output. The LayerNorms and the readers' quantization run on the shard, the
+        packed codes are all-gathered for the column-parallel q/k/v and ffn.0, and the
+        row-parallel o and ffn.2 outputs are reduce-scattered into the shard -- per row the
+        arithmetic of the all-reduce path."""
+        cfg, tp = self.cfg, self.tp
+        tr = lambda stage, t: t  # noqa: E731
+        qkv = self.qkv.sp_column(x_shard, lay, tp, norm=(None, cfg.eps))
+        att = self._attend(qkv, lay.rows, tr)
+        x_shard = self.o.sp_row(self.o.quantize_input(att), x_shard, lay, tp)
+        f0 = self.ffn0.sp_column(x_shard, lay, tp, norm=(None, cfg.eps))
+        return self.ffn2.sp_row(self.ffn2.activate_and_quantize(f0, "gelu_tanh"), x_shard, lay, tp)
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """``x [L, dim]`` bf16 (batch 1) -> ``[L, dim]``; with more than one rank the block
+        runs sequence-parallel on this rank's rows and the output rows are all-gathered."""
+        lay = self.seq_layout(x.shape[0])
+        if lay is not None:
+            out = self.forward_shard(x[lay.owned(x.device)], lay)
+            return sp_gather_rows(self.tp, lay, out)
+        cfg = self.cfg
+        seq = x.shape[0]
+        tr = (lambda stage, t: (self.trace(stage, 0, t), t)[1]) if self.trace is not None else (lambda stage, t: t)
+        fuse = self.fuse_residual and self.trace is None  # norms in the readers' K1, residual adds in epilogues
+        if fuse:
+            qkv = self.qkv(x, norm=(None, cfg.eps))
+        else:
+            qkv = tr("qkv", self.qkv(tr("norm1", ops.layer_norm(x, cfg.eps))))
+        att = self._attend(qkv, seq, tr)
+        x = tr("x_mid", self.o(att, residual=x) if fuse else x + tr("o", self.o(att)))
         if fuse:
             f0 = self.ffn0(x, norm=(None, cfg.eps))
         else:

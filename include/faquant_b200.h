@@ -98,13 +98,17 @@ int faq_hif4_quantize(const void* x, int x_dtype, int64_t rows, int64_t k, int64
  * times input_scale, rounded) rotated with signs / perm / rot_block and HiF4-quantized
  * exactly as faq_hif4_quantize. The normalized tensor never goes to memory. Replaces the
  * pair Qwen3RMSNorm (modeling_qwen3 as the reference's models use it) then the input
- * path of FakeQuantLinear.forward (src/faquant/quantization.py:200-221). bf16 only;
- * qdq is required, meta optional (codes: use the unfused pair). FAQ_ERR_UNSUPPORTED
- * unless k % 1024 == 0, k <= 16384 and 32 <= rot_block <= 1024.
+ * path of FakeQuantLinear.forward (src/faquant/quantization.py:200-221). bf16 only.
+ * Outputs as faq_hif4_quantize's (any may be NULL, not both codes and qdq): packed
+ * `codes` [rows, k/2] (16-byte aligned, row stride k/2), `meta` [rows, k/64] and the
+ * dequantized `qdq` [rows, ldq]; codes alone are what a sequence-parallel caller
+ * all-gathers (0.5625 bytes per value instead of 2). FAQ_ERR_UNSUPPORTED unless
+ * k % 1024 == 0, k <= 16384 and 32 <= rot_block <= 1024.
  */
 int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, const void* norm_weight,
                                float eps, const void* input_scale, const int8_t* signs, const int64_t* perm,
-                               int rot_block, int levels, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
+                               int rot_block, int levels, uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq,
+                               void* stream);
 /*
  * The same with the Wan DiT block's affine-free LayerNorm in front (norm1 -> qkv, norm2
  * -> ffn.0; the rbhn_r64 readers): bf16((x - mean) * rsqrt(var + eps)), biased
@@ -115,7 +119,7 @@ int faq_hif4_quantize_rms_norm(const void* x, int64_t rows, int64_t k, int64_t l
  */
 int faq_hif4_quantize_layer_norm(const void* x, int64_t rows, int64_t k, int64_t ldx, float eps,
                                  const void* input_scale, const int8_t* signs, const int64_t* perm, int rot_block,
-                                 int levels, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
+                                 int levels, uint8_t* codes, uint32_t* meta, void* qdq, int64_t ldq, void* stream);
 
 /*
  * faq_hif4_quantize of an activation's output, the activation fused into the load: `act`

@@ -151,18 +151,36 @@ def test_quantize_rms_norm_equals_norm_then_quantize(k: int, block: int) -> None
         fused, fmeta = ops.hif4_quantize_rms_norm(x, w, 1e-6, levels=levels, input_scale=sc, signs=signs,
                                                   permutation=perm, rot_block=block, want_meta=True)
         h = ops.rms_norm(x, w, 1e-6)
-        qdq, _, meta = ops.hif4_quantize(h, levels=levels, input_scale=sc, signs=signs, permutation=perm,
-                                         rot_block=block, want_codes=True)
+        qdq, codes, meta = ops.hif4_quantize(h, levels=levels, input_scale=sc, signs=signs, permutation=perm,
+                                             rot_block=block, want_codes=True)
         assert torch.equal(fused, qdq), (rows, levels)
         assert torch.equal(fmeta, meta), (rows, levels)
+        # packed codes as well (with the QDQ, and alone: what a sequence-parallel rank
+        # all-gathers); they expand back to exactly the QDQ values
+        for want_qdq in (True, False):
+            fc = torch.full_like(codes, 0xA5)
+            fq, fm = ops.hif4_quantize_rms_norm(x, w, 1e-6, levels=levels, input_scale=sc, signs=signs,
+                                                permutation=perm, rot_block=block, want_meta=True,
+                                                want_qdq=want_qdq, codes_out=fc)
+            assert torch.equal(fc, codes) and torch.equal(fm, meta), (rows, levels, want_qdq)
+            assert (fq is None) != want_qdq and (fq is None or torch.equal(fq, qdq))
+        assert torch.equal(ops.hif4_dequantize(codes, meta, k), qdq), (rows, levels)
         # the affine-free LayerNorm (norm_weight None), on values with an offset
         xo = x + 0.75
         fused, fmeta = ops.hif4_quantize_rms_norm(xo, None, 1e-6, levels=levels, input_scale=sc, signs=signs,
                                                   permutation=perm, rot_block=block, want_meta=True)
-        qdq, _, meta = ops.hif4_quantize(ops.layer_norm(xo, 1e-6), levels=levels, input_scale=sc, signs=signs,
-                                         permutation=perm, rot_block=block, want_codes=True)
+        qdq, codes, meta = ops.hif4_quantize(ops.layer_norm(xo, 1e-6), levels=levels, input_scale=sc, signs=signs,
+                                             permutation=perm, rot_block=block, want_codes=True)
         assert torch.equal(fused, qdq), ("layer", rows, levels)
         assert torch.equal(fmeta, meta), ("layer", rows, levels)
+        fc = torch.empty_like(codes)
+        _, fm = ops.hif4_quantize_rms_norm(xo, None, 1e-6, levels=levels, input_scale=sc, signs=signs,
+                                           permutation=perm, rot_block=block, want_meta=True, want_qdq=False,
+                                           codes_out=fc)
+        assert torch.equal(fc, codes) and torch.equal(fm, meta), ("layer codes", rows, levels)
+        half = torch.empty(rows, 2 * k, dtype=torch.bfloat16, device=DEV)  # into a strided buffer
+        ops.hif4_dequantize(codes, meta, k, out=half[:, k:])
+        assert torch.equal(half[:, k:], qdq), ("layer", rows, levels)
     empty, _ = ops.hif4_quantize_rms_norm(torch.zeros(0, k, dtype=torch.bfloat16, device=DEV), w, 1e-6,
                                           signs=signs, permutation=perm, rot_block=block)
     assert empty.shape == (0, k)

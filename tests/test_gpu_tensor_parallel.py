@@ -302,6 +302,27 @@ def _tp_rank(rank: int, world: int, port: int, results) -> None:
         chunked = lin(xr)
         lin.overlap_min_rows = 1 << 30
         mine["chunked_equal"] = bool(torch.equal(chunked, lin(xr)))
+        # sequence parallel (norm + K1 on the row shard, packed codes all-gathered, outputs
+        # reduce-scattered) against the all-reduce path: with two ranks every sum is of two
+        # values, so the same bits. Width 1024 takes the fused-norm packed path; layer 1 of
+        # the Qwen3 model is a bf16 layer (its normalized rows are gathered as bf16)
+        from faquant_b200.tensor_parallel import Qwen3TPConfig, WanBlockConfig
+
+        qc = Qwen3TPConfig(hidden=1024, layers=2, heads=8, kv_heads=2, head_dim=128, ffn=2048, vocab=1000,
+                           bf16_layers=(1,), column_block=1024)
+        m = Qwen3TPPrefill(qc, tp, dev)
+        ids = default_input_ids(2, 256, qc.vocab, dev, seed=5)
+        assert m.seq_layout(2, 256) is not None
+        sp = m(ids)
+        m.sequence_parallel = False
+        mine["qwen_sp_equal"] = bool(torch.equal(sp, m(ids)))
+        wc = WanBlockConfig(dim=1024, heads=8, head_dim=128, ffn=2048, grid=(2, 6, 16))
+        wb = WanBlockTP(wc, tp, dev)
+        xw = torch.randn(wc.seq, wc.dim, generator=torch.Generator().manual_seed(19)).to(torch.bfloat16).to(dev)
+        assert wb.seq_layout(wc.seq) is not None
+        sp = wb(xw)
+        wb.sequence_parallel = False
+        mine["wan_sp_equal"] = bool(torch.equal(sp, wb(xw)))
         results[rank] = mine  # one assignment: a managed dict hands out copies of its values
         dist.barrier()
     finally:
@@ -314,7 +335,8 @@ def test_tp2_over_nccl_matches_tp1() -> None:
     attention of each rank are bit-identical slices of the TP 1 results (same quantized
     inputs, same kernels); the row-parallel o_proj after the all-reduce differs only by
     the order of its partial sums. (Later stages re-quantize those last-bit differences,
-    so they are checked against the oracle stage by stage instead.)"""
+    so they are checked against the oracle stage by stage instead.) The sequence-parallel
+    forwards of both models equal their all-reduce forwards bit for bit at TP 2."""
     import torch.multiprocessing as mp
 
     from faquant_b200.tensor_parallel import Qwen3TPPrefill, TPGroup, WanBlockTP, default_input_ids
@@ -329,6 +351,8 @@ def test_tp2_over_nccl_matches_tp1() -> None:
     x = torch.randn(block.cfg.seq, block.cfg.dim, generator=torch.Generator().manual_seed(9)).to(torch.bfloat16)
     block(x.to(DEV))
     assert results[0]["chunked_equal"] and results[1]["chunked_equal"]
+    for key in ("qwen_sp_equal", "wan_sp_equal"):
+        assert results[0][key] and results[1][key], key
     for tag, tr, hq, hkv in (("qwen", tq, 8, 2), ("wan", tw, 4, 4)):
         d = 128
         qkv1 = tr[("qkv", 0)].numpy()

@@ -12,8 +12,9 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from faquant_b200.hisq_rotation import derive_hisq_rotation, restrict_hisq_rotation
-from faquant_b200.tensor_parallel import (HIF4_GROUP, Qwen3TPConfig, TPGroup, WanBlockConfig, column_rotation,
-                                          qwen3_shard_slices, random_weight, row_rotation)
+from faquant_b200.tensor_parallel import (HIF4_GROUP, Qwen3TPConfig, SeqLayout, TPGroup, WanBlockConfig,
+                                          column_rotation, qwen3_shard_slices, random_weight, row_rotation,
+                                          seq_layout, sp_gather_rows, sp_reduce_scatter_rows)
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -61,6 +62,50 @@ def test_column_rotation_is_shared_per_norm() -> None:
     assert torch.equal(a.signs, b.signs) and torch.equal(a.permutation, b.permutation)
     assert torch.equal(a.signs, ref.signs) and torch.equal(a.permutation, ref.permutation)
     assert not torch.equal(a.permutation, c.permutation)
+
+
+@pytest.mark.parametrize("rows,world", [(32768, 1), (32768, 2), (32768, 8), (75600, 2), (75600, 4), (75600, 8),
+                                        (48, 2), (96, 3)])
+def test_sequence_parallel_layout_partitions_the_rows(rows: int, world: int) -> None:
+    """Every row belongs to exactly one rank's shard; ``locate`` inverts ``owned``; chunks are
+    whole and as many as allowed (at most 4) for the BASELINE token counts."""
+    lays = [seq_layout(rows, TPGroup(r, world)) for r in range(world)]
+    assert all(lay is not None for lay in lays)
+    owned = torch.cat([lay.owned() for lay in lays])
+    assert torch.equal(owned.sort().values, torch.arange(rows))
+    for r, lay in enumerate(lays):
+        assert lay.shard_rows * world == rows and lay.chunks * lay.chunk_rows == rows
+        for i, row in enumerate(lay.owned().tolist()):
+            assert lay.locate(row) == (r, i)
+    assert lays[0].chunks == (3 if (rows, world) == (75600, 8) else 4)
+    assert seq_layout(75601, TPGroup(0, 2)) is None
+
+
+def _sp_rank_main(rank: int, world: int, port: int, results) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tp = TPGroup(rank, world)
+        lay = SeqLayout(48, world, rank, 3)
+        g = torch.Generator().manual_seed(7)
+        full = torch.randn(48, 5, generator=g)
+        parts = [torch.randn(48, 5, generator=g) for _ in range(world)]  # every rank's partial output
+        shard = full[lay.owned()]
+        # the all-gather of the shards rebuilds the rows in order
+        ok_ag = torch.equal(sp_gather_rows(tp, lay, shard), full)
+        # the reduce-scatter of the partials gives this rank's rows of their sum
+        red = sp_reduce_scatter_rows(tp, lay, parts[rank])
+        ok_rs = torch.allclose(red, sum(parts)[lay.owned()], atol=1e-6)
+        results[rank] = bool(ok_ag and ok_rs)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_parallel_collectives_over_gloo() -> None:
+    world = 2
+    results = mp.Manager().dict()
+    mp.spawn(_sp_rank_main, args=(world, _free_port(), results), nprocs=world, join=True)
+    assert dict(results) == {0: True, 1: True}
 
 
 def _free_port() -> int:
