@@ -1092,8 +1092,9 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         e2e = _e2e_timed((lambda xs: block.forward_shard(xs, lay)) if lay is not None else block,
                          x.cpu().pin_memory(), args.tp_steps, device, barrier, dist)
         e2e.update({"value": wf["total"] / (e2e["ms_per_step"] * 1e-3) / 1e12, "unit": "TFLOPS",
-                    "path": "pinned host hidden states -> WanBlockTP (every rank its replicated input) -> "
-                            "pinned host output"})
+                    "path": ("pinned host token rows of this rank -> WanBlockTP.forward_shard (sequence "
+                             "parallel) -> pinned host output rows of this rank") if lay is not None else
+                            "pinned host hidden states -> WanBlockTP -> pinned host output"})
         out["wan22_block"]["e2e"] = e2e
     del block, x
     torch.cuda.empty_cache()
