@@ -17,6 +17,7 @@
 // The two accumulators (2 x 256 columns) let the epilogue of tile i overlap the
 // main loop of tile i+1. Every wait is bounded (common.cuh, mbar_wait).
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -414,6 +415,14 @@ using namespace faq;
 
 namespace faq {
 namespace gemm {
+// The SM count the persistent GEMMs (K3, K3p) size their grids for; 0: every SM. A
+// tensor-parallel caller lowers it while collectives run beside its GEMMs, so that the
+// collective kernels find free SMs instead of waiting for a GEMM that holds all of them.
+static std::atomic<int> g_sm_target{0};
+static int grid_sms() {
+  const int all = num_sms(), t = g_sm_target.load(std::memory_order_relaxed);
+  return t > 0 && t < all ? std::max(2, t) : all;
+}
 // FAQ_GEMM_ONE_SM=1 in the environment keeps every GEMM on the one-CTA kernel
 static bool one_sm_forced() {
   static const bool forced = [] {
@@ -478,7 +487,7 @@ extern "C" int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void*
     p.tiles_n = static_cast<int>((n + PB_N - 1) / PB_N);
     p.group_m = std::max(1, std::min(p.tiles_m, 8));  // 8 pair rows = 2048 rows of A per group
     const int tiles = p.tiles_m * p.tiles_n;
-    const int grid = 2 * std::max(1, std::min(tiles, num_sms() / 2));
+    const int grid = 2 * std::max(1, std::min(tiles, grid_sms() / 2));
     FAQ_CUDA(cudaFuncSetAttribute(gemm_bf16_tn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(P_SMEM_BYTES)));
     gemm_bf16_tn_pair_kernel<<<grid, THREADS, P_SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb2, p);
@@ -490,11 +499,17 @@ extern "C" int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void*
   // the panels a wave reads (G A panels + 148 / G B panels, B panels twice as large)
   p.group_m = std::max(1, std::min(p.tiles_m, 16));
   const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = std::min(tiles, num_sms());
+  const int grid = std::min(tiles, grid_sms());
   FAQ_CUDA(cudaFuncSetAttribute(gemm_bf16_tn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(SMEM_BYTES)));
   gemm_bf16_tn_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   return launch_status("gemm_bf16_tn_kernel");
+}
+
+extern "C" int faq_set_gemm_sm_target(int sms) {
+  FAQ_CHECK_ARG(sms >= 0, "sms must be >= 0 (0: every SM)");
+  faq::gemm::g_sm_target.store(sms, std::memory_order_relaxed);
+  return FAQ_OK;
 }
 
 extern "C" int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,

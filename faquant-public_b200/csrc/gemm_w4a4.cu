@@ -444,7 +444,7 @@ static int launch(Maps& maps, bool a_packed, Params& p, void* stream) {
   g.kblocks = g.k / BK;
   g.group_m = std::max(1, std::min(g.tiles_m, 8));
   const int tiles = g.tiles_m * g.tiles_n;
-  const int grid = 2 * std::max(1, std::min(tiles, num_sms() / 2));
+  const int grid = 2 * std::max(1, std::min(tiles, faq::gemm::grid_sms() / 2));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (a_packed) {
     constexpr size_t smem = Rings<true>::SMEM_BYTES;

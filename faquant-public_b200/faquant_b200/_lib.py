@@ -35,6 +35,7 @@ SIGNATURES: dict[str, list] = {
                                      _int, _int, _c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p],
     "faq_hif4_quantize_act": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _int, _int, _c_void_p,
                               _c_void_p, _c_void_p, _i64, _c_void_p],
+    "faq_set_gemm_sm_target": [_int],
     "faq_hif4_dequantize": [_c_void_p, _c_void_p, _i64, _i64, _c_void_p, _int, _i64, _c_void_p],
     "faq_hif4_pack_weight": [_c_void_p, _int, _i64, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _int,
                              _c_void_p, _c_void_p, _c_void_p, _c_void_p],

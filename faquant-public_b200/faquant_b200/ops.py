@@ -275,6 +275,12 @@ def hif4_pack_weight(
     return codes, meta, int(counter.item())
 
 
+def set_gemm_sm_target(sms: int) -> None:
+    """Size the persistent GEMMs' grids for ``sms`` SMs from the next launch on (0: every
+    SM; ``faq_set_gemm_sm_target``): leaves SMs free for collectives that run beside them."""
+    _lib.call("faq_set_gemm_sm_target", int(sms))
+
+
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, bias: torch.Tensor | None = None,
               out: torch.Tensor | None = None, residual: torch.Tensor | None = None) -> torch.Tensor:
     """``a [m, k] @ b [n, k]^T (+ bias)`` in bf16 with fp32 accumulation (tcgen05); with

@@ -23,8 +23,10 @@ residual stream between projections is sharded by rows, so the norms and the rea
 quantization run on 1/N of the rows instead of on every rank in full; the column-parallel
 inputs are all-gathered as packed HiF4 codes (0.5625 bytes per value instead of bf16's
 2) and the row-parallel outputs are reduce-scattered instead of all-reduced, one chunk of
-rows at a time so each collective overlaps the next chunk's GEMM. Per row the arithmetic
-is the all-reduce path's; at two ranks the outputs are the same bits.
+rows at a time (``sp_chunks``; one by default: the persistent GEMMs and the attention
+hold every SM, so a collective cannot run beside them and more chunks only add calls).
+Per row the arithmetic is the all-reduce path's; at two ranks the outputs are the same
+bits.
 """
 
 from __future__ import annotations
@@ -51,6 +53,27 @@ class TPGroup:
     # when a list: every collective appends (start event, end event, bytes, kind), recorded
     # on the stream it runs on -- the measurement of the collectives' share of a step
     timer: list | None = None
+    # SMs the persistent GEMMs leave free during a sequence-parallel forward, for the NCCL
+    # kernels of the chunked collectives that run beside them (0: GEMMs on every SM)
+    gemm_sm_reserve: int = 0
+
+    def gemm_sms(self, device: torch.device):
+        """Context: the GEMMs inside run on all but ``gemm_sm_reserve`` SMs."""
+        import contextlib
+
+        if self.gemm_sm_reserve <= 0:
+            return contextlib.nullcontext()
+
+        @contextlib.contextmanager
+        def ctx():
+            total = torch.cuda.get_device_properties(device).multi_processor_count
+            ops.set_gemm_sm_target(max(2, total - self.gemm_sm_reserve))
+            try:
+                yield
+            finally:
+                ops.set_gemm_sm_target(0)
+
+        return ctx()
 
     def shard(self, n: int, unit: int) -> tuple[int, int]:
         """(start, size) of this rank's even share of ``n`` items in whole ``unit``s."""
@@ -523,8 +546,10 @@ class Qwen3TPPrefill(nn.Module):
         # needs the projections' own outputs)
         self.fuse_residual = True
         # with more than one rank: the residual stream sharded by rows, reduce-scatter and
-        # all-gather of packed codes instead of all-reduces (off while a trace hook is set)
+        # all-gather of packed codes instead of all-reduces (off while a trace hook is set),
+        # in up to sp_chunks row chunks (one: the fewest collectives, fastest measured at TP 8)
         self.sequence_parallel = True
+        self.sp_chunks = 1
         d = cfg.head_dim
         sl = qwen3_shard_slices(cfg, tp)
         hq, hkv = cfg.heads // tp.world, cfg.kv_heads // tp.world
@@ -607,7 +632,7 @@ class Qwen3TPPrefill(nn.Module):
         """The sequence-parallel layout the forward uses (None: the replicated path)."""
         if not self.sequence_parallel or self.tp.world == 1 or self.trace is not None:
             return None
-        return seq_layout(batch * seq, self.tp)
+        return seq_layout(batch * seq, self.tp, self.sp_chunks)
 
     def _forward_sp(self, input_ids: torch.Tensor, lay: SeqLayout) -> torch.Tensor:
         """Sequence-parallel forward: the residual stream is sharded by rows (``lay``), the
@@ -616,6 +641,10 @@ class Qwen3TPPrefill(nn.Module):
         are reduce-scattered into the shard (:meth:`TPHiF4Linear.sp_row`). The same
         per-row arithmetic as the all-reduce path: at two ranks the logits are the same
         bits."""
+        with self.tp.gemm_sms(self.device):
+            return self._forward_sp_layers(input_ids, lay)
+
+    def _forward_sp_layers(self, input_ids: torch.Tensor, lay: SeqLayout) -> torch.Tensor:
         cfg, tp = self.cfg, self.tp
         batch, seq = input_ids.shape
         cos, sin = rope_tables(seq, cfg.head_dim, cfg.rope_theta, self.device)
@@ -756,6 +785,7 @@ class WanBlockTP(nn.Module):
         self.trace = None  # trace(stage, 0, tensor) at each stage boundary, as in Qwen3TPPrefill
         self.fuse_residual = True
         self.sequence_parallel = True  # as in Qwen3TPPrefill (off while a trace hook is set)
+        self.sp_chunks = 1
         if cfg.heads % tp.world:
             raise ValueError("heads must divide by the TP size")
         d = cfg.head_dim
@@ -795,7 +825,7 @@ class WanBlockTP(nn.Module):
         """The sequence-parallel layout of ``seq`` tokens (None: the replicated path)."""
         if not self.sequence_parallel or self.tp.world == 1 or self.trace is not None:
             return None
-        return seq_layout(seq, self.tp)
+        return seq_layout(seq, self.tp, self.sp_chunks)
 
     def _attend(self, qkv: torch.Tensor, seq: int, tr) -> torch.Tensor:
         """The rank's heads of the self-attention from the qkv output ``[L, 3 hl d]``: Wan's
@@ -823,6 +853,10 @@ class WanBlockTP(nn.Module):
         packed codes are all-gathered for the column-parallel q/k/v and ffn.0, and the
         row-parallel o and ffn.2 outputs are reduce-scattered into the shard -- per row the
         arithmetic of the all-reduce path."""
+        with self.tp.gemm_sms(x_shard.device):
+            return self._forward_shard(x_shard, lay)
+
+    def _forward_shard(self, x_shard: torch.Tensor, lay: SeqLayout) -> torch.Tensor:
         cfg, tp = self.cfg, self.tp
         tr = lambda stage, t: t  # noqa: E731
         qkv = self.qkv.sp_column(x_shard, lay, tp, norm=(None, cfg.eps))

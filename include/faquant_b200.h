@@ -180,6 +180,16 @@ int faq_gemm_bf16_tn(const void* a, int64_t lda, const void* b, int64_t ldb, int
 int faq_gemm_bf16_tn_residual(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m,
                               int64_t n, int64_t k, const void* bias, const void* residual, int64_t ldr,
                               void* y, int64_t ldy, void* stream);
+/*
+ * The number of SMs the persistent GEMMs (faq_gemm_bf16_tn*, faq_w4a4_gemm*) size their
+ * grids for, from the next launch on (0, the default: every SM of the device; values
+ * above the SM count mean every SM). Process-wide and read on the host at launch, not
+ * stream-ordered. For callers that run collectives (NCCL) beside the GEMMs on another
+ * stream: a GEMM grid over every SM leaves no SM for the collective's kernels until the
+ * GEMM drains. The result bits do not depend on it. The counterpart of cuBLAS's
+ * cublasSetSmCountTarget; no counterpart in the reference.
+ */
+int faq_set_gemm_sm_target(int sms);
 
 /*
  * K3p -- the W4A4 GEMM on packed HiF4 operands: y [m, n] = deq(a) . deq(b)^T (+ bias [n])

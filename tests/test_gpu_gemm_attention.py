@@ -95,6 +95,30 @@ def test_gemm_cta_pairs_equal_one_cta(tmp_path) -> None:
         assert torch.equal(a, b), (m, n, k)
 
 
+def test_gemm_sm_target_keeps_the_bits() -> None:
+    """faq_set_gemm_sm_target (fewer SMs for the persistent grids, so collectives find free
+    SMs) changes only which CTA computes a tile: the bf16 GEMM (pairs and one-CTA shapes)
+    and the packed W4A4 GEMM give the same bits at 2, 17, 100 SMs and at every SM."""
+    ops = _ops()
+    cases = [(2048, 4096, 1024), (300, 520, 256), (8192, 1024, 512)]
+    try:
+        for i, (m, n, k) in enumerate(cases):
+            a = _hif4_operand(m, k, 40 + i).to(DEV)
+            b = _hif4_operand(n, k, 50 + i, 0.02).to(DEV)
+            ac, am = ops.hif4_quantize(a, want_codes=True)[1:]
+            bc, bm, _ = ops.hif4_pack_weight(b)
+            ops.set_gemm_sm_target(0)
+            ref, ref_p = ops.gemm_bf16(a, b), ops.w4a4_gemm((ac, am), bc, bm)
+            for sms in (2, 17, 100, 1000):
+                ops.set_gemm_sm_target(sms)
+                assert torch.equal(ops.gemm_bf16(a, b), ref), (m, n, k, sms)
+                assert torch.equal(ops.w4a4_gemm((ac, am), bc, bm), ref_p), (m, n, k, sms)
+    finally:
+        ops.set_gemm_sm_target(0)
+    with pytest.raises(Exception):
+        ops.set_gemm_sm_target(-1)
+
+
 @pytest.mark.parametrize("m,n,k", [(300, 520, 200), (1000, 1000, 1024), (33, 48, 64), (2048, 4096, 512)])
 def test_gemm_residual_epilogue_is_the_separate_bf16_add(m: int, n: int, k: int) -> None:
     """y = bf16(bf16(a b^T + bias) + residual): the same bits as the GEMM followed by the

@@ -318,8 +318,9 @@ def _tp_rank(rank: int, world: int, port: int, results) -> None:
         mine["qwen_sp_equal"] = bool(torch.equal(sp, m(ids)))
         wc = WanBlockConfig(dim=1024, heads=8, head_dim=128, ffn=2048, grid=(2, 6, 16))
         wb = WanBlockTP(wc, tp, dev)
+        wb.sp_chunks = 4  # the chunked collectives (the Qwen3 model runs the default single chunk)
         xw = torch.randn(wc.seq, wc.dim, generator=torch.Generator().manual_seed(19)).to(torch.bfloat16).to(dev)
-        assert wb.seq_layout(wc.seq) is not None
+        assert wb.seq_layout(wc.seq).chunks == 4 and m.seq_layout(2, 256).chunks == 1
         sp = wb(xw)
         wb.sequence_parallel = False
         mine["wan_sp_equal"] = bool(torch.equal(sp, wb(xw)))
