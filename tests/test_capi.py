@@ -45,6 +45,13 @@ def test_host_side_argument_validation() -> None:
     assert lib.faq_hif4_quantize(fake, 0, 4, 64, 64, None, None, None, 0, 123, None, None, None, 64, None) == 1
     assert lib.faq_gemm_bf16_tn(fake, 12, fake, 16, 4, 4, 12, None, fake, 4, None) == 1
     assert "multiples of 8" in _lib.last_error()
+    # the GEMM SM target is host state: a negative count is refused, 0 (every SM) accepted
+    assert lib.faq_set_gemm_sm_target(-1) == 1 and "sms" in _lib.last_error()
+    assert lib.faq_set_gemm_sm_target(0) == 0
+    # the fused-norm quantizer needs at least one of codes and qdq
+    assert lib.faq_hif4_quantize_rms_norm(fake, 4, 1024, 1024, fake, ctypes.c_float(1e-6), None, fake, None, 1024,
+                                          123, None, None, None, 1024, None) == 1
+    assert "both null" in _lib.last_error()
     with pytest.raises(ValueError):
         _lib.check(1, "demo")
 
