@@ -600,6 +600,50 @@ def cpu_baseline(tokens: int = 1024, steps: int = 2) -> dict:
     }
 
 
+def cpu_attention_baseline(seq: int = ATT["seq"], heads: int = 1) -> dict:
+    """The reference's own attention simulator (``simulated_flash_attention_forward``,
+    src/faquant/simulated_flash_attention.py:457-909, imported from baseline/_ref) with config
+    3's settings -- causal, HiF4 Q/K/V and P in groups of 64, P-Reordering
+    (``quantized_same``), query chunks of 256 and key chunks of 128 -- on the host cores: a
+    bounded sample of ``heads`` query heads (with their KV head) at the full sequence length;
+    its work per (query, key) pair is that of the full configuration, 32 heads."""
+    import torch
+
+    if _import_reference() is None:
+        return {"unavailable": "the reference is not importable (no offline install under baseline/_ref)"}
+    from types import SimpleNamespace
+
+    from faquant.simulated_flash_attention import new_simulated_attention_stats, simulated_flash_attention_forward
+
+    threads = cpu_threads()
+    d = ATT["d"]
+
+    def module():
+        return SimpleNamespace(
+            is_causal=True, training=False, faquant_attention_query_chunk_size=256,
+            faquant_attention_key_chunk_size=128, faquant_qk_matmul_quant=True, faquant_pv_matmul_quant=True,
+            faquant_pv_normalizer_mode="quantized_same",
+            faquant_matmul_quant_kwargs={"quant_format": "hif4", "bits": 4, "group_size": 64, "symmetric": True,
+                                         "clip_ratio": 1.0},
+            faquant_simulated_attention_stats=new_simulated_attention_stats())
+
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, heads if i == 0 else 1, seq, d, generator=g).to(torch.bfloat16) for i in range(3))
+    with torch.no_grad():
+        simulated_flash_attention_forward(module(), q[:, :, :1024], k[:, :, :1024], v[:, :, :1024], None,
+                                          scaling=d ** -0.5)  # warm-up
+        t0 = time.perf_counter()
+        simulated_flash_attention_forward(module(), q, k, v, None, scaling=d ** -0.5)
+        dt = time.perf_counter() - t0
+    flops = 4.0 * d * heads * seq * (seq + 1) / 2.0
+    return {"value": flops / dt / 1e12, "unit": "TFLOPS", "cores": threads, "kind": "reference",
+            "sample": f"{heads} of the {ATT['hq']} query heads (with its KV head) at the full S={seq}, causal: the "
+                      f"reference's simulated_flash_attention_forward (HiF4 Q/K/V and P, P-Reordering, query chunk "
+                      f"256, key chunk 128), CPU torch on {threads} threads, one call after a 1024-token warm-up; "
+                      f"the full configuration is {ATT['hq'] // heads}x this work",
+            "seconds": dt, "seconds_full_config_estimate": dt * ATT["hq"] / heads}
+
+
 def reference_arm(args) -> None:
     rank, world, _ = dist_env()
     if world > 1 and rank != 0:
@@ -908,6 +952,11 @@ def main_arm(args) -> None:
         }
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
+            if att is not None and world == 1:
+                try:
+                    att["cpu_baseline"] = cpu_attention_baseline()
+                except Exception as exc:  # noqa: BLE001 - a reported baseline never costs the bench line
+                    att["cpu_baseline"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
