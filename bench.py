@@ -1009,7 +1009,7 @@ def run_decode(args, device, pk: dict, barrier, dist) -> dict:
             "gpu_launches_per_step": 3, "steps": 20}
 
 
-def _allreduce_share(tp, step, step_ms: float, world: int, barrier) -> dict | None:
+def _collective_share(tp, step, step_ms: float, world: int, barrier) -> dict | None:
     """One more step with the collectives (all-reduces; with sequence parallelism the
     reduce-scatters and all-gathers) timed by CUDA events on the streams they run on: their
     summed device time and bytes against the timed step (an untimed extra step, so the
@@ -1126,7 +1126,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
         run_block = lambda: block(x)  # noqa: E731
         w_io = "all 75600 token rows in and out"
     w_ms = _timed(run_block, args.tp_steps, 1, barrier, dist, device)
-    w_comm = _allreduce_share(tp, run_block, w_ms, world, barrier)
+    w_comm = _collective_share(tp, run_block, w_ms, world, barrier)
     wf = wcfg.flops()
     out["wan22_block"] = {
         "workload": "Wan2.2-A14B DiT block, S=75600 (21x45x80), 40 heads, self-attention + FFN (BASELINE config 4)",
@@ -1151,7 +1151,7 @@ def run_tp_workloads(args, rank: int, world: int, device, pk: dict, barrier, dis
     model = Qwen3TPPrefill(qcfg, tp, device)
     ids = default_input_ids(4, 8192, qcfg.vocab, device)
     q_ms = _timed(lambda: model(ids), args.tp_steps, 1, barrier, dist, device)
-    q_comm = _allreduce_share(tp, lambda: model(ids), q_ms, world, barrier)
+    q_comm = _collective_share(tp, lambda: model(ids), q_ms, world, barrier)
     qf = qcfg.flops(4, 8192)
     q_e2e = None
     if not args.no_e2e:
