@@ -108,6 +108,41 @@ def test_sequence_parallel_collectives_over_gloo() -> None:
     assert dict(results) == {0: True, 1: True}
 
 
+def _sp_packed_rank_main(rank: int, world: int, port: int, results) -> None:
+    import numpy as np
+
+    from oracle import hif4 as oh
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        tp = TPGroup(rank, world)
+        rows, k = 96, 256
+        lay = seq_layout(rows, tp, max_chunks=3)
+        g = torch.Generator().manual_seed(23)
+        x = (torch.randn(rows, k, generator=g) * 3).to(torch.bfloat16).float().numpy()
+        x[5, :64] = 0.0  # a zero block
+        mine = x[lay.owned().numpy()]
+        # this rank packs its own rows only (what the fused-norm K1 writes on the shard)
+        codes, meta = oh.hif4_encode(mine)
+        full_codes = sp_gather_rows(tp, lay, torch.from_numpy(codes))
+        full_meta = sp_gather_rows(tp, lay, torch.from_numpy(meta.view(np.int32)))
+        got = oh.hif4_decode(full_codes.numpy(), full_meta.numpy().view(np.uint32), k)
+        results[rank] = bool(np.array_equal(got, oh.fake_quantize(x)) and lay.chunks == 3)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sequence_parallel_packed_code_gather_matches_the_oracle_over_gloo() -> None:
+    """The sequence-parallel all-gather of packed HiF4 codes and meta words (uint8 and
+    int32, chunked row layout): every rank packs only its own rows, and the gathered bytes
+    decode to the oracle's QDQ of all rows in row order."""
+    world = 2
+    results = mp.Manager().dict()
+    mp.spawn(_sp_packed_rank_main, args=(world, _free_port(), results), nprocs=world, join=True)
+    assert dict(results) == {0: True, 1: True}
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
