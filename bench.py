@@ -819,7 +819,9 @@ def main_arm(args) -> None:
 
     # ---------------- the reference's own GPU kernel beside K5 (config 4 attention), rank 0
     gpu_ref = None
-    if A is not None and rank == 0 and not args.no_gpu_reference:
+    # one GPU's comparison; at N > 1 the other ranks would wait at the next barrier while
+    # rank 0 compiles and runs the reference's Triton kernel
+    if A is not None and world == 1 and not args.no_gpu_reference:
         gpu_ref = gpu_reference_attention(2)
 
     # ---------------- decode step (K6): one new token per sequence against a 32K-key cache
