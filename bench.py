@@ -343,7 +343,9 @@ def run_decode_linear(layers, device, pk):
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.no_grad(), torch.cuda.graph(g):
+        # thread_local: under torchrun the process group's watchdog thread queries its
+        # events while this thread captures; only this thread's calls must be capturable
+        with torch.no_grad(), torch.cuda.graph(g, capture_error_mode="thread_local"):
             for _ in range(reps):
                 for m, x in zip(mods, xs):
                     m(x)
