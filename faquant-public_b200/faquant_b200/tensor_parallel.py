@@ -196,24 +196,13 @@ def seq_layout(rows: int, tp: TPGroup, max_chunks: int = 4) -> SeqLayout | None:
     return None
 
 
-def _stream_ctx(stream):
-    import contextlib
-
-    return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
-
-
-def sp_gather_rows(tp: TPGroup, lay: SeqLayout, shard: torch.Tensor, out: torch.Tensor | None = None,
-                   comm=None, on_chunk=None) -> torch.Tensor:
+def sp_gather_rows(tp: TPGroup, lay: SeqLayout, shard: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """All-gather of a sequence-parallel shard back to ``[rows, ...]`` in row order, one
-    collective per chunk (on ``comm`` when given). ``on_chunk(c)``, called after chunk
-    ``c``'s collective was issued, lets the caller consume it while later chunks move."""
+    collective per chunk."""
     if out is None:
         out = torch.empty((lay.rows, *shard.shape[1:]), dtype=shard.dtype, device=shard.device)
     for c in range(lay.chunks):
-        with _stream_ctx(comm):
-            tp.all_gather_into(out[lay.chunk(c)], shard[lay.piece_of_shard(c)])
-        if on_chunk is not None:
-            on_chunk(c)
+        tp.all_gather_into(out[lay.chunk(c)], shard[lay.piece_of_shard(c)])
     return out
 
 
