@@ -135,7 +135,7 @@ class TPGroup:
         return out
 
     def comm_stream(self, device: torch.device) -> torch.cuda.Stream:
-        """The side stream the chunked all-reduces run on (one per rank and device)."""
+        """The side stream the chunked collectives run on (one per rank and device)."""
         key = ("stream", device.index)
         cache = self.__dict__.setdefault("_streams", {})
         if key not in cache:
